@@ -1,0 +1,379 @@
+"""Benchmark of the int8 GEMM path (BASELINE.json metric: Int8Gemm TOPS at 8192^3 s8 x s8 -> s32).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3|c2|c4|c5|dq] [--impl ours|reference]
+
+One step is one Int8Gemm.EncodeInt32 + Submit of the workload (config 3 by default: A int8 [8192 x 8192] x B int8
+[8192 x 8192], zero points absent, int32 C) with inputs resident in HBM; L2 is flushed (a 512 MB write) before every
+step and the step itself is timed with CUDA events on the device stream. With N > 1 (torchrun, one process per GPU,
+NCCL only for the barrier and the max-over-ranks of the times) the product is N-sharded: rank g computes the columns
+[g N/G, (g+1) N/G) from the full A and its slab of B, with no collective in the data path ("strong" scaling: the
+total work is fixed). `e2e` runs the same product through the C ABI from pinned host buffers (uploads of A and the B
+slab, the product, readback of C), timed on the device. `--impl reference` times the CPU restatement of the
+reference's int8 product (oracle/, all host threads) on a bounded row sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "onegpu-csharp_b200"))
+
+METRIC = "Int8Gemm TOPS at 8192³ s8×s8→s32, % int8 tensor peak, 1/2/4/8 B200"
+
+WORKLOADS = {
+    # name: (M, N, K, batch, a_signed, za, zb, out, description)
+    "c3": dict(m=8192, n=8192, k=8192, batch=1, a_signed=True, zp=False, out="i32",
+               desc="square s8 x s8 -> s32, 8192^3, zero points absent"),
+    "c2": dict(m=4096, n=4096, k=4096, batch=1, a_signed=False, zp=True, out="f32",
+               desc="u8 (DQL output, scalar zp) x s8 (per-column zp) -> f32 dequant, 4096^3"),
+    "c4": dict(m=2048, n=12288, k=4096, batch=8, a_signed=False, zp=True, out="i32",
+               desc="batched QKV u8 (zp) x shared s8 (per-column zp) -> s32, 8 x 2048 x 12288 x 4096"),
+    "c5": dict(m=16, n=28672, k=8192, batch=1, a_signed=False, zp=True, out="i32",
+               desc="decode u8 (zp 128) x s8 (per-column zp) -> s32, 16 x 28672 x 8192"),
+}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"bf16_tflops": p.get("bf16_tflops"), "bf16_tflops_sustained": p.get("bf16_tflops_sustained"),
+                "hbm_gbs": p.get("hbm_gbs"), "source": "measured"}
+    return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def profile_traffic(workload: str):
+    """Per-launch DRAM bytes of the top kernel from the committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", f"int8_gemm_tc_{workload}.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
+
+
+def cpu_gemm_tops(n: int, k: int, threads: int, target_s: float, max_rows: int, seed: int = 0):
+    """Times the oracle's threaded restatement of the reference's int8 product (Int8Tests.Reference) on a sample of
+    rows of A against the whole B, sized to about `target_s` seconds; returns (TOPS, seconds, rows)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import og_oracle as oracle
+
+    b = oracle.bytes_(k * n, seed + 31)
+    rows = 4
+    while True:
+        a = oracle.bytes_(rows * k, seed + 30)
+        t0 = time.perf_counter()
+        oracle.int8_gemm(a, True, b, True, m=rows, n=n, k=k, threads=threads)
+        dt = time.perf_counter() - t0
+        if dt >= 0.5 * target_s or rows >= max_rows:
+            return 2.0 * rows * n * k / dt / 1e12, dt, rows
+        rows = int(min(max_rows, max(rows * 2, rows * target_s / max(dt, 1e-3) * 0.9)))
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    w = WORKLOADS[args.workload]
+    threads = os.cpu_count() or 1
+    per_step = max(1.0, args.cpu_seconds / max(args.steps, 1))
+    for _ in range(args.warmup):
+        cpu_gemm_tops(w["n"], w["k"], threads, 0.2, 4)
+    values, rows = [], 0
+    for _ in range(args.steps):
+        tops, dt, rows = cpu_gemm_tops(w["n"], w["k"], threads, per_step, w["m"])
+        values.append(tops)
+    tops = statistics.median(values)
+    full_ms = 2.0 * w["batch"] * w["m"] * w["n"] * w["k"] / (tops * 1e12) * 1e3
+    sample = (f"{rows} of {w['m']} rows of A against the full B ({w['n']} x K {w['k']}) per step, extrapolated; "
+              f"oracle og_oracle_int8_gemm (restates Int8Tests.Reference) on {threads} threads")
+    line = {"metric": METRIC, "impl": "reference", "value": round(tops, 6), "unit": "TOPS", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(full_ms, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"{args.workload}: {w['desc']}", "parallelism": "host threads",
+                       "sample": sample},
+            "cpu_baseline": {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(tops, 6), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, local_rank: int, dist):
+    import onegpu_cuda as og
+
+    w = WORKLOADS[args.workload]
+    dev = og.GpuDevice(local_rank)
+    M, N, K, B = w["m"], w["n"], w["k"], w["batch"]
+    shard_n = N // world
+    n0 = rank * shard_n
+    rng = np.random.default_rng(1234)
+    a_dtype = np.int8 if w["a_signed"] else np.uint8
+    # Synthetic inputs with the config's distributions, generated on the host once.
+    a_host = rng.integers(-128 if w["a_signed"] else 0, 128 if w["a_signed"] else 256, size=B * M * K,
+                          dtype=np.int16).astype(a_dtype)
+    b_full_cols = rng.integers(-128 if args.workload == "c3" else -127, 128, size=(K, N), dtype=np.int16)
+    b_host = np.ascontiguousarray(b_full_cols[:, n0:n0 + shard_n]).astype(np.int8).reshape(-1)
+    del b_full_cols
+    a = dev.create_buffer(a_dtype, a_host)
+    b = dev.create_buffer(np.int8, b_host)
+    count = B * M * shard_n
+    out_dtype = {"i32": np.int32, "f32": np.float32}[w["out"]]
+    c = dev.create_buffer(out_dtype, count)
+    zpa = zpb = scale = None
+    extra = []
+    if w["zp"]:
+        za = dev.create_buffer(a_dtype, np.array([128 if not w["a_signed"] else 0], a_dtype))
+        zb = dev.create_buffer(np.int8, rng.integers(-8, 9, size=shard_n).astype(np.int8))
+        zpa, zpb = og.Int8Operand(za, 0), og.Int8Operand(zb, 0, True)
+        extra += [za, zb]
+    if w["out"] == "f32":
+        s = dev.create_buffer(np.float32, rng.uniform(0.001, 0.02, size=shard_n).astype(np.float32) * 0.02)
+        scale = og.Int8Operand(s, 0, True)
+        extra.append(s)
+    flush = dev.create_buffer(np.uint8, 512 << 20)
+    prob = og.Int8GemmProblem(M, shard_n, K, batch=B, stride_a=M * K if B > 1 else 0, stride_b=0)
+    gemm = og.Int8Gemm(dev)
+
+    def encode(enc):
+        if w["out"] == "f32":
+            gemm.encode_float(enc, prob, a, b, c, scale, zpa, zpb)
+        else:
+            gemm.encode_int32(enc, prob, a, b, c, zpa, zpb)
+
+    stamps = og.GpuTimestampSet(dev, 2 * args.steps + 2)
+
+    def step(i=None):
+        flush.fill(i if i is not None else 0)
+        enc = dev.begin_commands()
+        if i is not None:
+            enc.write_timestamp(stamps, 2 * i)
+        encode(enc)
+        if i is not None:
+            enc.write_timestamp(stamps, 2 * i + 1)
+        launches = enc.dispatch_count
+        dev.submit(enc)
+        return launches
+
+    for _ in range(args.warmup):
+        step()
+    dev.wait_idle()
+    kernel = gemm.last_kernel
+    launches = 0
+
+    def barrier():
+        if dist is not None:
+            import torch
+            dist.barrier(device_ids=[local_rank])
+            torch.cuda.synchronize(local_rank)
+
+    barrier()
+    with ClockSampler(local_rank) as clocks:
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            launches += step(i)
+        dev.wait_idle()
+        wall = time.perf_counter() - t0
+    barrier()
+    ts = stamps.read(0)
+    per_step_ns = [ts[2 * i + 1] - ts[2 * i] for i in range(args.steps)]
+    gemm_ns = sum(per_step_ns)
+
+    # e2e through the C ABI from pinned host memory: upload A and the B slab, product, readback of C.
+    import ctypes
+    h2d = a_host.nbytes + b_host.nbytes
+    d2h = count * np.dtype(out_dtype).itemsize
+    pin = ctypes.c_void_p()
+    og._check(og._lib.og_host_alloc(h2d + d2h, ctypes.byref(pin)))
+    ctypes.memmove(pin.value, a_host.ctypes.data, a_host.nbytes)
+    ctypes.memmove(pin.value + a_host.nbytes, b_host.ctypes.data, b_host.nbytes)
+    e2e_stamps = og.GpuTimestampSet(dev, 2 * args.steps)
+    for i in range(-1, args.steps):
+        idx = max(i, 0)
+        if i >= 0:
+            dev.timestamp(e2e_stamps, 2 * idx)
+        og._check(og._lib.og_buffer_write(dev.handle, a.ptr, pin.value, a_host.nbytes))
+        og._check(og._lib.og_buffer_write(dev.handle, b.ptr, pin.value + a_host.nbytes, b_host.nbytes))
+        enc = dev.begin_commands()
+        encode(enc)
+        dev.submit(enc)
+        og._check(og._lib.og_buffer_read(dev.handle, pin.value + h2d, c.ptr, d2h))
+        if i >= 0:
+            dev.timestamp(e2e_stamps, 2 * idx + 1)
+    ets = e2e_stamps.read(0)
+    e2e_ns = sum(ets[2 * i + 1] - ets[2 * i] for i in range(args.steps))
+    og._check(og._lib.og_host_free(pin))
+
+    # cuBLAS (torch._int_mm) on the same shard for context: library int8 throughput on this GPU.
+    lib_tops = None
+    if args.workload == "c3" and not args.no_library:
+        try:
+            import torch
+            ta = torch.from_numpy(a_host.reshape(M, K)).cuda(local_rank)
+            tb = torch.from_numpy(b_host.reshape(K, shard_n)).cuda(local_rank)
+            for _ in range(3):
+                torch._int_mm(ta, tb)
+            torch.cuda.synchronize(local_rank)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(5):
+                torch._int_mm(ta, tb)
+            e1.record()
+            torch.cuda.synchronize(local_rank)
+            lib_tops = 2.0 * M * shard_n * K * 5 / (e0.elapsed_time(e1) * 1e-3) / 1e12
+            del ta, tb
+        except Exception as exc:  # noqa: BLE001 - context only
+            lib_tops = f"unavailable: {type(exc).__name__}"
+
+    local = np.array([gemm_ns, e2e_ns], dtype=np.float64)
+    if dist is not None:
+        import torch
+        t = torch.tensor(local, device=f"cuda:{local_rank}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        local = t.cpu().numpy()
+    gemm_ns, e2e_ns = float(local[0]), float(local[1])
+
+    total_ops = 2.0 * B * M * N * K
+    ms_per_step = gemm_ns / args.steps / 1e6
+    value = total_ops / (ms_per_step * 1e-3) / 1e12
+    per_launch_s = statistics.mean(per_step_ns) * 1e-9
+    shard_ops = 2.0 * B * M * shard_n * K
+    achieved = shard_ops / per_launch_s / 1e12
+    peaks = load_peaks()
+    peak = 2.0 * peaks["bf16_tflops"]
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            threads = os.cpu_count() or 1
+            tops, dt, rows = cpu_gemm_tops(shard_n, K, threads, args.cpu_seconds, M)
+            cpu = {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port",
+                   "sample": f"{rows} of {M} rows x {shard_n} x K {K} on {threads} threads "
+                             f"({dt:.1f} s), extrapolated to TOPS"}
+        clk = clocks.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": f"{args.workload}: {w['desc']}", "m": M, "n": N, "k": K, "batch": B,
+                       "parallelism": f"N-shard x{world}" if world > 1 else "single GPU",
+                       "l2": "flushed before every step (512 MB write), steps timed by CUDA events",
+                       "kernel": kernel, "variant": gemm.variant},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 1), "unit": "TOPS",
+                         "frac": round(achieved / peak, 4), "traffic": profile_traffic(args.workload),
+                         "peak_source": f"2 x {peaks['source']} dense bf16 burst ({peaks['bf16_tflops']} TF/s): "
+                                        "int8 dense rate is twice bf16 on B200"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(total_ops / (e2e_ns / args.steps * 1e-9) / 1e12, 3), "unit": "TOPS",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "library_int8_tops": round(lib_tops, 3) if isinstance(lib_tops, float) else lib_tops,
+            "wall_s": round(wall, 3),
+        }
+        print(json.dumps(line), flush=True)
+    for v in [a, b, c, flush] + extra:
+        v.dispose()
+    gemm.dispose()
+    stamps.dispose()
+    e2e_stamps.dispose()
+    dev.dispose()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-library", action="store_true")
+    args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as tdist
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                 device_id=torch.device(f"cuda:{local_rank}"))
+        dist = tdist
+    try:
+        run_ours(args, rank, world, local_rank, dist)
+    finally:
+        if dist is not None:
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,251 @@
+/*
+ * onegpu_cuda.h - C ABI of libonegpu_cuda.so, the B200 (sm_100a) backend of onegpu's quantized-matmul path.
+ *
+ * The reference (recursive-ai-oss/onegpu-csharp) has no FFI of its own: its boundary is the shipped C# API of
+ * RecursiveAI.OneGpu.Kernels (PublicAPI.Shipped.txt) written against the GpuDevice abstraction. Each entry point below
+ * is what a `RecursiveAI.OneGpu.Cuda` backend binds through [LibraryImport] to keep that API drop-in; the comment on
+ * each names the reference member it replaces (paths relative to the reference repository root).
+ *
+ * Conventions
+ *  - Every function returns og_status. On failure, og_last_error() (per calling thread) holds the typed error the C#
+ *    side turns into its exception: operation / argument / message for GpuKernelShapeException and
+ *    ArgumentNullException, capability / expected / actual for GpuUnsupportedException.
+ *  - Argument checks run synchronously, before anything is recorded, in the reference's order and with the
+ *    reference's argument names (src/RecursiveAI.OneGpu.Kernels/Int8Gemm.cs:393-501,
+ *    src/RecursiveAI.OneGpu.Kernels/DynamicQuantizeKernels.cs:59-75, KernelSupport.cs:75-91).
+ *  - Buffers are plain device pointers with an element count and element type (og_buffer): the caller owns them.
+ *  - Encoders record; nothing runs until og_device_submit, which replays the recorded work in order on the device's
+ *    stream (src/RecursiveAI.OneGpu/GpuDevice.cs:155-167).
+ *  - Objects are not thread-safe, like the reference's (Int8Gemm.cs:122, DynamicQuantizeKernels.cs:18).
+ * No C++ exception crosses this boundary.
+ */
+#ifndef ONEGPU_CUDA_H
+#define ONEGPU_CUDA_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define OG_API __attribute__((visibility("default")))
+#else
+#define OG_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status and errors --------------------------------------------------------------------------------------- */
+
+typedef enum og_status {
+    OG_OK = 0,
+    OG_ERROR_SHAPE = 1,           /* GpuKernelShapeException (GpuKernelShapeException.cs:7-25) */
+    OG_ERROR_UNSUPPORTED = 2,     /* GpuUnsupportedException (src/RecursiveAI.OneGpu/GpuDevice.cs:283-312) */
+    OG_ERROR_ARGUMENT_NULL = 3,   /* ArgumentNullException */
+    OG_ERROR_ARGUMENT_RANGE = 4,  /* ArgumentOutOfRangeException (Int8Gemm.cs:541-542) */
+    OG_ERROR_OUT_OF_MEMORY = 5,   /* GpuOutOfMemoryException */
+    OG_ERROR_DEVICE_LOST = 6,     /* GpuDeviceLostException (GpuDevice.cs:377): a sticky CUDA error */
+    OG_ERROR_COMMAND_FAILED = 7,  /* GpuCommandFailedException (GpuDevice.cs:337-374): a kernel reported a failure */
+    OG_ERROR_CUDA = 8,            /* any other CUDA runtime error */
+    OG_ERROR_INVALID_HANDLE = 9
+} og_status;
+
+typedef struct og_error_info {
+    int32_t status;
+    char operation[64];   /* "Int8Gemm", "DynamicQuantizeLinear", ... */
+    char argument[64];    /* "M", "OffsetA", "zpA", "scratch", ... (GpuKernelShapeException.Argument) */
+    char message[512];
+    char capability[64];  /* GpuUnsupportedException.Capability */
+    char expected[128];
+    char actual[128];
+} og_error_info;
+
+/* The last error raised on the calling thread. */
+OG_API og_status og_last_error(og_error_info* out);
+
+/* ---- element types and buffer views ---------------------------------------------------------------------------- */
+
+typedef enum og_element_type {
+    OG_U8 = 0,  /* byte */
+    OG_S8 = 1,  /* sbyte */
+    OG_I32 = 2, /* int */
+    OG_F32 = 3, /* float */
+    OG_F16 = 4, /* Half */
+    OG_U32 = 5  /* uint */
+} og_element_type;
+
+/* A GpuBuffer<T> (src/RecursiveAI.OneGpu/GpuBufferOfT.cs:11): device pointer of element 0, element count, type. */
+typedef struct og_buffer {
+    void* ptr;
+    int64_t length;
+    int32_t type;
+} og_buffer;
+
+/* Int8Operand<T> (Int8Gemm.cs:28): a zero point, scale or bias - buffer, element offset, one value or a vector. */
+typedef struct og_operand {
+    og_buffer buffer;
+    int32_t offset;
+    int32_t is_vector;
+} og_operand;
+
+/* ---- device (compute subset of GpuDevice, src/RecursiveAI.OneGpu/GpuDevice.cs:27-228) ------------------------- */
+
+typedef struct og_device og_device;
+typedef struct og_encoder og_encoder;
+typedef struct og_timestamps og_timestamps;
+
+typedef struct og_device_info {
+    char name[256];          /* GpuAdapterInfo.Name */
+    int32_t ordinal;
+    int32_t sm_count;
+    int32_t cc_major, cc_minor;
+    int64_t total_memory;    /* bytes */
+    int32_t max_shared_memory_per_block;
+    int32_t tensor_core_i8;  /* 1 when the tcgen05 int8 product runs here */
+} og_device_info;
+
+OG_API og_status og_device_count(int32_t* count);
+/* GpuBackends.CreateDevice (src/RecursiveAI.OneGpu.Backends/GpuBackends.cs:69-72) for the CUDA backend. */
+OG_API og_status og_device_create(int32_t ordinal, og_device** out);
+/* GpuDevice.Dispose: waits for the device's work, then releases it. */
+OG_API og_status og_device_destroy(og_device* device);
+OG_API og_status og_device_info_get(og_device* device, og_device_info* out);
+/* GpuDevice.WaitIdle. Also reports (once) a failure a kernel recorded since the last check. */
+OG_API og_status og_device_wait_idle(og_device* device);
+/* The cudaStream_t submissions run on; og_device_set_stream binds an external one (e.g. a framework's). */
+OG_API og_status og_device_stream(og_device* device, void** stream);
+OG_API og_status og_device_set_stream(og_device* device, void* stream);
+
+/* GpuDevice.CreateBuffer<T> / GpuBuffer.Dispose: device memory. Free is stream-ordered: it happens once the work
+ * submitted before it has finished (GpuBufferOfT.cs:77-78). */
+OG_API og_status og_buffer_alloc(og_device* device, uint64_t bytes, void** ptr);
+OG_API og_status og_buffer_free(og_device* device, void* ptr);
+/* GpuDevice.WriteBuffer: the upload runs before any later submission (GpuDevice.cs:163-167). */
+OG_API og_status og_buffer_write(og_device* device, void* dst, const void* host_src, uint64_t bytes);
+/* GpuBuffer<T>.ReadAsync (GpuBufferOfT.cs:63-75) completed synchronously: returns after all prior work and the copy. */
+OG_API og_status og_buffer_read(og_device* device, void* host_dst, const void* src, uint64_t bytes);
+/* Fills bytes of a buffer with a value, in stream order. */
+OG_API og_status og_buffer_fill(og_device* device, void* dst, int32_t value, uint64_t bytes);
+/* Page-locked host memory for fast uploads and readbacks. */
+OG_API og_status og_host_alloc(uint64_t bytes, void** ptr);
+OG_API og_status og_host_free(void* ptr);
+
+/* ---- encoders and timestamps (GpuCommandEncoder, Resources.cs:148-243; GpuTimestampSet, GpuDevice.cs:103-109) ---- */
+
+/* GpuDevice.BeginCommands. */
+OG_API og_status og_encoder_begin(og_device* device, og_encoder** out);
+/* GpuDevice.Submit (GpuDevice.cs:161): replays the recorded work in order on the device stream; consumes the
+ * encoder whatever the outcome. */
+OG_API og_status og_device_submit(og_device* device, og_encoder* encoder);
+OG_API og_status og_encoder_discard(og_encoder* encoder);
+/* Number of kernel launches the encoder holds (GpuCommandEncoder.DispatchCount). */
+OG_API og_status og_encoder_dispatch_count(og_encoder* encoder, int64_t* count);
+
+OG_API og_status og_timestamps_create(og_device* device, uint32_t count, og_timestamps** out);
+OG_API og_status og_timestamps_destroy(og_timestamps* set);
+/* Records timestamp `index` at this point of the encoder (between recorded operations). */
+OG_API og_status og_encoder_timestamp(og_encoder* encoder, og_timestamps* set, uint32_t index);
+/* Records timestamp `index` on the device stream now (outside any encoder), e.g. around uploads and readbacks. */
+OG_API og_status og_device_timestamp(og_device* device, og_timestamps* set, uint32_t index);
+/* GpuDevice.TryReadTimestamps: nanoseconds of each timestamp relative to timestamp `first`; waits for them. */
+OG_API og_status og_timestamps_read(og_timestamps* set, uint32_t first, uint32_t count, double* ns);
+
+/* ---- Int8Gemm (src/RecursiveAI.OneGpu.Kernels/Int8Gemm.cs:124-683) --------------------------------------------- */
+
+typedef struct og_int8_gemm og_int8_gemm;
+
+/* Int8GemmProblem (Int8Gemm.cs:43-95). Lda/Ldb 0 = dense. OffsetA/OffsetB/StrideA/StrideB in bytes, OffsetC in
+ * elements of the output. */
+typedef struct og_int8_gemm_problem {
+    int32_t m, n, k, batch;
+    int32_t transpose_b;
+    int32_t lda, ldb;
+    int32_t offset_a, offset_b, offset_c;
+    int32_t stride_a, stride_b;
+} og_int8_gemm_problem;
+
+/* Kernel choice for og_int8_gemm_options.kernel (a test hook like Int8GemmOptions.Tile, Int8Gemm.cs:15-19). */
+typedef enum og_int8_kernel {
+    OG_KERNEL_AUTO = 0,         /* tensor cores when the operands allow, else the portable kernel */
+    OG_KERNEL_TENSOR_CORE = 1,  /* tcgen05 only; OG_ERROR_UNSUPPORTED when the operands do not allow it */
+    OG_KERNEL_PORTABLE = 2      /* the SIMT kernel */
+} og_int8_kernel;
+
+/* Int8GemmOptions (Int8Gemm.cs:7-21). allow_packed_dot = 0 forces the portable variant, as in the reference. */
+typedef struct og_int8_gemm_options {
+    int32_t allow_packed_dot;
+    int32_t kernel;
+} og_int8_gemm_options;
+
+/* new Int8Gemm(device, options) (Int8Gemm.cs:153-177). options may be NULL (defaults). */
+OG_API og_status og_int8_gemm_create(og_device* device, const og_int8_gemm_options* options, og_int8_gemm** out);
+/* Int8Gemm.Dispose (Int8Gemm.cs:378-391): waits for the device, releases the instance's scratch. */
+OG_API og_status og_int8_gemm_destroy(og_int8_gemm* gemm);
+/* Int8Gemm.Variant (Int8Gemm.cs:215). */
+OG_API og_status og_int8_gemm_variant(og_int8_gemm* gemm, char* buffer, uint64_t capacity);
+/* The kernel the last encode call recorded ("tensor-core", "portable" or "none"); a diagnostic. */
+OG_API og_status og_int8_gemm_last_kernel(og_int8_gemm* gemm, char* buffer, uint64_t capacity);
+/* Int8Gemm.ScratchElements (Int8Gemm.cs:531). */
+OG_API int64_t og_int8_gemm_scratch_elements(const og_int8_gemm_problem* problem);
+/* Int8Gemm.ReserveScratch (Int8Gemm.cs:539-549): OG_ERROR_ARGUMENT_RANGE when negative or above int.MaxValue. */
+OG_API og_status og_int8_gemm_reserve_scratch(og_int8_gemm* gemm, int64_t elements);
+/* Int8Gemm.BindGroupsCreated (Int8Gemm.cs:366): always 0 on CUDA, where kernel arguments are passed by value. */
+OG_API og_status og_int8_gemm_bind_groups_created(og_int8_gemm* gemm, int32_t* count);
+
+/* Int8Gemm.EncodeInt32<TA,TB> (Int8Gemm.cs:230-253). zero_point_a / zero_point_b / bias may be NULL. */
+OG_API og_status og_int8_gemm_encode_int32(og_int8_gemm* gemm, og_encoder* encoder, const og_int8_gemm_problem* problem,
+                                           const og_buffer* a, const og_buffer* b, const og_buffer* c,
+                                           const og_operand* zero_point_a, const og_operand* zero_point_b,
+                                           const og_operand* bias);
+/* Int8Gemm.EncodeFloat<TA,TB> (Int8Gemm.cs:270-314). */
+OG_API og_status og_int8_gemm_encode_float(og_int8_gemm* gemm, og_encoder* encoder, const og_int8_gemm_problem* problem,
+                                           const og_buffer* a, const og_buffer* b, const og_buffer* c,
+                                           const og_operand* scale, const og_operand* zero_point_a,
+                                           const og_operand* zero_point_b, const og_operand* float_bias,
+                                           const og_operand* int_bias);
+/* Int8Gemm.EncodeRequantized<TA,TB,TY> (Int8Gemm.cs:336-363). scratch (Int8Scratch, Int8Gemm.cs:37) may be NULL; its
+ * buffer is an int32 buffer and its offset an element offset. */
+OG_API og_status og_int8_gemm_encode_requantized(og_int8_gemm* gemm, og_encoder* encoder,
+                                                 const og_int8_gemm_problem* problem, const og_buffer* a,
+                                                 const og_buffer* b, const og_buffer* y, const og_operand* multiplier,
+                                                 int32_t zero_point_y, const og_operand* zero_point_a,
+                                                 const og_operand* zero_point_b, const og_operand* int_bias,
+                                                 const og_operand* scratch);
+
+/* The argument checks of the three forms alone (no device needed): the same checks, in the same order, that the
+ * encode functions run before recording (Int8Gemm.cs:230-253, 270-314, 336-363, 419-501). */
+OG_API og_status og_int8_gemm_check_int32(const og_int8_gemm_problem* problem, const og_buffer* a, const og_buffer* b,
+                                          const og_buffer* c, const og_operand* zero_point_a,
+                                          const og_operand* zero_point_b, const og_operand* bias);
+OG_API og_status og_int8_gemm_check_float(const og_int8_gemm_problem* problem, const og_buffer* a, const og_buffer* b,
+                                          const og_buffer* c, const og_operand* scale, const og_operand* zero_point_a,
+                                          const og_operand* zero_point_b, const og_operand* float_bias,
+                                          const og_operand* int_bias);
+OG_API og_status og_int8_gemm_check_requantized(const og_int8_gemm_problem* problem, const og_buffer* a,
+                                                const og_buffer* b, const og_buffer* y, const og_operand* multiplier,
+                                                int32_t zero_point_y, const og_operand* zero_point_a,
+                                                const og_operand* zero_point_b, const og_operand* int_bias,
+                                                const og_operand* scratch);
+
+/* ---- DynamicQuantizeKernels (src/RecursiveAI.OneGpu.Kernels/DynamicQuantizeKernels.cs:20-110) ------------------- */
+
+typedef struct og_dynamic_quantize og_dynamic_quantize;
+
+/* new DynamicQuantizeKernels(device) (DynamicQuantizeKernels.cs:36-45): keeps a small partials buffer. */
+OG_API og_status og_dynamic_quantize_create(og_device* device, og_dynamic_quantize** out);
+OG_API og_status og_dynamic_quantize_destroy(og_dynamic_quantize* dq);
+/* DynamicQuantizeKernels.Encode (DynamicQuantizeKernels.cs:59-90): x float32, y uint8, scale float32, zeroPoint
+ * uint8 (only the byte at offset_zero_point is written). */
+OG_API og_status og_dynamic_quantize_encode(og_dynamic_quantize* dq, og_encoder* encoder, const og_buffer* x,
+                                            int32_t offset_x, int32_t count, const og_buffer* y, int32_t offset_y,
+                                            const og_buffer* scale, int32_t offset_scale, const og_buffer* zero_point,
+                                            int32_t offset_zero_point);
+/* The checks of Encode alone (DynamicQuantizeKernels.cs:61-75). */
+OG_API og_status og_dynamic_quantize_check(const og_buffer* x, int32_t offset_x, int32_t count, const og_buffer* y,
+                                           int32_t offset_y, const og_buffer* scale, int32_t offset_scale,
+                                           const og_buffer* zero_point, int32_t offset_zero_point);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ONEGPU_CUDA_H */

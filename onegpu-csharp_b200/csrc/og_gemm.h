@@ -1,0 +1,46 @@
+// Internal launch descriptions shared by the host layer (og_capi.cu) and the kernel files.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "og_kernels.cuh"
+
+namespace og {
+
+// One validated product, pointers resolved: a and b point at the first byte of batch 0 (OffsetA/OffsetB applied),
+// the epilogue's output pointer at element OffsetC.
+struct GemmLaunch {
+    const uint8_t* a;
+    const uint8_t* b;
+    int m, n, k, batch;
+    int trans_b;
+    int64_t lda, ldb;        // bytes
+    int64_t stride_a, stride_b;
+    int a_signed, b_signed;
+    Epilogue epi;
+    int num_sms;
+    int* error_flag;
+};
+
+// tcgen05 product (og_gemm_tc.cu). Eligible when K >= 1 and both operands' rows and batches start on 16-byte
+// boundaries (the TMA requirement).
+bool tc_eligible(const GemmLaunch& L);
+cudaError_t launch_gemm_tc(const GemmLaunch& L, cudaStream_t stream);
+
+// Portable SIMT product (og_gemm_simt.cu): any alignment, subtracts the zero points while staging, so it needs no
+// byte sums; its epilogue ignores row_sum_a / col_sum_b.
+cudaError_t launch_gemm_simt(const GemmLaunch& L, cudaStream_t stream);
+
+// Byte sums for the zero-point correction (og_gemm_simt.cu): row sums of A ([batchA][M], batchA = batch when A has
+// its own stride, else 1) when `row_sums` is set, column sums of B ([batchB][N]) when `col_sums` is set.
+cudaError_t launch_byte_sums(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, cudaStream_t stream);
+
+// DynamicQuantizeLinear (og_dq.cu).
+struct DqScratch;
+size_t dq_scratch_bytes();
+cudaError_t launch_dynamic_quantize(const float* x, int64_t count, uint8_t* y, float* scale_out, uint8_t* zp_out,
+                                    DqScratch* scratch, int num_sms, cudaStream_t stream);
+
+}  // namespace og

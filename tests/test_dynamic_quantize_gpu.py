@@ -1,0 +1,98 @@
+"""DynamicQuantizeKernels on the GPU through the C ABI, bit for bit against the oracle (Int8Tests.cs:617-751)."""
+import numpy as np
+import pytest
+
+import og_oracle as oracle
+import onegpu_cuda as og
+from cases import golden, oracle_shape, problem
+
+pytestmark = pytest.mark.gpu
+
+
+def test_dynamic_quantize_is_bit_exact(device):
+    """DynamicQuantizeIsBitExact: 15 counts x 7 distributions, odd offsets, sentinel bytes around every output."""
+    t = golden()["tables"]["dq_counts"]
+    off_x, off_y, off_s, off_z = 1, 3, 2, 5
+    with og.DynamicQuantizeKernels(device) as dq:
+        seed = 1
+        bad = 0
+        for count in t["counts"]:
+            for kind in t["kinds"]:
+                x = oracle.dq_input(count, seed, kind)
+                wy, ws, wz = oracle.dynamic_quantize(x)
+                xs = np.concatenate([np.zeros(off_x, np.float32), x])
+                y_init = np.full(((off_y + count + 3) & ~3) + 4, 0x3C, np.uint8)
+                z_init = np.full(8, 0xEE, np.uint8)
+                bx = device.create_buffer(np.float32, xs)
+                by = device.create_buffer(np.uint8, y_init)
+                bs = device.create_buffer(np.float32, np.zeros(4, np.float32))
+                bz = device.create_buffer(np.uint8, z_init)
+                enc = device.begin_commands()
+                dq.encode(enc, bx, off_x, count, by, off_y, bs, off_s, bz, off_z)
+                device.submit(enc)
+                y, s, z = by.read(), bs.read(), bz.read()
+                here = int(np.count_nonzero(y[off_y:off_y + count] != wy))
+                here += int(s[off_s].view(np.uint32) != np.float32(ws).view(np.uint32))
+                here += int(z[off_z] != wz)
+                here += int(np.count_nonzero(y[:off_y] != 0x3C)) + int(np.count_nonzero(y[off_y + count:] != 0x3C))
+                here += int(np.count_nonzero(np.delete(z, off_z) != 0xEE))
+                assert here == 0, f"count {count} kind {kind}: scale {s[off_s]!r} want {ws!r}, zero {z[off_z]} want {wz}"
+                bad += here
+                for v in (bx, by, bs, bz):
+                    v.dispose()
+                seed += 1
+        assert bad == 0
+
+
+@pytest.mark.parametrize("count", [4096 * 4096, 8 * 2048 * 4096 + 5])
+def test_dynamic_quantize_full_size(device, count):
+    """The configs' sizes (16.8 M and 67 M elements) against the oracle, aligned and misaligned offsets."""
+    rng = np.random.default_rng(count)
+    x = rng.standard_normal(count).astype(np.float32) * np.float32(0.5)
+    wy, ws, wz = oracle.dynamic_quantize(x)
+    with og.DynamicQuantizeKernels(device) as dq:
+        for off in (0, 1):
+            bx = device.create_buffer(np.float32, np.concatenate([np.zeros(off, np.float32), x]))
+            by = device.create_buffer(np.uint8, count + off)
+            bs = device.create_buffer(np.float32, 1)
+            bz = device.create_buffer(np.uint8, 1)
+            enc = device.begin_commands()
+            dq.encode(enc, bx, off, count, by, off, bs, 0, bz, 0)
+            device.submit(enc)
+            assert np.array_equal(by.read()[off:], wy)
+            assert bs.read()[0].view(np.uint32) == np.float32(ws).view(np.uint32)
+            assert int(bz.read()[0]) == wz
+            for v in (bx, by, bs, bz):
+                v.dispose()
+
+
+def test_dynamic_quantize_feeds_the_product_without_leaving_the_device(device):
+    """DynamicQuantizeFeedsTheProductWithoutLeavingTheDevice (Int8Tests.cs:705-751): quantize, then the float form
+    with the activation's zero point read from the device; expected (float)sum * (a_scale * w_scale[n])."""
+    M, N, K = 128, 384, 384
+    x = oracle.random(M * K, 3, -3.0, 5.0)
+    wy, wscale, wzero = oracle.dynamic_quantize(x)
+    w = oracle.bytes_(N * K, 4)
+    wscales = (np.float32(0.002) + (np.arange(N) % 17).astype(np.float32) * np.float32(1e-4)).astype(np.float32)
+    p = problem(M, N, K, trans_b=True)
+    sums = oracle.int8_gemm(wy, False, w, True, np.array([wzero], np.uint8), False, **oracle_shape(p))
+    scale_vec = (np.float32(wscale) * wscales).astype(np.float32)  # the elementwise Mul of the chain, in float32
+    want = (sums.astype(np.float32) * np.tile(scale_vec, M)).astype(np.float32)
+    with og.DynamicQuantizeKernels(device) as dq, og.Int8Gemm(device) as gemm:
+        bx = device.create_buffer(np.float32, x)
+        by = device.create_buffer(np.uint8, M * K)
+        bs = device.create_buffer(np.float32, 1)
+        bz = device.create_buffer(np.uint8, 1)
+        bw = device.create_buffer(np.int8, w.view(np.int8))
+        bscale = device.create_buffer(np.float32, scale_vec)
+        bc = device.create_buffer(np.float32, M * N)
+        enc = device.begin_commands()
+        dq.encode(enc, bx, 0, M * K, by, 0, bs, 0, bz, 0)
+        gemm.encode_float(enc, og.Int8GemmProblem(**p), by, bw, bc, og.Int8Operand(bscale, 0, True),
+                          og.Int8Operand(bz, 0))
+        device.submit(enc)
+        got = bc.read()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+        assert bs.read()[0].view(np.uint32) == np.float32(wscale).view(np.uint32)
+        for v in (bx, by, bs, bz, bw, bscale, bc):
+            v.dispose()

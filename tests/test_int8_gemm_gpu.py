@@ -1,0 +1,301 @@
+"""Int8Gemm on the GPU through the C ABI, bit for bit against the oracle.
+
+Mirrors tests/RecursiveAI.OneGpu.Kernels.Tests/Int8Tests.cs (EdgeShapesAreBitExact, ModelShapesAreBitExact,
+ForcingTheDotVariantOffChangesNothing, FloatAndRequantizedFormsAreBitExact, RequantizationRoundsHalfToEvenAndSaturates,
+BadArgumentsAreRejected), Int8ScratchTests.cs, MultiDeviceTests.cs and ConvIntegerTests.cs:343-392, run on both
+kernels (the tcgen05 tensor-core kernel on TMA-aligned copies of each case, and the portable SIMT kernel).
+"""
+import numpy as np
+import pytest
+
+import og_oracle as oracle
+import onegpu_cuda as og
+from cases import (Case, case_data, edge_cases, float_biases, float_scale, golden, oracle_shape, problem, requant_bias,
+                   requant_mult)
+from gpu_rig import SENTINEL, align_case, run_int32, typed
+
+pytestmark = pytest.mark.gpu
+
+
+def configs(device):
+    return [("default", og.Int8Gemm(device)),
+            ("portable", og.Int8Gemm(device, og.Int8GemmOptions(allow_packed_dot=False))),
+            ("tensor-core", og.Int8Gemm(device, og.Int8GemmOptions(kernel=og.KERNEL_TENSOR_CORE)))]
+
+
+def test_edge_shapes_are_bit_exact(device):
+    cases = edge_cases()
+    aligned = [align_case(c) for c in cases]
+    total = {}
+    for name, gemm in configs(device):
+        with gemm:
+            bad = 0
+            kernels = set()
+            for seed, c in enumerate(cases + aligned, start=1):
+                if name == "tensor-core" and (c.p["k"] == 0 or "aligned" not in c.name):
+                    continue
+                b, k = run_int32(device, gemm, c, seed)
+                kernels.add(k)
+                assert b == 0, f"[{name}] {c.name} signed {c.a_signed}/{c.b_signed} zp {c.za_mode}/{c.zb_mode}"
+                bad += b
+            total[name] = kernels
+    assert total["portable"] == {"portable"}
+    assert total["tensor-core"] == {"tensor-core"}
+
+
+def test_model_shapes_are_bit_exact(device):
+    """ModelShapesAreBitExact: uint8 activations with a zero point, int8 weights stored N x K."""
+    for name, m, n, k in golden()["tables"]["model_shapes"]["shapes"]:
+        c = Case(name, problem(m, n, k, trans_b=True), False, True, 1, 0)
+        data = case_data(c, m + n + k, oracle.bytes_)
+        a, b, za, _ = data
+        want = oracle.int8_gemm(a, False, b, True, za, False, **oracle_shape(c.p))
+        for cfg, gemm in configs(device):
+            with gemm:
+                bad, kern = run_int32(device, gemm, c, m + n + k, want, data)
+                assert bad == 0, f"{name} [{cfg}] via {kern}"
+
+
+def test_forcing_the_dot_variant_off_changes_nothing(device):
+    with og.Int8Gemm(device) as chosen, og.Int8Gemm(device, og.Int8GemmOptions(allow_packed_dot=False)) as forced:
+        c = Case("forced", problem(70, 90, 100), False, True, 1, 2)
+        assert run_int32(device, chosen, c, 5)[0] == 0
+        assert run_int32(device, forced, c, 5)[0] == 0
+        assert chosen.variant.startswith("tcgen05-i8")
+        assert forced.variant.startswith("portable")
+        assert chosen.bind_groups_created == 0
+
+
+def float_case(device, gemm, m, n, k, scale_vec, with_ib, with_fb, seed, aligned=False):
+    """FloatCase (Int8Tests.cs:334-386)."""
+    p = problem(m, n, k)
+    if aligned:
+        p = align_case(Case("f", p)).p
+    a = oracle.bytes_(p["m"] * (p["lda"] or k) + 4 + p["offset_a"], seed)
+    b = oracle.bytes_(k * (p["ldb"] or n) + 4 + p["offset_b"], seed + 1)
+    za = oracle.bytes_(1, seed + 2)
+    zb = oracle.bytes_(n, seed + 3)
+    want = oracle.int8_gemm(a, False, b, True, za, False, zb, True, **oracle_shape(p))
+    scale = float_scale(n, scale_vec, seed)
+    ib, fb = float_biases(n)
+    expected = oracle.float_epilogue(want, np.resize(scale, want.size) if not scale_vec else np.tile(scale, m),
+                                     np.tile(ib, m) if with_ib else None, np.tile(fb, m) if with_fb else None)
+    bufs = dict(a=typed(device, a, False), b=typed(device, b, True), za=typed(device, za, False),
+                zb=typed(device, zb, True), s=device.create_buffer(np.float32, scale),
+                ib=device.create_buffer(np.int32, ib), fb=device.create_buffer(np.float32, fb),
+                c=device.create_buffer(np.float32, np.full(m * n, np.nan, np.float32)))
+    try:
+        enc = device.begin_commands()
+        gemm.encode_float(enc, og.Int8GemmProblem(**p), bufs["a"], bufs["b"], bufs["c"],
+                          og.Int8Operand(bufs["s"], 0, scale_vec), og.Int8Operand(bufs["za"], 0),
+                          og.Int8Operand(bufs["zb"], 0, True), og.Int8Operand(bufs["fb"], 0, True) if with_fb else None,
+                          og.Int8Operand(bufs["ib"], 0, True) if with_ib else None)
+        device.submit(enc)
+        got = bufs["c"].read()
+    finally:
+        for v in bufs.values():
+            v.dispose()
+    return int(np.count_nonzero(got.view(np.uint32) != expected.view(np.uint32)))
+
+
+def requant_case(device, gemm, m, n, k, mult_vec, unsigned, zero_y, with_bias, seed, a_signed, b_signed,
+                 aligned=False):
+    """RequantCase (Int8Tests.cs:388-466): odd output offset 3, sentinel bytes 0xA7 around the output."""
+    p = problem(m, n, k, off_c=3)
+    if aligned:
+        p = align_case(Case("q", p)).p
+    a = oracle.bytes_(p["m"] * (p["lda"] or k) + 4 + p["offset_a"], seed)
+    b = oracle.bytes_(k * (p["ldb"] or n) + 4 + p["offset_b"], seed + 1)
+    za = oracle.bytes_(1, seed + 2)
+    want = oracle.int8_gemm(a, a_signed, b, b_signed, za, False, **oracle_shape(p))
+    mult = requant_mult(n, mult_vec, seed)
+    ib = requant_bias(n)
+    acc = want.astype(np.int64) + (np.tile(ib, m) if with_bias else 0)
+    acc = ((acc + 2 ** 31) % 2 ** 32 - 2 ** 31).astype(np.int32)
+    expected = oracle.requant_array(acc, np.tile(mult, m) if mult_vec else np.resize(mult, acc.size), zero_y,
+                                    unsigned)
+    out = np.full(((3 + m * n + 3 + 3) // 4) * 4 + 4, 0xA7, np.uint8)
+    bufs = dict(a=typed(device, a, a_signed), b=typed(device, b, b_signed), za=typed(device, za, a_signed),
+                m=device.create_buffer(np.float32, mult), ib=device.create_buffer(np.int32, ib),
+                y=typed(device, out, not unsigned))
+    try:
+        enc = device.begin_commands()
+        gemm.encode_requantized(enc, og.Int8GemmProblem(**p), bufs["a"], bufs["b"], bufs["y"],
+                                og.Int8Operand(bufs["m"], 0, mult_vec), zero_y, og.Int8Operand(bufs["za"], 0), None,
+                                og.Int8Operand(bufs["ib"], 0, True) if with_bias else None)
+        device.submit(enc)
+        got = bufs["y"].read().view(np.uint8)
+    finally:
+        for v in bufs.values():
+            v.dispose()
+    bad = int(np.count_nonzero(got[3:3 + m * n] != expected))
+    bad += int(np.count_nonzero(got[:3] != 0xA7)) + int(np.count_nonzero(got[3 + m * n:] != 0xA7))
+    return bad
+
+
+@pytest.mark.parametrize("cfg", ["default", "portable", "tensor-core"])
+def test_float_and_requantized_forms_are_bit_exact(device, cfg):
+    gemm = dict(configs(device))[cfg]
+    aligned = cfg == "tensor-core"
+    with gemm:
+        bad_f = bad_q = 0
+        seed = 10
+        shapes = golden()["tables"]["float_requant_shapes"]["shapes"] + [[130, 80, 384], [64, 272, 128], [257, 33, 96]]
+        for (m, n, k) in shapes:
+            for vec in (False, True):
+                for ib, fb in ((False, False), (True, False), (False, True), (True, True)):
+                    bad_f += float_case(device, gemm, m, n, k, vec, ib, fb, seed, aligned)
+                    seed += 1
+            for vec in (False, True):
+                for unsigned, zero in golden()["tables"]["requant_output_modes"]["modes"]:
+                    bad_q += requant_case(device, gemm, m, n, k, vec, unsigned, zero, (seed & 1) == 0, seed,
+                                          (seed & 2) != 0, (seed & 4) != 0, aligned)
+                    seed += 1
+        assert bad_f == 0 and bad_q == 0
+
+
+@pytest.mark.parametrize("cfg", ["default", "tensor-core"])
+def test_requantization_rounds_half_to_even_and_saturates(device, cfg):
+    """Int8Tests.cs:503-547: a 1 x 1 product of K = 1 puts ties, saturation, NaN and infinity through the epilogue
+    (for the tensor-core kernel the product is padded to 16 x 16 x 16 with zeros)."""
+    gemm = dict(configs(device))[cfg]
+    pad = 16 if cfg == "tensor-core" else 1
+    with gemm:
+        for c in golden()["tables"]["requant_ties"]["cases"]:
+            a = np.zeros(pad * pad + 4, np.int8)
+            a[0] = c["a"]
+            b = np.zeros(pad * pad + 4, np.int8)
+            b[0] = 1
+            bufs = [device.create_buffer(np.int8, a), device.create_buffer(np.int8, b),
+                    device.create_buffer(np.float32, np.array([c["mult"]], np.float32)),
+                    typed(device, np.zeros(pad * pad + 4, np.uint8), not c["unsigned"])]
+            try:
+                enc = device.begin_commands()
+                gemm.encode_requantized(enc, og.Int8GemmProblem(pad, pad, pad), bufs[0], bufs[1], bufs[3],
+                                        og.Int8Operand(bufs[2], 0), c["zero"])
+                device.submit(enc)
+                got = int(bufs[3].read().view(np.uint8)[0])
+            finally:
+                for v in bufs:
+                    v.dispose()
+            assert got == c["expected"], c
+
+
+def test_bad_arguments_are_rejected_on_the_device(device):
+    """Int8Tests.cs:549-574 through the encode entry points: raised before anything is recorded."""
+    with og.Int8Gemm(device) as gemm:
+        a = device.create_buffer(np.uint8, 64)
+        b = device.create_buffer(np.int8, 64)
+        c = device.create_buffer(np.int32, 64)
+        f = device.create_buffer(np.float32, 64)
+        fl = device.create_buffer(np.float32, 1)
+        enc = device.begin_commands()
+        P, Op = og.Int8GemmProblem, og.Int8Operand
+        bad = [
+            lambda: gemm.encode_int32(enc, P(9, 9, 9), a, b, c),
+            lambda: gemm.encode_int32(enc, P(-1, 2, 2), a, b, c),
+            lambda: gemm.encode_int32(enc, P(2, 2, 2, batch=0), a, b, c),
+            lambda: gemm.encode_int32(enc, P(2, 2, 2, lda=1), a, b, c),
+            lambda: gemm.encode_int32(enc, P(2, 2, 2, offset_c=62), a, b, c),
+            lambda: gemm.encode_int32(enc, P(8, 8, 8, offset_a=1), a, b, c),
+            lambda: gemm.encode_int32(enc, P(2, 2, 2), a, b, c, Op(a, 63, True)),
+            lambda: gemm.encode_int32(enc, P(2, 2, 2), f, b, c),
+            lambda: gemm.encode_float(enc, P(2, 8, 2), a, b, f, Op(fl, 0, True)),
+            lambda: gemm.encode_requantized(enc, P(2, 2, 2), a, b, a, Op(fl, 0), 300),
+            lambda: gemm.encode_requantized(enc, P(2, 2, 2), a, b, b, Op(fl, 0), 128),
+        ]
+        for fn in bad:
+            with pytest.raises(og.GpuKernelShapeException):
+                fn()
+        assert enc.dispatch_count == 0
+        with pytest.raises(og.ArgumentNullException):
+            gemm.encode_int32(None, P(2, 2, 2), a, b, c)
+        device.submit(enc)
+        device.wait_idle()
+        for v in (a, b, c, f, fl):
+            v.dispose()
+
+
+def test_a_caller_sized_scratch_and_reserved_scratch(device):
+    """Int8ScratchTests.cs:27-66: caller-placed and reserved scratch; CUDA builds no bind groups at all."""
+    N, K, small, large = 96, 64, 32, 160
+    a = device.create_buffer(np.uint8, oracle.bytes_(large * K + 4, 1))
+    b = device.create_buffer(np.int8, np.zeros(N * K + 4, np.int8))
+    y = device.create_buffer(np.uint8, large * N + 4)
+    mult = device.create_buffer(np.float32, np.array([0.001], np.float32))
+    need = og.Int8Gemm.scratch_elements(og.Int8GemmProblem(large, N, K))
+    assert need == large * N
+    scratch = device.create_buffer(np.int32, need)
+    for reserve, caller in ((False, True), (True, False), (False, False)):
+        with og.Int8Gemm(device) as gemm:
+            if reserve:
+                gemm.reserve_scratch(need)
+            for m in (small, large):
+                enc = device.begin_commands()
+                gemm.encode_requantized(enc, og.Int8GemmProblem(m, N, K), a, b, y, og.Int8Operand(mult, 0), 3,
+                                        scratch=og.Int8Scratch(scratch) if caller else None)
+                device.submit(enc)
+            got = y.read()[:large * N]
+            assert np.all(got == 3)  # B is all zero, so every output is the zero point
+            assert gemm.bind_groups_created == 0
+    with og.Int8Gemm(device) as gemm:
+        with pytest.raises(og.ArgumentOutOfRangeException):
+            gemm.reserve_scratch(-1)
+        with pytest.raises(og.GpuKernelShapeException) as e:
+            gemm.encode_requantized(device.begin_commands(), og.Int8GemmProblem(64, 64, 8), a, b, y,
+                                    og.Int8Operand(mult, 0), 0, scratch=og.Int8Scratch(scratch, need - 100))
+        assert e.value.argument == "scratch"
+    for v in (a, b, y, mult, scratch):
+        v.dispose()
+
+
+def test_multi_device_known_answer():
+    """MultiDeviceTests.cs:6-107: every visible device computes the 2 x 3 x 2 known answer, interleaved."""
+    n = og.device_count()
+    devices = [og.GpuDevice(i) for i in range(n)]
+    try:
+        gemms = [og.Int8Gemm(d) for d in devices]
+        kat = golden()["kat_multidevice"]
+        a = [d.create_buffer(np.uint8, np.array(kat["a_u8"], np.uint8)) for d in devices]
+        b = [d.create_buffer(np.int8, np.array(kat["b_s8"], np.int8)) for d in devices]
+        c = [d.create_buffer(np.int32, 6) for d in devices]
+        for _ in range(3):
+            for i, d in enumerate(devices):
+                enc = d.begin_commands()
+                gemms[i].encode_int32(enc, og.Int8GemmProblem(2, 3, 2), a[i], b[i], c[i])
+                d.submit(enc)
+        for i in range(n):
+            assert c[i].read().tolist() == kat["expected"]
+        for i in range(n):
+            for v in (a[i], b[i], c[i]):
+                v.dispose()
+            gemms[i].dispose()
+    finally:
+        for d in devices:
+            d.dispose()
+
+
+def test_products_wider_than_one_grid_axis(device):
+    """ConvIntegerTests.cs:343-392: products with millions of columns or rows (k = 5)."""
+    for (m, n) in ((3, 4_300_001), (4_300_001, 3), (2, 4_194_241)):
+        c = Case(f"{m}x{n}", problem(m, n, 5), False, True, 1, 2)
+        for name, gemm in configs(device)[:2]:
+            with gemm:
+                bad, _ = run_int32(device, gemm, c, 11)
+                assert bad == 0, f"{m}x{n} [{name}]"
+
+
+def test_tensor_core_sums_wrap_modulo_2_32(device):
+    """The definition wraps modulo 2^32 (Int8Gemm.cs:103-105): 255 * 255 * K passes 2^32 at K = 66560."""
+    m, n, k = 130, 144, 66560
+    c = Case("wrap", problem(m, n, k), False, False, 1, 2)
+    a = np.full(m * k + 4, 255, np.uint8)
+    b = np.full(k * n + 4, 255, np.uint8)
+    za = np.zeros(1, np.uint8)
+    zb = np.ones(n + 1, np.uint8)
+    with og.Int8Gemm(device, og.Int8GemmOptions(kernel=og.KERNEL_TENSOR_CORE)) as gemm:
+        for zpa, zpb in ((None, None), (za, zb)):
+            cc = Case("wrap", c.p, False, False, 0 if zpa is None else 1, 0 if zpb is None else 2)
+            bad, kern = run_int32(device, gemm, cc, 3, data=(a, b, zpa, zpb))
+            assert kern == "tensor-core"
+            assert bad == 0

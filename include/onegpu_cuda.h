@@ -170,10 +170,13 @@ typedef enum og_int8_kernel {
     OG_KERNEL_PORTABLE = 2      /* the SIMT kernel */
 } og_int8_kernel;
 
-/* Int8GemmOptions (Int8Gemm.cs:7-21). allow_packed_dot = 0 forces the portable variant, as in the reference. */
+/* Int8GemmOptions (Int8Gemm.cs:7-21). allow_packed_dot = 0 forces the portable variant, as in the reference.
+ * tile is the test hook of Int8GemmOptions.Tile: 0 chooses by size, 128 forces the one-SM 128 x 256 tile, 256 the
+ * two-SM (CTA pair) 256 x 256 tile of the tensor-core kernel. */
 typedef struct og_int8_gemm_options {
     int32_t allow_packed_dot;
     int32_t kernel;
+    int32_t tile;
 } og_int8_gemm_options;
 
 /* new Int8Gemm(device, options) (Int8Gemm.cs:153-177). options may be NULL (defaults). */
@@ -182,7 +185,7 @@ OG_API og_status og_int8_gemm_create(og_device* device, const og_int8_gemm_optio
 OG_API og_status og_int8_gemm_destroy(og_int8_gemm* gemm);
 /* Int8Gemm.Variant (Int8Gemm.cs:215). */
 OG_API og_status og_int8_gemm_variant(og_int8_gemm* gemm, char* buffer, uint64_t capacity);
-/* The kernel the last encode call recorded ("tensor-core", "portable" or "none"); a diagnostic. */
+/* The kernel the last encode call recorded ("tensor-core-2sm", "tensor-core-1sm", "portable" or "none"). */
 OG_API og_status og_int8_gemm_last_kernel(og_int8_gemm* gemm, char* buffer, uint64_t capacity);
 /* Int8Gemm.ScratchElements (Int8Gemm.cs:531). */
 OG_API int64_t og_int8_gemm_scratch_elements(const og_int8_gemm_problem* problem);

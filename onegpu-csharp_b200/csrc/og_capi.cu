@@ -137,6 +137,7 @@ struct og_int8_gemm {
     og_device* device = nullptr;
     bool allow_dot = true;
     int kernel = OG_KERNEL_AUTO;
+    int tile = 0;
     std::string variant;
     std::string last = "none";
     std::vector<void*> scratch;  // int32 byte-sum buffers; older ones live until destroy (recorded work may name them)
@@ -393,6 +394,7 @@ og::GemmLaunch make_launch(og_int8_gemm* g, const og_int8_gemm_problem* p, const
     L.b_signed = b->type == OG_S8;
     L.num_sms = g->device->sm_count;
     L.error_flag = g->device->status;
+    L.tile = g->tile;
     og::Epilogue& e = L.epi;
     e.out_kind = out_kind;
     const int esize = out_kind == og::OUT_I32 || out_kind == og::OUT_F32 ? 4 : 1;
@@ -463,7 +465,7 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
         enc->ops.push_back([L, rows, cols](cudaStream_t s) { return og::launch_byte_sums(L, rows, cols, s); });
         enc->dispatches += 1;
     }
-    g->last = "tensor-core";
+    g->last = og::tc_cta_group(L) == 2 ? "tensor-core-2sm" : "tensor-core-1sm";
     enc->ops.push_back([L](cudaStream_t s) { return og::launch_gemm_tc(L, s); });
     enc->dispatches += 1;
 }
@@ -751,6 +753,11 @@ OG_API og_status og_int8_gemm_create(og_device* d, const og_int8_gemm_options* o
         g->device = d;
         g->allow_dot = options == nullptr || options->allow_packed_dot != 0;
         g->kernel = options == nullptr ? OG_KERNEL_AUTO : options->kernel;
+        g->tile = options == nullptr ? 0 : options->tile;
+        if (g->tile != 0 && g->tile != 128 && g->tile != 256) {
+            delete g;
+            throw OgError{OG_ERROR_ARGUMENT_RANGE, kGemm, "Tile", "the tile hook takes 0, 128 or 256", "", "", ""};
+        }
         const bool tc_hw = d->prop.major == 10 && d->prop.minor == 0;
         if (g->kernel == OG_KERNEL_TENSOR_CORE && (!tc_hw || !g->allow_dot)) {
             delete g;
@@ -758,8 +765,10 @@ OG_API og_status og_int8_gemm_create(og_device* d, const og_int8_gemm_options* o
                         "sm_" + std::to_string(d->prop.major) + std::to_string(d->prop.minor));
         }
         if (!tc_hw) g->allow_dot = false;
-        g->variant = g->allow_dot && g->kernel != OG_KERNEL_PORTABLE ? "tcgen05-i8-tile128x256x128"
-                                                                      : "portable-simt-tile64x64x32";
+        const char* tcv = g->tile == 128   ? "tcgen05-i8-1sm-tile128x256x128"
+                          : g->tile == 256 ? "tcgen05-i8-2sm-tile256x256x128"
+                                           : "tcgen05-i8-2sm-tile256x256x128+1sm-tile128x256x128";
+        g->variant = g->allow_dot && g->kernel != OG_KERNEL_PORTABLE ? tcv : "portable-simt-tile64x64x32";
         *out = g;
     });
 }

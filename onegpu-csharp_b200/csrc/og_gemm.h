@@ -22,11 +22,13 @@ struct GemmLaunch {
     Epilogue epi;
     int num_sms;
     int* error_flag;
+    int tile;  // tensor-core tile rows: 0 chooses by size, 128 one CTA per tile, 256 a CTA pair (cta_group::2)
 };
 
 // tcgen05 product (og_gemm_tc.cu). Eligible when K >= 1 and both operands' rows and batches start on 16-byte
 // boundaries (the TMA requirement).
 bool tc_eligible(const GemmLaunch& L);
+int tc_cta_group(const GemmLaunch& L);  // 1 or 2: the tile launch_gemm_tc will use
 cudaError_t launch_gemm_tc(const GemmLaunch& L, cudaStream_t stream);
 
 // Portable SIMT product (og_gemm_simt.cu): any alignment, subtracts the zero points while staging, so it needs no

@@ -26,18 +26,26 @@
 namespace og {
 
 namespace tc {
-constexpr int BM = 128;
 constexpr int BN = 256;
-constexpr int BK = 128;  // bytes of K per stage = one 128-byte swizzle row
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK;           // 16 KB
-constexpr int B_BYTES = BN * BK;           // 32 KB
-constexpr int B_HALF = 128 * BK;           // one 128-column box of an MN-major B
+constexpr int BK = 128;                    // bytes of K per stage = one 128-byte swizzle row
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = NUM_ACC * BN;    // 512: all of TMEM
 constexpr int THREADS = 192;               // producer, MMA, 4 epilogue warps
-constexpr int GROUP_M = 8;                 // M tiles per raster group
-constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024 /* alignment */ + 256 /* barriers */;
+constexpr int GROUP_M = 8;                 // output tiles per raster group along M
+
+// CG = 1: one CTA computes a 128 x 256 tile. CG = 2: a CTA pair computes a 256 x 256 tile with tcgen05.mma
+// cta_group::2; each CTA stages its own 128 rows of A and its own 128 columns of B, so every SM pulls 32 KB per
+// K block instead of 48 KB.
+template <int CG>
+struct Cfg {
+    static constexpr int BM = 128 * CG;
+    static constexpr int A_BYTES = 128 * BK;          // 16 KB per CTA
+    static constexpr int B_COLS = BN / CG;            // columns of B staged by one CTA
+    static constexpr int B_BYTES = B_COLS * BK;       // 32 KB or 16 KB per CTA
+    static constexpr int B_BOX = 128 * BK;            // one 128-column box of an MN-major B
+    static constexpr int STAGES = CG == 1 ? 4 : 6;
+    static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024 /* alignment */ + 256 /* barriers */;
+};
 }  // namespace tc
 
 struct TcParams {
@@ -51,6 +59,7 @@ struct TcParams {
     int* error_flag;
 };
 
+template <int BM>
 __device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& b, int& tm, int& tn) {
     const int per_batch = p.tiles_m * p.tiles_n;
     b = tile / per_batch;
@@ -133,33 +142,37 @@ __device__ __forceinline__ void store_chunk(const Epilogue& e, const RowTerms& r
     }
 }
 
-template <bool B_MN, int OUT>
-__global__ void __launch_bounds__(tc::THREADS, 1)
-    int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                        const TcParams p, uint32_t idesc) {
+template <int CG, bool B_MN, int OUT>
+__device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const TcParams& p,
+                                             uint32_t idesc) {
+    using C = tc::Cfg<CG>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
-    uint8_t* sB = smem + tc::STAGES * tc::A_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + tc::STAGES * tc::B_BYTES);
+    uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
     uint64_t* full = bars;
-    uint64_t* empty = bars + tc::STAGES;
-    uint64_t* tfull = bars + 2 * tc::STAGES;
-    uint64_t* tempty = bars + 2 * tc::STAGES + tc::NUM_ACC;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * tc::STAGES + 2 * tc::NUM_ACC);
+    uint64_t* empty = bars + C::STAGES;
+    uint64_t* tfull = bars + 2 * C::STAGES;
+    uint64_t* tempty = bars + 2 * C::STAGES + tc::NUM_ACC;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 2 * tc::NUM_ACC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
+    const uint32_t rank = CG == 2 ? cluster_ctarank() : 0;  // CTA of the pair: rank 0 issues the MMAs
+    const bool leader = rank == 0;
+    const int worker = CG == 2 ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+    const int workers = CG == 2 ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < tc::STAGES; s++) {
+        for (int s = 0; s < C::STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < tc::NUM_ACC; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 4);
+            mbar_init(&tempty[a], 4 * CG);  // one arrival per epilogue warp of every CTA of the pair
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -169,87 +182,123 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
         prefetch_tmap(&tmap_b);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_holder, tc::TMEM_COLS);
-        tmem_relinquish();
+        if constexpr (CG == 2) {
+            tmem_alloc_pair(tmem_holder, tc::TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_holder, tc::TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync_all();  // the peer's barriers are initialised before any remote arrival
     tc_fence_after();
     const uint32_t tmem_base = *tmem_holder;
 
     if (warp == 0) {
         // TMA producer: the whole warp walks the ring, lane 0 issues.
         uint32_t it = 0;
-        for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x) {
+        for (int tile = worker; tile < p.total_tiles; tile += workers) {
             int b, tm, tn;
-            tile_coords(p, tile, b, tm, tn);
+            tile_coords<C::BM>(p, tile, b, tm, tn);
             const int ba = p.a_batched ? b : 0;
             const int bb = p.b_batched ? b : 0;
-            const bool second_half = B_MN && (tn * tc::BN + 128 < p.n);
-            const uint32_t bytes = tc::A_BYTES + (B_MN ? (second_half ? 2 : 1) * tc::B_HALF : tc::B_BYTES);
+            const int row0 = tm * C::BM + static_cast<int>(rank) * 128;
+            const int col0 = tn * tc::BN + static_cast<int>(rank) * C::B_COLS;
+            // With one CTA, a second 128-column box wholly past N is skipped; a pair always loads full boxes
+            // (TMA fills what lies outside the tensor with zeros) so the leader knows the byte count.
+            const bool second_half = CG == 1 && B_MN && (col0 + 128 < p.n);
+            const uint32_t bytes = CG == 2 ? 2u * (C::A_BYTES + C::B_BYTES)
+                                           : C::A_BYTES + (B_MN ? (second_half ? 2 : 1) * C::B_BOX : C::B_BYTES);
             for (int kb = 0; kb < p.k_blocks; kb++, it++) {
-                const int s = it % tc::STAGES;
-                const uint32_t ph = (it / tc::STAGES) & 1;
+                const int s = it % C::STAGES;
+                const uint32_t ph = (it / C::STAGES) & 1;
                 if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) goto done;
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&full[s], bytes);
-                    tma_load_3d(sA + s * tc::A_BYTES, &tmap_a, &full[s], kb * tc::BK, tm * tc::BM, ba);
-                    if constexpr (B_MN) {
-                        tma_load_3d(sB + s * tc::B_BYTES, &tmap_b, &full[s], tn * tc::BN, kb * tc::BK, bb);
-                        if (second_half)
-                            tma_load_3d(sB + s * tc::B_BYTES + tc::B_HALF, &tmap_b, &full[s], tn * tc::BN + 128,
-                                        kb * tc::BK, bb);
+                    if constexpr (CG == 2) {
+                        const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+                        if (leader) mbar_arrive_expect_tx(&full[s], bytes);
+                        tma_load_3d_pair(sA + s * C::A_BYTES, &tmap_a, bar, kb * tc::BK, row0, ba);
+                        if constexpr (B_MN)
+                            tma_load_3d_pair(sB + s * C::B_BYTES, &tmap_b, bar, col0, kb * tc::BK, bb);
+                        else
+                            tma_load_3d_pair(sB + s * C::B_BYTES, &tmap_b, bar, kb * tc::BK, col0, bb);
                     } else {
-                        tma_load_3d(sB + s * tc::B_BYTES, &tmap_b, &full[s], kb * tc::BK, tn * tc::BN, bb);
+                        mbar_arrive_expect_tx(&full[s], bytes);
+                        tma_load_3d(sA + s * C::A_BYTES, &tmap_a, &full[s], kb * tc::BK, row0, ba);
+                        if constexpr (B_MN) {
+                            tma_load_3d(sB + s * C::B_BYTES, &tmap_b, &full[s], col0, kb * tc::BK, bb);
+                            if (second_half)
+                                tma_load_3d(sB + s * C::B_BYTES + C::B_BOX, &tmap_b, &full[s], col0 + 128,
+                                            kb * tc::BK, bb);
+                        } else {
+                            tma_load_3d(sB + s * C::B_BYTES, &tmap_b, &full[s], kb * tc::BK, col0, bb);
+                        }
                     }
                 }
                 __syncwarp();
             }
         }
     } else if (warp == 1) {
-        // MMA issuer: lane 0 issues four K=32 MMAs per stage into the accumulator of this tile.
-        uint32_t it = 0;
-        int lt = 0;
-        for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, lt++) {
-            const int acc = lt & 1;
-            const uint32_t aph = (lt >> 1) & 1;
-            if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) goto done;
-            tc_fence_after();
-            const uint32_t d_tmem = tmem_base + acc * tc::BN;
-            for (int kb = 0; kb < p.k_blocks; kb++, it++) {
-                const int s = it % tc::STAGES;
-                const uint32_t ph = (it / tc::STAGES) & 1;
-                if (!mbar_wait(&full[s], ph, abort_flag)) goto done;
+        // MMA issuer (the leader CTA of a pair issues for both): four K = 32 MMAs per stage.
+        if (leader) {
+            uint32_t it = 0;
+            int lt = 0;
+            for (int tile = worker; tile < p.total_tiles; tile += workers, lt++) {
+                const int acc = lt & 1;
+                const uint32_t aph = (lt >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) goto done;
                 tc_fence_after();
-                if (lane == 0) {
-                    const uint32_t a_addr = smem_u32(sA + s * tc::A_BYTES);
-                    const uint32_t b_addr = smem_u32(sB + s * tc::B_BYTES);
+                const uint32_t d_tmem = tmem_base + acc * tc::BN;
+                for (int kb = 0; kb < p.k_blocks; kb++, it++) {
+                    const int s = it % C::STAGES;
+                    const uint32_t ph = (it / C::STAGES) & 1;
+                    if (!mbar_wait(&full[s], ph, abort_flag)) goto done;
+                    tc_fence_after();
+                    if (lane == 0) {
+                        const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
+                        const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < tc::BK / 32; kk++) {
-                        const uint64_t adesc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
-                        const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + kk * 32 * 128, tc::B_HALF, 1024)
-                                                    : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-                        mma_i8(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+                        for (int kk = 0; kk < tc::BK / 32; kk++) {
+                            const uint64_t adesc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
+                            const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + kk * 32 * 128, C::B_BOX, 1024)
+                                                        : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
+                            const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
+                            if constexpr (CG == 2)
+                                mma_i8_pair(d_tmem, adesc, bdesc, idesc, accum);
+                            else
+                                mma_i8(d_tmem, adesc, bdesc, idesc, accum);
+                        }
+                        if constexpr (CG == 2)
+                            mma_commit_pair(&empty[s], 0x3);
+                        else
+                            mma_commit(&empty[s]);
                     }
-                    mma_commit(&empty[s]);
+                    __syncwarp();
+                }
+                if (lane == 0) {
+                    if constexpr (CG == 2)
+                        mma_commit_pair(&tfull[acc], 0x3);
+                    else
+                        mma_commit(&tfull[acc]);
                 }
                 __syncwarp();
             }
-            if (lane == 0) mma_commit(&tfull[acc]);
-            __syncwarp();
         }
     } else {
-        // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, i.e. rows 32*(w%4) + lane of the tile.
+        // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, i.e. rows 32*(w%4) + lane of this CTA's 128 rows.
         const int q = warp & 3;
+        const uint32_t tempty_leader = CG == 2 ? mapa_shared(smem_u32(&tempty[0]), 0) : 0;
         int lt = 0;
-        for (int tile = blockIdx.x; tile < p.total_tiles; tile += gridDim.x, lt++) {
+        for (int tile = worker; tile < p.total_tiles; tile += workers, lt++) {
             int b, tm, tn;
-            tile_coords(p, tile, b, tm, tn);
+            tile_coords<C::BM>(p, tile, b, tm, tn);
             const int acc = lt & 1;
             const uint32_t aph = (lt >> 1) & 1;
             if (!mbar_wait(&tfull[acc], aph, abort_flag)) goto done;
             tc_fence_after();
-            const int m = tm * tc::BM + q * 32 + lane;
+            const int m = tm * C::BM + static_cast<int>(rank) * 128 + q * 32 + lane;
             const bool row_ok = m < p.m;
             const RowTerms rt = row_ok ? row_terms(p.epi, b, m) : RowTerms{0, 0};
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * tc::BN;
@@ -264,17 +313,40 @@ __global__ void __launch_bounds__(tc::THREADS, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[acc]);
+            if (lane == 0) {
+                if constexpr (CG == 2)
+                    mbar_arrive_cluster(tempty_leader + acc * sizeof(uint64_t));
+                else
+                    mbar_arrive(&tempty[acc]);
+            }
         }
     }
 
 done:
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync_all();  // neither CTA frees the pair's TMEM while the other still reads it
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, tc::TMEM_COLS);
+        if constexpr (CG == 2)
+            tmem_dealloc_pair(tmem_base, tc::TMEM_COLS);
+        else
+            tmem_dealloc(tmem_base, tc::TMEM_COLS);
     }
     if (threadIdx.x == 0 && *abort_flag) atomicExch(p.error_flag, 1);
+}
+
+template <bool B_MN, int OUT>
+__global__ void __launch_bounds__(tc::THREADS, 1)
+    int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        const TcParams p, uint32_t idesc) {
+    gemm_tc_body<1, B_MN, OUT>(tmap_a, tmap_b, p, idesc);
+}
+
+template <bool B_MN, int OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::THREADS, 1)
+    int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                         const TcParams p, uint32_t idesc) {
+    gemm_tc_body<2, B_MN, OUT>(tmap_a, tmap_b, p, idesc);
 }
 
 // ---- host side ---------------------------------------------------------------------------------------------------
@@ -317,35 +389,52 @@ bool tc_eligible(const GemmLaunch& L) {
     return true;
 }
 
-template <bool B_MN, int OUT>
-static cudaError_t launch_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensorMap& ma, const CUtensorMap& mb,
-                               int grid, cudaStream_t stream) {
-    auto kern = int8_gemm_tc_kernel<B_MN, OUT>;
-    static uint64_t configured = 0;  // one bit per device ordinal: the attribute is per device
+// Sets the kernel's dynamic shared-memory limit once per device (the attribute is per device).
+template <class K>
+static cudaError_t configure(K kern, int smem, uint64_t& configured) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     const uint64_t bit = uint64_t(1) << (dev & 63);
     if (!(configured & bit)) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_BYTES);
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         configured |= bit;
     }
-    const uint32_t idesc = idesc_i8(L.a_signed, L.b_signed, false, B_MN, tc::BM, tc::BN);
-    kern<<<grid, tc::THREADS, tc::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
+    return cudaSuccess;
+}
+
+template <int CG, bool B_MN, int OUT>
+static cudaError_t launch_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensorMap& ma, const CUtensorMap& mb,
+                               int grid, cudaStream_t stream) {
+    using C = tc::Cfg<CG>;
+    static uint64_t configured = 0;
+    const uint32_t idesc = idesc_i8(L.a_signed, L.b_signed, false, B_MN, C::BM, tc::BN);
+    if constexpr (CG == 2) {
+        auto kern = int8_gemm_tc2_kernel<B_MN, OUT>;
+        cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
+        if (e != cudaSuccess) return e;
+        kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
+    } else {
+        auto kern = int8_gemm_tc_kernel<B_MN, OUT>;
+        cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
+        if (e != cudaSuccess) return e;
+        kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
+    }
     return cudaGetLastError();
 }
 
-cudaError_t launch_gemm_tc(const GemmLaunch& L, cudaStream_t stream) {
+template <int CG>
+static cudaError_t launch_cg(const GemmLaunch& L, cudaStream_t stream) {
+    using C = tc::Cfg<CG>;
     const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
     const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
     CUtensorMap ma, mb;
-    if (!make_map(&ma, L.a, L.k, L.m, ba, L.lda, ba > 1 ? L.stride_a : round16(uint64_t(L.lda) * L.m), tc::BK,
-                  tc::BM))
+    if (!make_map(&ma, L.a, L.k, L.m, ba, L.lda, ba > 1 ? L.stride_a : round16(uint64_t(L.lda) * L.m), tc::BK, 128))
         return cudaErrorInvalidValue;
     const uint64_t rows_b = L.trans_b ? L.n : L.k;
     const uint64_t sb = bb > 1 ? uint64_t(L.stride_b) : round16(uint64_t(L.ldb) * rows_b);
-    const bool ok = L.trans_b ? make_map(&mb, L.b, L.k, L.n, bb, L.ldb, sb, tc::BK, tc::BN)
+    const bool ok = L.trans_b ? make_map(&mb, L.b, L.k, L.n, bb, L.ldb, sb, tc::BK, C::B_COLS)
                               : make_map(&mb, L.b, L.n, L.k, bb, L.ldb, sb, 128, tc::BK);
     if (!ok) return cudaErrorInvalidValue;
 
@@ -353,7 +442,7 @@ cudaError_t launch_gemm_tc(const GemmLaunch& L, cudaStream_t stream) {
     p.m = L.m;
     p.n = L.n;
     p.k = L.k;
-    p.tiles_m = (L.m + tc::BM - 1) / tc::BM;
+    p.tiles_m = (L.m + C::BM - 1) / C::BM;
     p.tiles_n = (L.n + tc::BN - 1) / tc::BN;
     p.batch = L.batch;
     p.a_batched = ba > 1;
@@ -363,18 +452,32 @@ cudaError_t launch_gemm_tc(const GemmLaunch& L, cudaStream_t stream) {
     p.total_tiles = static_cast<int>(total);
     p.epi = L.epi;
     p.error_flag = L.error_flag;
-    const int grid = static_cast<int>(total < L.num_sms ? total : L.num_sms);
+    const int64_t workers = L.num_sms / CG;
+    const int grid = static_cast<int>((total < workers ? total : workers) * CG);
     const bool bmn = !L.trans_b;
     switch (L.epi.out_kind) {
-        case OUT_I32: return bmn ? launch_tc_t<true, OUT_I32>(L, p, ma, mb, grid, stream)
-                                 : launch_tc_t<false, OUT_I32>(L, p, ma, mb, grid, stream);
-        case OUT_F32: return bmn ? launch_tc_t<true, OUT_F32>(L, p, ma, mb, grid, stream)
-                                 : launch_tc_t<false, OUT_F32>(L, p, ma, mb, grid, stream);
-        case OUT_U8: return bmn ? launch_tc_t<true, OUT_U8>(L, p, ma, mb, grid, stream)
-                                : launch_tc_t<false, OUT_U8>(L, p, ma, mb, grid, stream);
-        default: return bmn ? launch_tc_t<true, OUT_S8>(L, p, ma, mb, grid, stream)
-                            : launch_tc_t<false, OUT_S8>(L, p, ma, mb, grid, stream);
+        case OUT_I32: return bmn ? launch_tc_t<CG, true, OUT_I32>(L, p, ma, mb, grid, stream)
+                                 : launch_tc_t<CG, false, OUT_I32>(L, p, ma, mb, grid, stream);
+        case OUT_F32: return bmn ? launch_tc_t<CG, true, OUT_F32>(L, p, ma, mb, grid, stream)
+                                 : launch_tc_t<CG, false, OUT_F32>(L, p, ma, mb, grid, stream);
+        case OUT_U8: return bmn ? launch_tc_t<CG, true, OUT_U8>(L, p, ma, mb, grid, stream)
+                                : launch_tc_t<CG, false, OUT_U8>(L, p, ma, mb, grid, stream);
+        default: return bmn ? launch_tc_t<CG, true, OUT_S8>(L, p, ma, mb, grid, stream)
+                            : launch_tc_t<CG, false, OUT_S8>(L, p, ma, mb, grid, stream);
     }
+}
+
+int tc_cta_group(const GemmLaunch& L) {
+    if (L.tile == 128) return 1;
+    if (L.tile == 256) return 2;
+    // The pair tile halves the operand bytes each SM pulls from L2 per MMA; use it once there are enough 256-row
+    // tiles to give most SM pairs work.
+    const int64_t pair_tiles = int64_t((L.m + 255) / 256) * ((L.n + 255) / 256) * L.batch;
+    return (L.m > 128 && pair_tiles * 4 >= int64_t(L.num_sms / 2) * 3) ? 2 : 1;
+}
+
+cudaError_t launch_gemm_tc(const GemmLaunch& L, cudaStream_t stream) {
+    return tc_cta_group(L) == 2 ? launch_cg<2>(L, stream) : launch_cg<1>(L, stream);
 }
 
 }  // namespace og

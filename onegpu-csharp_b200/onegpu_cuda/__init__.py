@@ -74,7 +74,7 @@ class og_int8_gemm_problem(ctypes.Structure):
 
 
 class og_int8_gemm_options(ctypes.Structure):
-    _fields_ = [("allow_packed_dot", ctypes.c_int32), ("kernel", ctypes.c_int32)]
+    _fields_ = [("allow_packed_dot", ctypes.c_int32), ("kernel", ctypes.c_int32), ("tile", ctypes.c_int32)]
 
 
 _P = ctypes.c_void_p
@@ -431,9 +431,11 @@ class Int8Scratch:
 
 @dataclass
 class Int8GemmOptions:
-    """Int8GemmOptions (Int8Gemm.cs:7-21); `kernel` is the test hook (KERNEL_AUTO / _TENSOR_CORE / _PORTABLE)."""
+    """Int8GemmOptions (Int8Gemm.cs:7-21); `kernel` (KERNEL_AUTO / _TENSOR_CORE / _PORTABLE) and `tile` (0, 128 or
+    256 rows per tensor-core tile) are test hooks like the reference's internal Tile."""
     allow_packed_dot: bool = True
     kernel: int = KERNEL_AUTO
+    tile: int = 0
 
 
 def _buf(b: Optional[GpuBuffer]):
@@ -452,7 +454,8 @@ class Int8Gemm:
         h = ctypes.c_void_p()
         opt = None
         if options is not None:
-            opt = ctypes.byref(og_int8_gemm_options(int(bool(options.allow_packed_dot)), int(options.kernel)))
+            opt = ctypes.byref(og_int8_gemm_options(int(bool(options.allow_packed_dot)), int(options.kernel),
+                                                    int(options.tile)))
         _check(_lib.og_int8_gemm_create(device.handle, opt, ctypes.byref(h)))
         self.handle = h.value
 

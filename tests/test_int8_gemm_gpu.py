@@ -17,10 +17,18 @@ from gpu_rig import SENTINEL, align_case, run_int32, typed
 pytestmark = pytest.mark.gpu
 
 
-def configs(device):
-    return [("default", og.Int8Gemm(device)),
-            ("portable", og.Int8Gemm(device, og.Int8GemmOptions(allow_packed_dot=False))),
-            ("tensor-core", og.Int8Gemm(device, og.Int8GemmOptions(kernel=og.KERNEL_TENSOR_CORE)))]
+CONFIGS = {
+    "default": og.Int8GemmOptions(),
+    "portable": og.Int8GemmOptions(allow_packed_dot=False),
+    "tensor-core-1sm": og.Int8GemmOptions(kernel=og.KERNEL_TENSOR_CORE, tile=128),
+    "tensor-core-2sm": og.Int8GemmOptions(kernel=og.KERNEL_TENSOR_CORE, tile=256),
+}
+
+
+def configs(device, names=None):
+    """Every way the product can run: as chosen, the portable kernel, and each tensor-core tile forced (the
+    reference's Configs, Int8Tests.cs:24-34)."""
+    return [(n, og.Int8Gemm(device, CONFIGS[n])) for n in (names or CONFIGS)]
 
 
 def test_edge_shapes_are_bit_exact(device):
@@ -29,18 +37,17 @@ def test_edge_shapes_are_bit_exact(device):
     total = {}
     for name, gemm in configs(device):
         with gemm:
-            bad = 0
             kernels = set()
             for seed, c in enumerate(cases + aligned, start=1):
-                if name == "tensor-core" and (c.p["k"] == 0 or "aligned" not in c.name):
+                if name.startswith("tensor-core") and (c.p["k"] == 0 or "aligned" not in c.name):
                     continue
                 b, k = run_int32(device, gemm, c, seed)
                 kernels.add(k)
                 assert b == 0, f"[{name}] {c.name} signed {c.a_signed}/{c.b_signed} zp {c.za_mode}/{c.zb_mode}"
-                bad += b
             total[name] = kernels
     assert total["portable"] == {"portable"}
-    assert total["tensor-core"] == {"tensor-core"}
+    assert total["tensor-core-1sm"] == {"tensor-core-1sm"}
+    assert total["tensor-core-2sm"] == {"tensor-core-2sm"}
 
 
 def test_model_shapes_are_bit_exact(device):
@@ -133,10 +140,10 @@ def requant_case(device, gemm, m, n, k, mult_vec, unsigned, zero_y, with_bias, s
     return bad
 
 
-@pytest.mark.parametrize("cfg", ["default", "portable", "tensor-core"])
+@pytest.mark.parametrize("cfg", list(CONFIGS))
 def test_float_and_requantized_forms_are_bit_exact(device, cfg):
-    gemm = dict(configs(device))[cfg]
-    aligned = cfg == "tensor-core"
+    gemm = og.Int8Gemm(device, CONFIGS[cfg])
+    aligned = cfg.startswith("tensor-core")
     with gemm:
         bad_f = bad_q = 0
         seed = 10
@@ -154,12 +161,12 @@ def test_float_and_requantized_forms_are_bit_exact(device, cfg):
         assert bad_f == 0 and bad_q == 0
 
 
-@pytest.mark.parametrize("cfg", ["default", "tensor-core"])
+@pytest.mark.parametrize("cfg", list(CONFIGS))
 def test_requantization_rounds_half_to_even_and_saturates(device, cfg):
     """Int8Tests.cs:503-547: a 1 x 1 product of K = 1 puts ties, saturation, NaN and infinity through the epilogue
-    (for the tensor-core kernel the product is padded to 16 x 16 x 16 with zeros)."""
-    gemm = dict(configs(device))[cfg]
-    pad = 16 if cfg == "tensor-core" else 1
+    (for the tensor-core kernels the product is padded to 16 x 16 x 16 with zeros)."""
+    gemm = og.Int8Gemm(device, CONFIGS[cfg])
+    pad = 16 if cfg.startswith("tensor-core") else 1
     with gemm:
         for c in golden()["tables"]["requant_ties"]["cases"]:
             a = np.zeros(pad * pad + 4, np.int8)
@@ -279,23 +286,80 @@ def test_products_wider_than_one_grid_axis(device):
     """ConvIntegerTests.cs:343-392: products with millions of columns or rows (k = 5)."""
     for (m, n) in ((3, 4_300_001), (4_300_001, 3), (2, 4_194_241)):
         c = Case(f"{m}x{n}", problem(m, n, 5), False, True, 1, 2)
-        for name, gemm in configs(device)[:2]:
+        for name, gemm in configs(device, ["default", "portable"]):
             with gemm:
                 bad, _ = run_int32(device, gemm, c, 11)
                 assert bad == 0, f"{m}x{n} [{name}]"
 
 
-def test_tensor_core_sums_wrap_modulo_2_32(device):
+@pytest.mark.parametrize("cfg", ["tensor-core-1sm", "tensor-core-2sm"])
+def test_tensor_core_sums_wrap_modulo_2_32(device, cfg):
     """The definition wraps modulo 2^32 (Int8Gemm.cs:103-105): 255 * 255 * K passes 2^32 at K = 66560."""
-    m, n, k = 130, 144, 66560
+    m, n, k = 300, 144, 66560
     c = Case("wrap", problem(m, n, k), False, False, 1, 2)
     a = np.full(m * k + 4, 255, np.uint8)
     b = np.full(k * n + 4, 255, np.uint8)
     za = np.zeros(1, np.uint8)
     zb = np.ones(n + 1, np.uint8)
-    with og.Int8Gemm(device, og.Int8GemmOptions(kernel=og.KERNEL_TENSOR_CORE)) as gemm:
+    with og.Int8Gemm(device, CONFIGS[cfg]) as gemm:
         for zpa, zpb in ((None, None), (za, zb)):
             cc = Case("wrap", c.p, False, False, 0 if zpa is None else 1, 0 if zpb is None else 2)
             bad, kern = run_int32(device, gemm, cc, 3, data=(a, b, zpa, zpb))
-            assert kern == "tensor-core"
+            assert kern == cfg
             assert bad == 0
+
+
+def full_size_check(device, gemm, m, n, k, batch, a_signed, zp, trans_b=False, sample_rows=24, seed=77):
+    """A product at a config's full size, checked without a full CPU reference: every column sum and row sum of C
+    against (1^T A') B' and A' (B' 1) computed exactly on the host (A' = A - za, B' = B - zb, all modulo 2^32), and
+    a sample of whole rows against the oracle."""
+    rng = np.random.default_rng(seed)
+    a_dt = np.int8 if a_signed else np.uint8
+    a = rng.integers(-128 if a_signed else 0, 128 if a_signed else 256, size=batch * m * k, dtype=np.int16).astype(a_dt)
+    b = rng.integers(-127, 128, size=k * n, dtype=np.int16).astype(np.int8)
+    za = np.array([128 if not a_signed else 3], a_dt) if zp else None
+    zb = rng.integers(-8, 9, size=n).astype(np.int8) if zp else None
+    p = og.Int8GemmProblem(m, n, k, batch=batch, transpose_b=trans_b, stride_a=m * k if batch > 1 else 0)
+    bufs = [device.create_buffer(a_dt, a), device.create_buffer(np.int8, b), device.create_buffer(np.int32, batch * m * n)]
+    zpa = zpb = None
+    if zp:
+        bufs += [device.create_buffer(a_dt, za), device.create_buffer(np.int8, zb)]
+        zpa, zpb = og.Int8Operand(bufs[3], 0), og.Int8Operand(bufs[4], 0, True)
+    enc = device.begin_commands()
+    gemm.encode_int32(enc, p, bufs[0], bufs[1], bufs[2], zpa, zpb)
+    kern = gemm.last_kernel
+    device.submit(enc)
+    c = bufs[2].read().reshape(batch, m, n)
+    for v in bufs:
+        v.dispose()
+    a64 = a.reshape(batch, m, k).astype(np.int64) - (int(za[0]) if zp else 0)
+    b64 = b.reshape(n, k).T.astype(np.int64) if trans_b else b.reshape(k, n).astype(np.int64)
+    b64 = b64 - (zb.astype(np.int64)[None, :] if zp else 0)
+    wrap = lambda x: ((x + 2 ** 31) % 2 ** 32 - 2 ** 31)
+    c64 = c.astype(np.int64)
+    for bt in range(batch):
+        col_want = wrap(a64[bt].sum(axis=0) @ b64)           # (1^T A') B'
+        row_want = wrap(a64[bt] @ b64.sum(axis=1))           # A' (B' 1)
+        assert np.array_equal(wrap(c64[bt].sum(axis=0)), col_want), f"column sums of batch {bt} [{kern}]"
+        assert np.array_equal(wrap(c64[bt].sum(axis=1)), row_want), f"row sums of batch {bt} [{kern}]"
+    rows = rng.choice(m, size=min(sample_rows, m), replace=False)
+    bt = batch - 1
+    a_rows = a.reshape(batch, m, k)[bt][rows].view(np.uint8)
+    want = oracle.int8_gemm(a_rows, a_signed, b.view(np.uint8), True, None if za is None else za.view(np.uint8),
+                            False, None if zb is None else zb.view(np.uint8), True, m=len(rows), n=n, k=k,
+                            transpose_b=trans_b)
+    assert np.array_equal(c[bt][rows].reshape(-1), want), f"sampled rows [{kern}]"
+    return kern
+
+
+@pytest.mark.parametrize("workload", ["c3", "c2", "c4", "c5", "c3-transposed"])
+def test_config_sizes_checksums_and_sampled_rows(device, workload):
+    """BASELINE.json's configs at full size: 8192^3 s8 x s8, 4096^3 u8 x s8 with zero points, the batched QKV
+    projection 8 x 2048 x 12288 x 4096, the decode shape 16 x 28672 x 8192, and 8192^3 with B stored N x K."""
+    shapes = {"c3": (8192, 8192, 8192, 1, True, False, False), "c2": (4096, 4096, 4096, 1, False, True, False),
+              "c4": (2048, 12288, 4096, 8, False, True, False), "c5": (16, 28672, 8192, 1, False, True, False),
+              "c3-transposed": (8192, 8192, 8192, 1, True, False, True)}
+    m, n, k, batch, a_signed, zp, trans_b = shapes[workload]
+    with og.Int8Gemm(device) as gemm:
+        kern = full_size_check(device, gemm, m, n, k, batch, a_signed, zp, trans_b)
+        assert kern.startswith("tensor-core")

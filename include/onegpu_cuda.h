@@ -214,6 +214,22 @@ OG_API og_status og_int8_gemm_encode_requantized(og_int8_gemm* gemm, og_encoder*
                                                  const og_operand* zero_point_b, const og_operand* int_bias,
                                                  const og_operand* scratch);
 
+/* EncodeInt32 for callers that cannot allocate device memory. No counterpart in the reference.
+ * Some callers cannot call cudaMalloc: code recording work while a CUDA graph is captured in the global capture mode
+ * (where cudaMalloc is not permitted), and hosts that give all device memory to their own pool. Int8Gemm allocates
+ * the scratch of the zero-point byte sums on demand; this entry point allocates nothing (no cudaMalloc, no cudaFree)
+ * and keeps those sums in a fixed array of the library instead: at most 1,048,576 int32 (4 MiB, held on every GPU that
+ * loads the library until exit), i.e. batchA * M (when B has a zero point) + batchB * N (when A has one); a product
+ * needing more is refused with OG_ERROR_UNSUPPORTED. It runs the product on `stream` (a cudaStream_t, NULL for the
+ * default stream) of the current device, after the same checks as og_int8_gemm_encode_int32 and with the same
+ * kernels, and returns once the work is queued (a kernel-side watchdog failure is not reported here).
+ * The first call on a device looks up the array's device address and sets the kernels' shared-memory limit: make that
+ * first call before any stream capture. All calls share the array and it keeps the last call's contents (what must
+ * start at zero is cleared on the stream before use); calls whose work overlaps on the GPU race on it. */
+OG_API og_status og_int8_gemm_int32_noalloc(void* stream, const og_int8_gemm_problem* problem, const og_buffer* a,
+                                            const og_buffer* b, const og_buffer* c, const og_operand* zero_point_a,
+                                            const og_operand* zero_point_b, const og_operand* bias);
+
 /* The argument checks of the three forms alone (no device needed): the same checks, in the same order, that the
  * encode functions run before recording (Int8Gemm.cs:230-253, 270-314, 336-363, 419-501). */
 OG_API og_status og_int8_gemm_check_int32(const og_int8_gemm_problem* problem, const og_buffer* a, const og_buffer* b,

@@ -960,3 +960,130 @@ OG_API og_status og_dynamic_quantize_encode(og_dynamic_quantize* q, og_encoder* 
 }
 
 }  // extern "C"
+
+// ---- EncodeInt32 without allocation ---------------------------------------------------------------------------------
+//
+// Some callers cannot call cudaMalloc: code that records its work while a CUDA graph is being captured in the global
+// capture mode (where cudaMalloc is not permitted), and hosts that hand all device memory to their own pool and forbid
+// any other allocation. Int8Gemm allocates (and grows) the scratch of the byte sums that the zero-point correction
+// needs on its first products, so such callers get og_int8_gemm_int32_noalloc instead: the same product, the same
+// checks, the same kernels, with the byte sums kept in a fixed array of device memory that is part of this library.
+//
+// The array holds at most kNoAllocSumElements int32 sums (row sums of A for every batch of A when B has a zero point,
+// plus column sums of B for every batch of B when A has one); larger requests are refused. Every GPU that loads the
+// library keeps the array (4 MiB) until the process exits. All calls share it and it keeps the last call's contents:
+// the column sums, which are accumulated with atomics, are cleared on the stream before each use, and calls whose
+// work overlaps on the GPU (different streams, no ordering between them) race on it.
+
+namespace {
+
+constexpr int64_t kNoAllocSumElements = int64_t(1) << 20;
+
+static __device__ __align__(256) int32_t g_noalloc_sums[kNoAllocSumElements];
+static __device__ __align__(256) int g_noalloc_status[64];
+
+struct NoAllocDevice {
+    bool ready = false;
+    int32_t* sums = nullptr;
+    int* status = nullptr;
+    int sm_count = 0;
+};
+
+NoAllocDevice g_noalloc[64];
+
+// The device addresses of the arrays for the current device, looked up on the first call on that device (host code
+// may not use the symbols as addresses: they name host-side stand-ins).
+const NoAllocDevice& noalloc_device() {
+    int dev = 0;
+    check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+    if (dev < 0 || dev >= 64)
+        unsupported(kGemm, "device ordinal out of range for the allocation-free entry point", "Device", "< 64",
+                    std::to_string(dev));
+    NoAllocDevice& d = g_noalloc[dev];
+    if (!d.ready) {
+        void* sums = nullptr;
+        void* status = nullptr;
+        check_cuda(cudaGetSymbolAddress(&sums, g_noalloc_sums), "cudaGetSymbolAddress");
+        check_cuda(cudaGetSymbolAddress(&status, g_noalloc_status), "cudaGetSymbolAddress");
+        check_cuda(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+        d.sums = static_cast<int32_t*>(sums);
+        d.status = static_cast<int*>(status);
+        d.ready = true;
+    }
+    return d;
+}
+
+}  // namespace
+
+extern "C" {
+
+OG_API og_status og_int8_gemm_int32_noalloc(void* stream, const og_int8_gemm_problem* p, const og_buffer* a,
+                                            const og_buffer* b, const og_buffer* c, const og_operand* za,
+                                            const og_operand* zb, const og_operand* bias) {
+    return guard([&] {
+        const Prepared pr = check_int32(p, a, b, c, za, zb, bias);
+        if (!pr.ok) return;
+        const NoAllocDevice& d = noalloc_device();
+        og::GemmLaunch L = {};
+        L.a = static_cast<const uint8_t*>(a->ptr) + p->offset_a;
+        L.b = static_cast<const uint8_t*>(b->ptr) + p->offset_b;
+        L.m = p->m;
+        L.n = p->n;
+        L.k = p->k;
+        L.batch = p->batch;
+        L.trans_b = p->transpose_b != 0;
+        L.lda = pr.lda;
+        L.ldb = pr.ldb;
+        L.stride_a = p->stride_a;
+        L.stride_b = p->stride_b;
+        L.a_signed = a->type == OG_S8;
+        L.b_signed = b->type == OG_S8;
+        L.num_sms = d.sm_count;
+        L.error_flag = d.status;
+        L.tile = 0;
+        og::Epilogue& e = L.epi;
+        e.out_kind = og::OUT_I32;
+        e.c = static_cast<int32_t*>(c->ptr) + p->offset_c;
+        e.ldc = p->n;
+        e.batch_stride_c = static_cast<int64_t>(p->m) * p->n;
+        e.m = p->m;
+        e.n = p->n;
+        e.k = p->k;
+        e.za = operand_ptr(za);
+        e.za_vector = za ? za->is_vector : 0;
+        e.za_signed = a->type == OG_S8;
+        e.zb = operand_ptr(zb);
+        e.zb_vector = zb ? zb->is_vector : 0;
+        e.zb_signed = b->type == OG_S8;
+        e.int_bias = reinterpret_cast<const int32_t*>(operand_ptr(bias));
+        e.vec_ok = ((reinterpret_cast<uintptr_t>(e.c) & 15) == 0) && ((static_cast<int64_t>(p->n) * 4) % 16 == 0);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        const bool tc = og::tc_eligible(L) && static_cast<int64_t>(L.m) * L.n * L.k >= (int64_t(1) << 16);
+        if (!tc) {
+            check_cuda(og::launch_gemm_simt(L, s), "og_int8_gemm_int32_noalloc");
+            return;
+        }
+        const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
+        const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
+        const int64_t rows = e.zb != nullptr ? int64_t(ba) * L.m : 0;
+        const int64_t cols = e.za != nullptr ? int64_t(bb) * L.n : 0;
+        if (rows + cols > kNoAllocSumElements)
+            unsupported(kGemm,
+                        "og_int8_gemm_int32_noalloc keeps the byte sums of the zero-point correction in a fixed array "
+                        "of " + std::to_string(kNoAllocSumElements) + " int32; this product needs " +
+                            std::to_string(rows + cols) + " (use og_int8_gemm_encode_int32, which allocates)",
+                        "NoAllocScratch", "at most " + std::to_string(kNoAllocSumElements) + " byte sums",
+                        std::to_string(rows + cols) + " byte sums");
+        if (rows + cols > 0) {
+            e.row_sum_a = rows ? d.sums : nullptr;
+            e.row_sum_a_stride = ba > 1 ? L.m : 0;
+            e.col_sum_b = cols ? d.sums + rows : nullptr;
+            e.col_sum_b_stride = bb > 1 ? L.n : 0;
+            check_cuda(og::launch_byte_sums(L, const_cast<int32_t*>(e.row_sum_a), const_cast<int32_t*>(e.col_sum_b), s),
+                       "og_int8_gemm_int32_noalloc");
+        }
+        check_cuda(og::launch_gemm_tc(L, s), "og_int8_gemm_int32_noalloc");
+    });
+}
+
+}  // extern "C"

@@ -119,6 +119,7 @@ EXPORTS = {
     "og_int8_gemm_encode_float": [_P, _P, _PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD, _OPD, _OPD],
     "og_int8_gemm_encode_requantized": [_P, _P, _PROB, _BUF, _BUF, _BUF, _OPD, ctypes.c_int32, _OPD, _OPD, _OPD,
                                         _OPD],
+    "og_int8_gemm_int32_noalloc": [_P, _PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD],
     "og_int8_gemm_check_int32": [_PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD],
     "og_int8_gemm_check_float": [_PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD, _OPD, _OPD],
     "og_int8_gemm_check_requantized": [_PROB, _BUF, _BUF, _BUF, _OPD, ctypes.c_int32, _OPD, _OPD, _OPD, _OPD],
@@ -547,6 +548,15 @@ class _BufferSpec:
 def buffer_spec(dtype, length: int, null: bool = False) -> _BufferSpec:
     """Describes a buffer of `length` elements of `dtype` for check_* (no allocation, no device)."""
     return _BufferSpec(dtype, length, 0 if null else 0x1000)
+
+
+def int8_gemm_int32_noalloc(stream: int, problem, a, b, c, zero_point_a=None, zero_point_b=None, bias=None) -> None:
+    """EncodeInt32 for callers that cannot allocate device memory (og_int8_gemm_int32_noalloc): queues the product on
+    `stream` of the current device, keeping the zero-point byte sums in the library's fixed array instead of
+    allocated scratch. No counterpart in the reference."""
+    p = problem.c_struct()
+    _check(_lib.og_int8_gemm_int32_noalloc(ctypes.c_void_p(stream), ctypes.byref(p), _buf(a), _buf(b), _buf(c),
+                                           _opd(zero_point_a), _opd(zero_point_b), _opd(bias)))
 
 
 def check_int32(problem, a, b, c, zero_point_a=None, zero_point_b=None, bias=None) -> None:

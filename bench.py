@@ -316,6 +316,9 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
     per_launch_s = statistics.mean(per_step_ns) * 1e-9
     shard_ops = 2.0 * B * M * shard_n * K
     achieved = shard_ops / per_launch_s / 1e12
+    # Bytes one launch must move at least: A, the B slab, C, and the zero-point / scale vectors.
+    algo_bytes = (a_host.nbytes + b_host.nbytes + count * np.dtype(out_dtype).itemsize
+                  + (shard_n + 1 if w["zp"] else 0) + (4 * shard_n if w["out"] == "f32" else 0))
     peaks = load_peaks()
     # A timed region of back-to-back launches longer than a second settles at the power-capped clock: compare with
     # the sustained figure then, with the burst figure for short runs.
@@ -343,6 +346,9 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
                          "frac": round(achieved / peak, 4), "traffic": profile_traffic(args.workload),
                          "peak_source": f"2 x {peaks['source']} dense bf16 {peak_kind} "
                                         f"({peak / 2.0} TF/s): the int8 dense rate is twice bf16 on B200"},
+            "hbm": {"algorithmic_bytes_per_launch": int(algo_bytes),
+                    "achieved_gbs": round(algo_bytes / per_launch_s / 1e9, 1), "peak_gbs": peaks["hbm_gbs"],
+                    "frac": round(algo_bytes / per_launch_s / 1e9 / peaks["hbm_gbs"], 4)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(total_ops / (e2e_ns / args.steps * 1e-9) / 1e12, 3), "unit": "TOPS",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},

@@ -442,6 +442,12 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
         enc->dispatches += 1;
         return;
     }
+    if (g->tile == 0 && og::rows_eligible(L)) {
+        g->last = "tensor-core-rows";
+        enc->ops.push_back([L](cudaStream_t s) { return og::launch_gemm_rows(L, s); });
+        enc->dispatches += 1;
+        return;
+    }
     const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
     const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
     const bool need_rows = L.epi.zb != nullptr;  // zb * rowsum(A)

@@ -1,6 +1,7 @@
 // Internal launch descriptions shared by the host layer (og_capi.cu) and the kernel files.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -30,6 +31,15 @@ struct GemmLaunch {
 bool tc_eligible(const GemmLaunch& L);
 int tc_cta_group(const GemmLaunch& L);  // 1 or 2: the tile launch_gemm_tc will use
 cudaError_t launch_gemm_tc(const GemmLaunch& L, cudaStream_t stream);
+
+// Few-rows product (og_gemm_rows.cu): M <= 16 per batch, TMA-loadable operands; streams B once and takes the column
+// sums of B from the same MMA, so it needs no byte-sum pass and no scratch.
+bool rows_eligible(const GemmLaunch& L);
+cudaError_t launch_gemm_rows(const GemmLaunch& L, cudaStream_t stream);
+
+// A 3-D byte tensor map (x innermost) with 128-byte swizzled box_x x box_y boxes (og_gemm_tc.cu).
+bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint64_t stride_y,
+                        uint64_t stride_z, uint32_t box_x, uint32_t box_y);
 
 // Portable SIMT product (og_gemm_simt.cu): any alignment, subtracts the zero points while staging, so it needs no
 // byte sums; its epilogue ignores row_sum_a / col_sum_b.

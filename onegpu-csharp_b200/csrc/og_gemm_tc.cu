@@ -378,6 +378,11 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y,
     return r == CUDA_SUCCESS;
 }
 
+bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint64_t stride_y,
+                        uint64_t stride_z, uint32_t box_x, uint32_t box_y) {
+    return make_map(map, base, x, y, z, stride_y, stride_z, box_x, box_y);
+}
+
 static uint64_t round16(uint64_t v) { return (v + 15) & ~uint64_t(15); }
 
 bool tc_eligible(const GemmLaunch& L) {

@@ -22,6 +22,7 @@ CONFIGS = {
     "portable": og.Int8GemmOptions(allow_packed_dot=False),
     "tensor-core-1sm": og.Int8GemmOptions(kernel=og.KERNEL_TENSOR_CORE, tile=128),
     "tensor-core-2sm": og.Int8GemmOptions(kernel=og.KERNEL_TENSOR_CORE, tile=256),
+    "tensor-core-auto": og.Int8GemmOptions(kernel=og.KERNEL_TENSOR_CORE),  # the few-rows kernel for M <= 16
 }
 
 
@@ -48,6 +49,7 @@ def test_edge_shapes_are_bit_exact(device):
     assert total["portable"] == {"portable"}
     assert total["tensor-core-1sm"] == {"tensor-core-1sm"}
     assert total["tensor-core-2sm"] == {"tensor-core-2sm"}
+    assert "tensor-core-rows" in total["tensor-core-auto"]
 
 
 def test_model_shapes_are_bit_exact(device):

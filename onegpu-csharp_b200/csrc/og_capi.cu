@@ -443,8 +443,11 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
         return;
     }
     if (g->tile == 0 && og::rows_eligible(L)) {
+        cudaError_t err;
+        og::LaunchFn fn = og::prepare_gemm_rows(L, &err);  // tensor maps built now, at record time
+        check_cuda(err, "Int8Gemm tensor maps");
         g->last = "tensor-core-rows";
-        enc->ops.push_back([L](cudaStream_t s) { return og::launch_gemm_rows(L, s); });
+        enc->ops.push_back(std::move(fn));
         enc->dispatches += 1;
         return;
     }
@@ -471,8 +474,11 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
         enc->ops.push_back([L, rows, cols](cudaStream_t s) { return og::launch_byte_sums(L, rows, cols, s); });
         enc->dispatches += 1;
     }
+    cudaError_t err;
+    og::LaunchFn fn = og::prepare_gemm_tc(L, &err);  // tensor maps built now, at record time
+    check_cuda(err, "Int8Gemm tensor maps");
     g->last = og::tc_cta_group(L) == 2 ? "tensor-core-2sm" : "tensor-core-1sm";
-    enc->ops.push_back([L](cudaStream_t s) { return og::launch_gemm_tc(L, s); });
+    enc->ops.push_back(std::move(fn));
     enc->dispatches += 1;
 }
 

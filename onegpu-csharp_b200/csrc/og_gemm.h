@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <functional>
 
 #include "og_kernels.cuh"
 
@@ -26,15 +27,20 @@ struct GemmLaunch {
     int tile;  // tensor-core tile rows: 0 chooses by size, 128 one CTA per tile, 256 a CTA pair (cta_group::2)
 };
 
+// A launch whose host-side preparation (tensor maps, parameters) is already done: calling it only launches.
+using LaunchFn = std::function<cudaError_t(cudaStream_t)>;
+
 // tcgen05 product (og_gemm_tc.cu). Eligible when K >= 1 and both operands' rows and batches start on 16-byte
-// boundaries (the TMA requirement).
+// boundaries (the TMA requirement). prepare_* builds the tensor maps at record time (null + *err on failure).
 bool tc_eligible(const GemmLaunch& L);
 int tc_cta_group(const GemmLaunch& L);  // 1 or 2: the tile launch_gemm_tc will use
+LaunchFn prepare_gemm_tc(const GemmLaunch& L, cudaError_t* err);
 cudaError_t launch_gemm_tc(const GemmLaunch& L, cudaStream_t stream);
 
 // Few-rows product (og_gemm_rows.cu): M <= 16 per batch, TMA-loadable operands; streams B once and takes the column
 // sums of B from the same MMA, so it needs no byte-sum pass and no scratch.
 bool rows_eligible(const GemmLaunch& L);
+LaunchFn prepare_gemm_rows(const GemmLaunch& L, cudaError_t* err);
 cudaError_t launch_gemm_rows(const GemmLaunch& L, cudaStream_t stream);
 
 // A 3-D byte tensor map (x innermost) with 128-byte swizzled box_x x box_y boxes (og_gemm_tc.cu).

@@ -1,12 +1,12 @@
 // The int8 product for few rows (M <= 16 per batch: decode steps), bandwidth-bound on B.
 //
 // The roles of the operands are swapped so that B streams through the tensor cores exactly once: the MMA computes
-// D[n, j] = sum_k B[k, n] * X[j, k] with tcgen05.mma.kind::i8, M = 128 columns of B per CTA, N = 32, where X's rows
-// 0..15 are the rows of A (TMA zero-fills the rows past M) and rows 16..31 are all ones. D's columns 0..15 are then
-// the dot products of the tile's 128 columns with the rows of A, and its columns 16..31 the column sums of B over K,
-// which the zero point of A needs - so no separate pass over B (235 MB at the decode config) is made for them.
+// D[n, j] = sum_k B[k, n] * A[j, k] with tcgen05.mma.kind::i8, M = 128 columns of B per CTA, N = 16 rows of A (TMA
+// zero-fills the rows past M). When A has a zero point, a second N = 16 MMA multiplies the same B tile with a block
+// of ones kept once in shared memory, so TMEM columns 16..31 hold the column sums of B over K - no separate pass over
+// B (235 MB at the decode config) is made for them.
 //
-// One CTA per 128 columns (and batch), the whole of K per CTA, 5 stages of 16 KB of B + 4 KB of X; two CTAs fit on
+// One CTA per 128 columns (and batch), the whole of K per CTA, 6 stages of 16 KB of B + 2 KB of A; two CTAs fit on
 // an SM, so every tile of the decode config (224) is resident at once and each pulls its share of HBM bandwidth
 // until all finish together. Warp 0 loads (TMA, no multicast), warp 1 issues the MMAs into a 32-column TMEM
 // accumulator, warps 2-5 compute the row sums of A while B streams (the zero point of B needs them), then drain TMEM:
@@ -24,15 +24,14 @@ namespace og {
 namespace rows {
 constexpr int BN = 128;          // columns of B (rows of the MMA) per CTA
 constexpr int BK = 128;
-constexpr int MAXM = 16;
-constexpr int XROWS = 32;        // rows of A (16) then ones (16)
-constexpr int STAGES = 5;
+constexpr int MAXM = 16;         // rows of A = N of the MMA
+constexpr int STAGES = 6;
 constexpr int B_BYTES = BN * BK;          // 16 KB
-constexpr int X_BYTES = XROWS * BK;       // 4 KB
-constexpr int A_BYTES = MAXM * BK;        // 2 KB loaded by TMA into the first half of X
+constexpr int A_BYTES = MAXM * BK;        // 2 KB
+constexpr int ONES_BYTES = MAXM * BK;     // 16 rows of ones, shared by every stage
 constexpr int THREADS = 192;
-constexpr int TMEM_COLS = 32;
-constexpr int SMEM_BYTES = STAGES * (B_BYTES + X_BYTES) + 1024 + 256;
+constexpr int TMEM_COLS = 32;             // columns 0..15 dot products, 16..31 column sums of B
+constexpr int SMEM_BYTES = STAGES * (B_BYTES + A_BYTES) + ONES_BYTES + 1024 + 256;
 }  // namespace rows
 
 struct RowsParams {
@@ -64,8 +63,9 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sB = smem;                                   // [STAGES][128 columns x 128 k]
-    uint8_t* sX = smem + rows::STAGES * rows::B_BYTES;    // [STAGES][32 rows x 128 k]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sX + rows::STAGES * rows::X_BYTES);
+    uint8_t* sX = smem + rows::STAGES * rows::B_BYTES;    // [STAGES][16 rows of A x 128 k]
+    uint8_t* sOnes = sX + rows::STAGES * rows::A_BYTES;   // [16 rows x 128 k] of ones
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + rows::ONES_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + rows::STAGES;
     uint64_t* tfull = bars + 2 * rows::STAGES;
@@ -77,14 +77,11 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
     const int lane = threadIdx.x & 31;
     const int tile = blockIdx.x;
     const int b = blockIdx.y;
+    const bool need_col_sums = p.epi.za != nullptr;  // za * colsum(B)
 
-    // The ones of X (rows 16..31 of every stage); any swizzle of all-ones bytes is all ones.
-    for (int i = threadIdx.x; i < rows::STAGES * (rows::X_BYTES - rows::A_BYTES) / 16; i += blockDim.x) {
-        const int s = i / ((rows::X_BYTES - rows::A_BYTES) / 16);
-        const int o = i % ((rows::X_BYTES - rows::A_BYTES) / 16);
-        reinterpret_cast<uint4*>(sX + s * rows::X_BYTES + rows::A_BYTES)[o] =
-            make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
-    }
+    // The block of ones (any swizzle of all-ones bytes is all ones).
+    for (int i = threadIdx.x; i < rows::ONES_BYTES / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(sOnes)[i] = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> visible to the tensor cores
     if (threadIdx.x == 0) {
         for (int s = 0; s < rows::STAGES; s++) {
@@ -121,7 +118,7 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
                     tma_load_3d(sB + s * rows::B_BYTES, &tmap_b, &full[s], kb * rows::BK, tile * rows::BN, bb);
                 else
                     tma_load_3d(sB + s * rows::B_BYTES, &tmap_b, &full[s], tile * rows::BN, kb * rows::BK, bb);
-                tma_load_3d(sX + s * rows::X_BYTES, &tmap_a, &full[s], kb * rows::BK, 0, ba);
+                tma_load_3d(sX + s * rows::A_BYTES, &tmap_a, &full[s], kb * rows::BK, 0, ba);
             }
             __syncwarp();
         }
@@ -133,13 +130,16 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
             tc_fence_after();
             if (lane == 0) {
                 const uint32_t b_addr = smem_u32(sB + s * rows::B_BYTES);
-                const uint32_t x_addr = smem_u32(sX + s * rows::X_BYTES);
+                const uint32_t x_addr = smem_u32(sX + s * rows::A_BYTES);
+                const uint32_t o_addr = smem_u32(sOnes);
 #pragma unroll
                 for (int kk = 0; kk < rows::BK / 32; kk++) {
                     const uint64_t adesc = B_KMAJOR ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
                                                     : smem_desc_sw128(b_addr + kk * 32 * 128, rows::B_BYTES, 1024);
-                    const uint64_t bdesc = smem_desc_sw128(x_addr + kk * 32, 16, 1024);
-                    mma_i8(tmem_base, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+                    const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+                    mma_i8(tmem_base, adesc, smem_desc_sw128(x_addr + kk * 32, 16, 1024), idesc, acc);
+                    if (need_col_sums)
+                        mma_i8(tmem_base + rows::MAXM, adesc, smem_desc_sw128(o_addr + kk * 32, 16, 1024), idesc, acc);
                 }
                 mma_commit(&empty[s]);
             }
@@ -150,40 +150,49 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
     } else {
         const int q = warp & 3;
         const Epilogue& e = p.epi;
-        // Row sums of A over K while B streams (needed for the zero point of B): warp q sums rows q, q+4, ...
+        // Row sums of A over K while B streams (needed for the zero point of B). Eight consecutive threads own a row
+        // (16 rows x 8 = the 128 epilogue threads) and read it in 16-byte chunks, 16 loads in flight per thread.
         if (e.zb != nullptr) {
-            for (int r = q; r < rows::MAXM; r += 4) {
-                int32_t sum = 0;
-                if (r < p.m) {
-                    const uint8_t* row = p.a + ba * p.stride_a + r * p.lda;
-                    for (int kk = lane * 16; kk < p.k; kk += 32 * 16) {
-                        if (kk + 16 <= p.k) {
-                            const uint4 w = __ldg(reinterpret_cast<const uint4*>(row + kk));
-                            if (e.za_signed) {
-                                sum = __dp4a(static_cast<int>(w.x), 0x01010101, sum);
-                                sum = __dp4a(static_cast<int>(w.y), 0x01010101, sum);
-                                sum = __dp4a(static_cast<int>(w.z), 0x01010101, sum);
-                                sum = __dp4a(static_cast<int>(w.w), 0x01010101, sum);
-                            } else {
-                                unsigned u = static_cast<unsigned>(sum);
-                                u = __dp4a(w.x, 0x01010101u, u);
-                                u = __dp4a(w.y, 0x01010101u, u);
-                                u = __dp4a(w.z, 0x01010101u, u);
-                                u = __dp4a(w.w, 0x01010101u, u);
-                                sum = static_cast<int32_t>(u);
-                            }
-                        } else {
-                            for (int t = kk; t < p.k; t++) {
-                                const uint8_t v = __ldg(row + t);
-                                sum += e.za_signed ? static_cast<int32_t>(static_cast<int8_t>(v)) : v;
-                            }
-                        }
+            const int t = threadIdx.x - 64;  // 0..127
+            const int r = t >> 3, part = t & 7;
+            int32_t sum = 0;
+            if (r < p.m) {
+                const uint8_t* row = p.a + ba * p.stride_a + r * p.lda;
+                const int chunks = p.k >> 4;
+                constexpr int U = 16;
+                for (int c0 = part; c0 < chunks; c0 += 8 * U) {
+                    uint4 w[U];
+#pragma unroll
+                    for (int u = 0; u < U; u++) {
+                        const int c = c0 + 8 * u;
+                        w[u] = c < chunks ? __ldg(reinterpret_cast<const uint4*>(row) + c) : make_uint4(0, 0, 0, 0);
                     }
 #pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+                    for (int u = 0; u < U; u++) {
+                        if (e.za_signed) {
+                            sum = __dp4a(static_cast<int>(w[u].x), 0x01010101, sum);
+                            sum = __dp4a(static_cast<int>(w[u].y), 0x01010101, sum);
+                            sum = __dp4a(static_cast<int>(w[u].z), 0x01010101, sum);
+                            sum = __dp4a(static_cast<int>(w[u].w), 0x01010101, sum);
+                        } else {
+                            unsigned s = static_cast<unsigned>(sum);
+                            s = __dp4a(w[u].x, 0x01010101u, s);
+                            s = __dp4a(w[u].y, 0x01010101u, s);
+                            s = __dp4a(w[u].z, 0x01010101u, s);
+                            s = __dp4a(w[u].w, 0x01010101u, s);
+                            sum = static_cast<int32_t>(s);
+                        }
+                    }
                 }
-                if (lane == 0) row_sum[r] = sum;
+                for (int kk = (chunks << 4) + part; kk < p.k; kk += 8) {  // the last k % 16 bytes
+                    const uint8_t v = __ldg(row + kk);
+                    sum += e.za_signed ? static_cast<int32_t>(static_cast<int8_t>(v)) : v;
+                }
             }
+            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+            sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 4);
+            if (part == 0) row_sum[r] = sum;
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
         if (!mbar_wait(tfull, 0, abort_flag)) goto done;
@@ -226,37 +235,45 @@ done:
 bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint64_t stride_y,
                         uint64_t stride_z, uint32_t box_x, uint32_t box_y);
 
-bool rows_eligible(const GemmLaunch& L) { return L.m >= 1 && L.m <= rows::MAXM && tc_eligible(L); }
-
-template <bool B_KMAJOR, int OUT>
-static cudaError_t launch_rows_t(const RowsParams& p, const CUtensorMap& ma, const CUtensorMap& mb, dim3 grid,
-                                 uint32_t idesc, cudaStream_t stream) {
-    auto kern = int8_gemm_rows_kernel<B_KMAJOR, OUT>;
-    static uint64_t configured = 0;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    const uint64_t bit = uint64_t(1) << (dev & 63);
-    if (!(configured & bit)) {
-        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rows::SMEM_BYTES);
-        if (e != cudaSuccess) return e;
-        configured |= bit;
-    }
-    kern<<<grid, rows::THREADS, rows::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
-    return cudaGetLastError();
+bool rows_eligible(const GemmLaunch& L) {
+    return L.m >= 1 && L.m <= rows::MAXM && L.batch <= 65535 && tc_eligible(L);
 }
 
-cudaError_t launch_gemm_rows(const GemmLaunch& L, cudaStream_t stream) {
+// Binds the kernel and its arguments; the returned function sets the shared-memory limit (first time per device)
+// and launches.
+template <bool B_KMAJOR, int OUT>
+static LaunchFn bind_rows_t(const RowsParams& p, const CUtensorMap& ma, const CUtensorMap& mb, dim3 grid,
+                            uint32_t idesc) {
+    return [=](cudaStream_t stream) -> cudaError_t {
+        auto kern = int8_gemm_rows_kernel<B_KMAJOR, OUT>;
+        static uint64_t configured = 0;
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        const uint64_t bit = uint64_t(1) << (dev & 63);
+        if (!(configured & bit)) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rows::SMEM_BYTES);
+            if (e != cudaSuccess) return e;
+            configured |= bit;
+        }
+        kern<<<grid, rows::THREADS, rows::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
+        return cudaGetLastError();
+    };
+}
+
+LaunchFn prepare_gemm_rows(const GemmLaunch& L, cudaError_t* err) {
+    *err = cudaErrorInvalidValue;
     const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
     const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
     CUtensorMap ma, mb;
     const uint64_t sa = ba > 1 ? uint64_t(L.stride_a) : (uint64_t(L.lda) * L.m + 15) & ~uint64_t(15);
-    if (!make_tensor_map_u8(&ma, L.a, L.k, L.m, ba, L.lda, sa, rows::BK, rows::MAXM)) return cudaErrorInvalidValue;
+    if (!make_tensor_map_u8(&ma, L.a, L.k, L.m, ba, L.lda, sa, rows::BK, rows::MAXM)) return nullptr;
     const uint64_t rows_b = L.trans_b ? L.n : L.k;
     const uint64_t sb = bb > 1 ? uint64_t(L.stride_b) : (uint64_t(L.ldb) * rows_b + 15) & ~uint64_t(15);
     const bool ok = L.trans_b ? make_tensor_map_u8(&mb, L.b, L.k, L.n, bb, L.ldb, sb, rows::BK, rows::BN)
                               : make_tensor_map_u8(&mb, L.b, L.n, L.k, bb, L.ldb, sb, rows::BN, rows::BK);
-    if (!ok) return cudaErrorInvalidValue;
+    if (!ok) return nullptr;
+    *err = cudaSuccess;
     RowsParams p;
     p.m = L.m;
     p.n = L.n;
@@ -269,20 +286,26 @@ cudaError_t launch_gemm_rows(const GemmLaunch& L, cudaStream_t stream) {
     p.a = L.a;
     p.epi = L.epi;
     p.error_flag = L.error_flag;
-    // The MMA's A operand is B (its type, MN-major unless B is stored N x K); its B operand is A plus the ones.
-    const uint32_t idesc = idesc_i8(L.b_signed, L.a_signed, !L.trans_b, false, rows::BN, rows::XROWS);
+    // The MMA's A operand is B (its type, MN-major unless B is stored N x K); its B operand is A (or the ones).
+    const uint32_t idesc = idesc_i8(L.b_signed, L.a_signed, !L.trans_b, false, rows::BN, rows::MAXM);
     const dim3 grid((L.n + rows::BN - 1) / rows::BN, L.batch);
     const bool km = L.trans_b != 0;
     switch (L.epi.out_kind) {
-        case OUT_I32: return km ? launch_rows_t<true, OUT_I32>(p, ma, mb, grid, idesc, stream)
-                                : launch_rows_t<false, OUT_I32>(p, ma, mb, grid, idesc, stream);
-        case OUT_F32: return km ? launch_rows_t<true, OUT_F32>(p, ma, mb, grid, idesc, stream)
-                                : launch_rows_t<false, OUT_F32>(p, ma, mb, grid, idesc, stream);
-        case OUT_U8: return km ? launch_rows_t<true, OUT_U8>(p, ma, mb, grid, idesc, stream)
-                               : launch_rows_t<false, OUT_U8>(p, ma, mb, grid, idesc, stream);
-        default: return km ? launch_rows_t<true, OUT_S8>(p, ma, mb, grid, idesc, stream)
-                           : launch_rows_t<false, OUT_S8>(p, ma, mb, grid, idesc, stream);
+        case OUT_I32: return km ? bind_rows_t<true, OUT_I32>(p, ma, mb, grid, idesc)
+                                : bind_rows_t<false, OUT_I32>(p, ma, mb, grid, idesc);
+        case OUT_F32: return km ? bind_rows_t<true, OUT_F32>(p, ma, mb, grid, idesc)
+                                : bind_rows_t<false, OUT_F32>(p, ma, mb, grid, idesc);
+        case OUT_U8: return km ? bind_rows_t<true, OUT_U8>(p, ma, mb, grid, idesc)
+                               : bind_rows_t<false, OUT_U8>(p, ma, mb, grid, idesc);
+        default: return km ? bind_rows_t<true, OUT_S8>(p, ma, mb, grid, idesc)
+                           : bind_rows_t<false, OUT_S8>(p, ma, mb, grid, idesc);
     }
+}
+
+cudaError_t launch_gemm_rows(const GemmLaunch& L, cudaStream_t stream) {
+    cudaError_t err;
+    LaunchFn fn = prepare_gemm_rows(L, &err);
+    return fn ? fn(stream) : err;
 }
 
 }  // namespace og

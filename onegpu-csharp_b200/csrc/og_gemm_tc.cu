@@ -44,7 +44,8 @@ struct Cfg {
     static constexpr int B_BYTES = B_COLS * BK;       // 32 KB or 16 KB per CTA
     static constexpr int B_BOX = 128 * BK;            // one 128-column box of an MN-major B
     static constexpr int STAGES = CG == 1 ? 4 : 6;
-    static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024 /* alignment */ + 256 /* barriers */;
+    static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024 /* alignment */ + 256 /* barriers */ +
+                                      5 * 4 * BN /* per-column epilogue terms */;
 };
 }  // namespace tc
 
@@ -73,70 +74,110 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& b,
     tn = in_group / gsize;
 }
 
+// Per-column terms of one output tile, staged in shared memory by the epilogue warps so that each element needs one
+// multiply-add and broadcast shared-memory reads:
+//   C = dot + zb[n] * (K * za[m] - rowsumA[m]) + c[n] - (za per row ? za[m] * colsumB[n] : 0)
+// with c[n] = intBias[n] - za * colsumB[n] when A has one zero point (intBias[n] otherwise), all modulo 2^32.
+struct ColTerms {
+    int32_t zb[tc::BN];
+    int32_t c[tc::BN];
+    int32_t csb[tc::BN];
+    float scale[tc::BN];
+    float fbias[tc::BN];
+};
+
+__device__ __forceinline__ void fill_col_terms(ColTerms& t, const Epilogue& e, int b, int col0, int tid, int nthreads) {
+    const bool za_scalar = e.za != nullptr && !e.za_vector;
+    const int32_t zas = za_scalar ? zp_value(e.za, 0, e.za_signed, 0) : 0;
+    for (int j = tid; j < tc::BN; j += nthreads) {
+        const int n = col0 + j;
+        const bool ok = n < e.n;
+        const int32_t csb = (ok && e.za != nullptr) ? __ldg(e.col_sum_b + b * e.col_sum_b_stride + n) : 0;
+        const int32_t bias = (ok && e.int_bias != nullptr) ? __ldg(e.int_bias + n) : 0;
+        t.zb[j] = ok ? zp_value(e.zb, e.zb_vector, e.zb_signed, n) : 0;
+        t.csb[j] = csb;
+        t.c[j] = static_cast<int32_t>(static_cast<uint32_t>(bias) - static_cast<uint32_t>(zas) * static_cast<uint32_t>(csb));
+        t.scale[j] = (ok && e.scale != nullptr) ? __ldg(e.scale + (e.scale_vector ? n : 0)) : 0.0f;
+        t.fbias[j] = (ok && e.float_bias != nullptr) ? __ldg(e.float_bias + n) : 0.0f;
+    }
+}
+
+// The corrected int32 sum of column j of the tile, for a row with zero point za and rt = K * za - rowsumA.
+__device__ __forceinline__ uint32_t tile_sum(const ColTerms& t, bool za_per_row, uint32_t za, uint32_t rt, int j,
+                                             uint32_t dot) {
+    uint32_t s = dot + static_cast<uint32_t>(t.zb[j]) * rt + static_cast<uint32_t>(t.c[j]);
+    if (za_per_row) s -= za * static_cast<uint32_t>(t.csb[j]);
+    return s;
+}
+
 template <int OUT>
-__device__ __forceinline__ void store_chunk(const Epilogue& e, const RowTerms& rt, int b, int m, int n0,
+__device__ __forceinline__ uint32_t finish_word(const ColTerms& t, const Epilogue& e, bool terms, bool za_per_row,
+                                                uint32_t za, uint32_t rt, int j, uint32_t dot) {
+    if constexpr (OUT == OUT_I32) {
+        return terms ? tile_sum(t, za_per_row, za, rt, j, dot) : dot;
+    } else if constexpr (OUT == OUT_F32) {
+        const uint32_t s = tile_sum(t, za_per_row, za, rt, j, dot);
+        float f = __fmul_rn(__int2float_rn(static_cast<int32_t>(s)), t.scale[j]);
+        if (e.float_bias != nullptr) f = __fadd_rn(f, t.fbias[j]);
+        return __float_as_uint(f);
+    } else {
+        const uint32_t s = tile_sum(t, za_per_row, za, rt, j, dot);
+        constexpr bool U = OUT == OUT_U8;
+        const int lo = U ? 0 : -128, hi = U ? 255 : 127;
+        const float v = __fmul_rn(__int2float_rn(static_cast<int32_t>(s)), t.scale[j]);
+        if (isnan(v)) return static_cast<uint32_t>(lo & 0xFF);
+        float r = rintf(v);
+        const float flo = static_cast<float>(lo - e.zero_point_y), fhi = static_cast<float>(hi - e.zero_point_y);
+        r = r < flo ? flo : (r > fhi ? fhi : r);
+        return static_cast<uint32_t>((static_cast<int>(r) + e.zero_point_y) & 0xFF);
+    }
+}
+
+// Stores 32 consecutive results of row m (columns n0.. of the output; j0 is n0's column within the tile).
+template <int OUT>
+__device__ __forceinline__ void store_chunk(const ColTerms& t, const Epilogue& e, bool terms, bool za_per_row,
+                                            uint32_t za, uint32_t rt, int b, int m, int n0, int j0,
                                             const uint32_t (&r)[32]) {
     const bool full = e.vec_ok && (n0 + 32 <= e.n);
-    if constexpr (OUT == OUT_I32) {
-        int32_t* row = static_cast<int32_t*>(e.c) + b * e.batch_stride_c + static_cast<int64_t>(m) * e.ldc;
+    if constexpr (OUT == OUT_I32 || OUT == OUT_F32) {
+        uint32_t* row = static_cast<uint32_t*>(e.c) + b * e.batch_stride_c + static_cast<int64_t>(m) * e.ldc;
         if (full) {
-            int4* dst = reinterpret_cast<int4*>(row + n0);
+            uint4* dst = reinterpret_cast<uint4*>(row + n0);
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                int4 v;
-                v.x = static_cast<int32_t>(corrected(e, rt, b, n0 + 4 * j + 0, r[4 * j + 0]));
-                v.y = static_cast<int32_t>(corrected(e, rt, b, n0 + 4 * j + 1, r[4 * j + 1]));
-                v.z = static_cast<int32_t>(corrected(e, rt, b, n0 + 4 * j + 2, r[4 * j + 2]));
-                v.w = static_cast<int32_t>(corrected(e, rt, b, n0 + 4 * j + 3, r[4 * j + 3]));
-                __stcs(dst + j, v);
+            for (int q = 0; q < 8; q++) {
+                uint4 v;
+                v.x = finish_word<OUT>(t, e, terms, za_per_row, za, rt, j0 + 4 * q + 0, r[4 * q + 0]);
+                v.y = finish_word<OUT>(t, e, terms, za_per_row, za, rt, j0 + 4 * q + 1, r[4 * q + 1]);
+                v.z = finish_word<OUT>(t, e, terms, za_per_row, za, rt, j0 + 4 * q + 2, r[4 * q + 2]);
+                v.w = finish_word<OUT>(t, e, terms, za_per_row, za, rt, j0 + 4 * q + 3, r[4 * q + 3]);
+                __stcs(dst + q, v);
             }
         } else {
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                if (n0 + j < e.n) row[n0 + j] = static_cast<int32_t>(corrected(e, rt, b, n0 + j, r[j]));
-            }
-        }
-    } else if constexpr (OUT == OUT_F32) {
-        float* row = static_cast<float*>(e.c) + b * e.batch_stride_c + static_cast<int64_t>(m) * e.ldc;
-        if (full) {
-            float4* dst = reinterpret_cast<float4*>(row + n0);
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                float4 v;
-                v.x = finish_float(e, n0 + 4 * j + 0, corrected(e, rt, b, n0 + 4 * j + 0, r[4 * j + 0]));
-                v.y = finish_float(e, n0 + 4 * j + 1, corrected(e, rt, b, n0 + 4 * j + 1, r[4 * j + 1]));
-                v.z = finish_float(e, n0 + 4 * j + 2, corrected(e, rt, b, n0 + 4 * j + 2, r[4 * j + 2]));
-                v.w = finish_float(e, n0 + 4 * j + 3, corrected(e, rt, b, n0 + 4 * j + 3, r[4 * j + 3]));
-                __stcs(dst + j, v);
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-                if (n0 + j < e.n) row[n0 + j] = finish_float(e, n0 + j, corrected(e, rt, b, n0 + j, r[j]));
+            for (int q = 0; q < 32; q++) {
+                if (n0 + q < e.n) row[n0 + q] = finish_word<OUT>(t, e, terms, za_per_row, za, rt, j0 + q, r[q]);
             }
         }
     } else {
-        constexpr bool U = (OUT == OUT_U8);
         uint8_t* row = static_cast<uint8_t*>(e.c) + b * e.batch_stride_c + static_cast<int64_t>(m) * e.ldc;
         if (full) {
             uint32_t w[8];
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
+            for (int q = 0; q < 8; q++) {
                 uint32_t x = 0;
 #pragma unroll
-                for (int t = 0; t < 4; t++) {
-                    const int n = n0 + 4 * j + t;
-                    x |= static_cast<uint32_t>(finish_byte(e, n, corrected(e, rt, b, n, r[4 * j + t]), U)) << (8 * t);
-                }
-                w[j] = x;
+                for (int u = 0; u < 4; u++)
+                    x |= finish_word<OUT>(t, e, terms, za_per_row, za, rt, j0 + 4 * q + u, r[4 * q + u]) << (8 * u);
+                w[q] = x;
             }
             uint4* dst = reinterpret_cast<uint4*>(row + n0);
             dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
             dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
         } else {
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                if (n0 + j < e.n) row[n0 + j] = finish_byte(e, n0 + j, corrected(e, rt, b, n0 + j, r[j]), U);
+            for (int q = 0; q < 32; q++) {
+                if (n0 + q < e.n)
+                    row[n0 + q] = static_cast<uint8_t>(finish_word<OUT>(t, e, terms, za_per_row, za, rt, j0 + q, r[q]));
             }
         }
     }
@@ -290,6 +331,11 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, i.e. rows 32*(w%4) + lane of this CTA's 128 rows.
         const int q = warp & 3;
         const uint32_t tempty_leader = CG == 2 ? mapa_shared(smem_u32(&tempty[0]), 0) : 0;
+        const Epilogue& e = p.epi;
+        ColTerms& terms_smem = *reinterpret_cast<ColTerms*>(reinterpret_cast<uint8_t*>(bars) + 256);
+        // Column terms are needed unless the result is the raw int32 sum.
+        const bool terms = OUT != OUT_I32 || e.za != nullptr || e.zb != nullptr || e.int_bias != nullptr;
+        const bool za_per_row = e.za != nullptr && e.za_vector;
         int lt = 0;
         for (int tile = worker; tile < p.total_tiles; tile += workers, lt++) {
             int b, tm, tn;
@@ -298,9 +344,20 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             const uint32_t aph = (lt >> 1) & 1;
             if (!mbar_wait(&tfull[acc], aph, abort_flag)) goto done;
             tc_fence_after();
+            if (terms) {
+                asm volatile("bar.sync 1, 128;" ::: "memory");  // the previous tile's terms are no longer read
+                fill_col_terms(terms_smem, e, b, tn * tc::BN, threadIdx.x - 64, 128);
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+            }
             const int m = tm * C::BM + static_cast<int>(rank) * 128 + q * 32 + lane;
             const bool row_ok = m < p.m;
-            const RowTerms rt = row_ok ? row_terms(p.epi, b, m) : RowTerms{0, 0};
+            uint32_t za = 0, rt = 0;  // zero point of A for this row, and K * za - rowsumA
+            if (row_ok && terms) {
+                za = static_cast<uint32_t>(zp_value(e.za, e.za_vector, e.za_signed, m));
+                const uint32_t rsa = e.row_sum_a ? static_cast<uint32_t>(__ldg(e.row_sum_a + b * e.row_sum_a_stride + m))
+                                                 : 0u;
+                rt = static_cast<uint32_t>(p.k) * za - rsa;
+            }
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * tc::BN;
 #pragma unroll 1
             for (int c = 0; c < tc::BN / 32; c++) {
@@ -309,7 +366,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                 uint32_t r[32];
                 tmem_ld_32x32b_x32(t_row + c * 32, r);
                 tmem_ld_wait();
-                if (row_ok) store_chunk<OUT>(p.epi, rt, b, m, n0, r);
+                if (row_ok) store_chunk<OUT>(terms_smem, e, terms, za_per_row, za, rt, b, m, n0, c * 32, r);
             }
             tc_fence_before();
             __syncwarp();
@@ -409,39 +466,49 @@ static cudaError_t configure(K kern, int smem, uint64_t& configured) {
     return cudaSuccess;
 }
 
+// Binds the kernel and its arguments; the returned function only sets the shared-memory limit (first time per
+// device) and launches.
 template <int CG, bool B_MN, int OUT>
-static cudaError_t launch_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensorMap& ma, const CUtensorMap& mb,
-                               int grid, cudaStream_t stream) {
+static LaunchFn bind_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensorMap& ma, const CUtensorMap& mb,
+                          int grid) {
     using C = tc::Cfg<CG>;
-    static uint64_t configured = 0;
     const uint32_t idesc = idesc_i8(L.a_signed, L.b_signed, false, B_MN, C::BM, tc::BN);
-    if constexpr (CG == 2) {
-        auto kern = int8_gemm_tc2_kernel<B_MN, OUT>;
-        cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
-        if (e != cudaSuccess) return e;
-        kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
-    } else {
-        auto kern = int8_gemm_tc_kernel<B_MN, OUT>;
-        cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
-        if (e != cudaSuccess) return e;
-        kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
-    }
-    return cudaGetLastError();
+    return [=](cudaStream_t stream) -> cudaError_t {
+        static uint64_t configured = 0;
+        if constexpr (CG == 2) {
+            auto kern = int8_gemm_tc2_kernel<B_MN, OUT>;
+            cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
+            if (e != cudaSuccess) return e;
+            kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
+        } else {
+            auto kern = int8_gemm_tc_kernel<B_MN, OUT>;
+            cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
+            if (e != cudaSuccess) return e;
+            kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
+        }
+        return cudaGetLastError();
+    };
 }
 
 template <int CG>
-static cudaError_t launch_cg(const GemmLaunch& L, cudaStream_t stream) {
+static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
     using C = tc::Cfg<CG>;
+    *err = cudaSuccess;
     const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
     const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
     CUtensorMap ma, mb;
-    if (!make_map(&ma, L.a, L.k, L.m, ba, L.lda, ba > 1 ? L.stride_a : round16(uint64_t(L.lda) * L.m), tc::BK, 128))
-        return cudaErrorInvalidValue;
+    if (!make_map(&ma, L.a, L.k, L.m, ba, L.lda, ba > 1 ? L.stride_a : round16(uint64_t(L.lda) * L.m), tc::BK, 128)) {
+        *err = cudaErrorInvalidValue;
+        return nullptr;
+    }
     const uint64_t rows_b = L.trans_b ? L.n : L.k;
     const uint64_t sb = bb > 1 ? uint64_t(L.stride_b) : round16(uint64_t(L.ldb) * rows_b);
     const bool ok = L.trans_b ? make_map(&mb, L.b, L.k, L.n, bb, L.ldb, sb, tc::BK, C::B_COLS)
                               : make_map(&mb, L.b, L.n, L.k, bb, L.ldb, sb, 128, tc::BK);
-    if (!ok) return cudaErrorInvalidValue;
+    if (!ok) {
+        *err = cudaErrorInvalidValue;
+        return nullptr;
+    }
 
     TcParams p;
     p.m = L.m;
@@ -461,14 +528,14 @@ static cudaError_t launch_cg(const GemmLaunch& L, cudaStream_t stream) {
     const int grid = static_cast<int>((total < workers ? total : workers) * CG);
     const bool bmn = !L.trans_b;
     switch (L.epi.out_kind) {
-        case OUT_I32: return bmn ? launch_tc_t<CG, true, OUT_I32>(L, p, ma, mb, grid, stream)
-                                 : launch_tc_t<CG, false, OUT_I32>(L, p, ma, mb, grid, stream);
-        case OUT_F32: return bmn ? launch_tc_t<CG, true, OUT_F32>(L, p, ma, mb, grid, stream)
-                                 : launch_tc_t<CG, false, OUT_F32>(L, p, ma, mb, grid, stream);
-        case OUT_U8: return bmn ? launch_tc_t<CG, true, OUT_U8>(L, p, ma, mb, grid, stream)
-                                : launch_tc_t<CG, false, OUT_U8>(L, p, ma, mb, grid, stream);
-        default: return bmn ? launch_tc_t<CG, true, OUT_S8>(L, p, ma, mb, grid, stream)
-                            : launch_tc_t<CG, false, OUT_S8>(L, p, ma, mb, grid, stream);
+        case OUT_I32: return bmn ? bind_tc_t<CG, true, OUT_I32>(L, p, ma, mb, grid)
+                                 : bind_tc_t<CG, false, OUT_I32>(L, p, ma, mb, grid);
+        case OUT_F32: return bmn ? bind_tc_t<CG, true, OUT_F32>(L, p, ma, mb, grid)
+                                 : bind_tc_t<CG, false, OUT_F32>(L, p, ma, mb, grid);
+        case OUT_U8: return bmn ? bind_tc_t<CG, true, OUT_U8>(L, p, ma, mb, grid)
+                                : bind_tc_t<CG, false, OUT_U8>(L, p, ma, mb, grid);
+        default: return bmn ? bind_tc_t<CG, true, OUT_S8>(L, p, ma, mb, grid)
+                            : bind_tc_t<CG, false, OUT_S8>(L, p, ma, mb, grid);
     }
 }
 
@@ -481,8 +548,14 @@ int tc_cta_group(const GemmLaunch& L) {
     return (L.m > 128 && pair_tiles * 4 >= int64_t(L.num_sms / 2) * 3) ? 2 : 1;
 }
 
+LaunchFn prepare_gemm_tc(const GemmLaunch& L, cudaError_t* err) {
+    return tc_cta_group(L) == 2 ? prepare_cg<2>(L, err) : prepare_cg<1>(L, err);
+}
+
 cudaError_t launch_gemm_tc(const GemmLaunch& L, cudaStream_t stream) {
-    return tc_cta_group(L) == 2 ? launch_cg<2>(L, stream) : launch_cg<1>(L, stream);
+    cudaError_t err;
+    LaunchFn fn = prepare_gemm_tc(L, &err);
+    return fn ? fn(stream) : err;
 }
 
 }  // namespace og

@@ -34,8 +34,9 @@ WORKLOADS = {
     # name: (M, N, K, batch, a_signed, za, zb, out, description)
     "c3": dict(m=8192, n=8192, k=8192, batch=1, a_signed=True, zp=False, out="i32",
                desc="square s8 x s8 -> s32, 8192^3, zero points absent"),
-    "c2": dict(m=4096, n=4096, k=4096, batch=1, a_signed=False, zp=True, out="f32",
-               desc="u8 (DQL output, scalar zp) x s8 (per-column zp) -> f32 dequant, 4096^3"),
+    "c2": dict(m=4096, n=4096, k=4096, batch=1, a_signed=False, zp=True, out="f32", dql=True,
+               desc="DynamicQuantizeLinear of f32 [4096 x 4096] ~ N(0,1) to u8, then u8 x s8 (per-column zp) -> f32 "
+                    "dequantized by a_scale * b_scale[col], 4096^3; one step = both"),
     "c4": dict(m=2048, n=12288, k=4096, batch=8, a_signed=False, zp=True, out="i32",
                desc="batched QKV u8 (zp) x shared s8 (per-column zp) -> s32, 8 x 2048 x 12288 x 4096"),
     "c5": dict(m=16, n=28672, k=8192, batch=1, a_signed=False, zp=True, out="i32",
@@ -203,7 +204,21 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         zb = dev.create_buffer(np.int8, rng.integers(-8, 9, size=shard_n).astype(np.int8))
         zpa, zpb = og.Int8Operand(za, 0), og.Int8Operand(zb, 0, True)
         extra += [za, zb]
-    if w["out"] == "f32":
+    dq = x_dev = None
+    if w.get("dql"):
+        # Config 2: the activations arrive as float32 ~ N(0, 1); DynamicQuantizeLinear turns them into A (u8) with a
+        # scale and zero point on the device, and the product dequantizes with a_scale * b_scale[col].
+        x_host = rng.standard_normal(size=M * K, dtype=np.float32)
+        x_dev = dev.create_buffer(np.float32, x_host)
+        a_scale = dev.create_buffer(np.float32, 1)
+        za = dev.create_buffer(np.uint8, 1)
+        zb = dev.create_buffer(np.int8, rng.integers(-8, 9, size=shard_n).astype(np.int8))
+        b_scale = dev.create_buffer(np.float32, rng.uniform(0.001, 0.02, size=shard_n).astype(np.float32))
+        zpa, zpb = og.Int8Operand(za, 0), og.Int8Operand(zb, 0, True)
+        dq = og.DynamicQuantizeKernels(dev)
+        extra += [x_dev, a_scale, za, zb, b_scale]
+        a_host = x_host  # what the e2e leg uploads
+    elif w["out"] == "f32":
         s = dev.create_buffer(np.float32, rng.uniform(0.001, 0.02, size=shard_n).astype(np.float32) * 0.02)
         scale = og.Int8Operand(s, 0, True)
         extra.append(s)
@@ -212,7 +227,11 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
     gemm = og.Int8Gemm(dev)
 
     def encode(enc):
-        if w["out"] == "f32":
+        if dq is not None:
+            dq.encode(enc, x_dev, 0, M * K, a, 0, a_scale, 0, za, 0)
+            gemm.encode_dequantize(enc, prob, a, b, c, og.Int8Operand(a_scale, 0), og.Int8Operand(b_scale, 0, True),
+                                   zpa, zpb)
+        elif w["out"] == "f32":
             gemm.encode_float(enc, prob, a, b, c, scale, zpa, zpb)
         else:
             gemm.encode_int32(enc, prob, a, b, c, zpa, zpb)
@@ -269,7 +288,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         idx = max(i, 0)
         if i >= 0:
             dev.timestamp(e2e_stamps, 2 * idx)
-        og._check(og._lib.og_buffer_write(dev.handle, a.ptr, pin.value, a_host.nbytes))
+        og._check(og._lib.og_buffer_write(dev.handle, (x_dev or a).ptr, pin.value, a_host.nbytes))
         og._check(og._lib.og_buffer_write(dev.handle, b.ptr, pin.value + a_host.nbytes, b_host.nbytes))
         enc = dev.begin_commands()
         encode(enc)
@@ -318,7 +337,8 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
     achieved = shard_ops / per_launch_s / 1e12
     # Bytes one launch must move at least: A, the B slab, C, and the zero-point / scale vectors.
     algo_bytes = (a_host.nbytes + b_host.nbytes + count * np.dtype(out_dtype).itemsize
-                  + (shard_n + 1 if w["zp"] else 0) + (4 * shard_n if w["out"] == "f32" else 0))
+                  + (shard_n + 1 if w["zp"] else 0) + (4 * shard_n if w["out"] == "f32" else 0)
+                  + (2 * M * K if w.get("dql") else 0))  # the quantized A written by DQL and read by the product
     peaks = load_peaks()
     # A timed region of back-to-back launches longer than a second settles at the power-capped clock: compare with
     # the sustained figure then, with the burst figure for short runs.
@@ -360,6 +380,8 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         print(json.dumps(line), flush=True)
     for v in [a, b, c, flush] + extra:
         v.dispose()
+    if dq is not None:
+        dq.dispose()
     gemm.dispose()
     stamps.dispose()
     e2e_stamps.dispose()

@@ -205,6 +205,17 @@ OG_API og_status og_int8_gemm_encode_float(og_int8_gemm* gemm, og_encoder* encod
                                            const og_operand* scale, const og_operand* zero_point_a,
                                            const og_operand* zero_point_b, const og_operand* float_bias,
                                            const og_operand* int_bias);
+/* MatMulIntegerToFloat in one call: float(sum + intBias) * (aScale * bScale[n]) (+ floatBias[n]), the scale product
+ * formed in the epilogue with the same float32 rounding as the reference's chain, which forms it in a pass of its own
+ * (ElementwiseKernels.EncodeBinary(Mul), tests/RecursiveAI.OneGpu.Kernels.Tests/Int8Tests.cs:733-739) and hands it to
+ * EncodeFloat (Int8Gemm.cs:270-314). aScale is one float (e.g. the scale DynamicQuantizeLinear wrote on the device);
+ * bScale is one value or one per column. Checks as EncodeFloat, argument names "aScale" and "bScale". */
+OG_API og_status og_int8_gemm_encode_dequantize(og_int8_gemm* gemm, og_encoder* encoder,
+                                                const og_int8_gemm_problem* problem, const og_buffer* a,
+                                                const og_buffer* b, const og_buffer* c, const og_operand* a_scale,
+                                                const og_operand* b_scale, const og_operand* zero_point_a,
+                                                const og_operand* zero_point_b, const og_operand* float_bias,
+                                                const og_operand* int_bias);
 /* Int8Gemm.EncodeRequantized<TA,TB,TY> (Int8Gemm.cs:336-363). scratch (Int8Scratch, Int8Gemm.cs:37) may be NULL; its
  * buffer is an int32 buffer and its offset an element offset. */
 OG_API og_status og_int8_gemm_encode_requantized(og_int8_gemm* gemm, og_encoder* encoder,
@@ -239,6 +250,11 @@ OG_API og_status og_int8_gemm_check_float(const og_int8_gemm_problem* problem, c
                                           const og_buffer* c, const og_operand* scale, const og_operand* zero_point_a,
                                           const og_operand* zero_point_b, const og_operand* float_bias,
                                           const og_operand* int_bias);
+OG_API og_status og_int8_gemm_check_dequantize(const og_int8_gemm_problem* problem, const og_buffer* a,
+                                               const og_buffer* b, const og_buffer* c, const og_operand* a_scale,
+                                               const og_operand* b_scale, const og_operand* zero_point_a,
+                                               const og_operand* zero_point_b, const og_operand* float_bias,
+                                               const og_operand* int_bias);
 OG_API og_status og_int8_gemm_check_requantized(const og_int8_gemm_problem* problem, const og_buffer* a,
                                                 const og_buffer* b, const og_buffer* y, const og_operand* multiplier,
                                                 int32_t zero_point_y, const og_operand* zero_point_a,

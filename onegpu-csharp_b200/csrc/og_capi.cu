@@ -322,6 +322,34 @@ Prepared check_float(const og_int8_gemm_problem* p, const og_buffer* a, const og
     return pr;
 }
 
+// The float form with the scale formed as scaleA * scaleB[n]: EncodeFloat's checks with "bScale" for the scale,
+// plus one value of "aScale".
+Prepared check_dequantize(const og_int8_gemm_problem* p, const og_buffer* a, const og_buffer* b, const og_buffer* c,
+                          const og_operand* a_scale, const og_operand* b_scale, const og_operand* za,
+                          const og_operand* zb, const og_operand* fbias, const og_operand* ibias) {
+    if (c == nullptr || c->ptr == nullptr) null_arg(kGemm, "c");
+    Prepared pr = prepare(p, a, b, za, zb);
+    require_type(kGemm, c, "c", OG_F32);
+    range(kGemm, "c", c->length, p->offset_c, result_count(p));
+    if (a_scale == nullptr) null_arg(kGemm, "aScale");
+    if (b_scale == nullptr) null_arg(kGemm, "bScale");
+    if (a_scale->is_vector) shape(kGemm, "aScale", "must be one value (the scale of the whole of A)");
+    check_vector("aScale", a_scale, p->n);
+    require_type(kGemm, &a_scale->buffer, "aScale", OG_F32);
+    check_vector("bScale", b_scale, p->n);
+    require_type(kGemm, &b_scale->buffer, "bScale", OG_F32);
+    if (fbias != nullptr) {
+        check_vector("floatBias", fbias, p->n);
+        require_type(kGemm, &fbias->buffer, "floatBias", OG_F32);
+    }
+    if (!pr.ok) return pr;
+    if (ibias != nullptr) {
+        check_vector("intBias", ibias, p->n);
+        require_type(kGemm, &ibias->buffer, "intBias", OG_I32);
+    }
+    return pr;
+}
+
 Prepared check_requantized(const og_int8_gemm_problem* p, const og_buffer* a, const og_buffer* b, const og_buffer* y,
                            const og_operand* mult, int32_t zero_y, const og_operand* za, const og_operand* zb,
                            const og_operand* ibias, const og_operand* scratch) {
@@ -884,6 +912,38 @@ OG_API og_status og_int8_gemm_encode_float(og_int8_gemm* g, og_encoder* enc, con
         L.epi.int_bias = reinterpret_cast<const int32_t*>(operand_ptr(ibias));
         L.epi.scale = reinterpret_cast<const float*>(operand_ptr(scale));
         L.epi.scale_vector = scale->is_vector;
+        L.epi.float_bias = reinterpret_cast<const float*>(operand_ptr(fbias));
+        record_gemm(g, enc, L, nullptr);
+    });
+}
+
+OG_API og_status og_int8_gemm_check_dequantize(const og_int8_gemm_problem* p, const og_buffer* a, const og_buffer* b,
+                                               const og_buffer* c, const og_operand* a_scale, const og_operand* b_scale,
+                                               const og_operand* za, const og_operand* zb, const og_operand* fbias,
+                                               const og_operand* ibias) {
+    return guard([&] { check_dequantize(p, a, b, c, a_scale, b_scale, za, zb, fbias, ibias); });
+}
+
+OG_API og_status og_int8_gemm_encode_dequantize(og_int8_gemm* g, og_encoder* enc, const og_int8_gemm_problem* p,
+                                                const og_buffer* a, const og_buffer* b, const og_buffer* c,
+                                                const og_operand* a_scale, const og_operand* b_scale,
+                                                const og_operand* za, const og_operand* zb, const og_operand* fbias,
+                                                const og_operand* ibias) {
+    return guard([&] {
+        live_gemm(g);
+        if (c == nullptr || c->ptr == nullptr) null_arg(kGemm, "c");
+        if (enc == nullptr) null_arg(kGemm, "encoder");
+        const Prepared pr = check_dequantize(p, a, b, c, a_scale, b_scale, za, zb, fbias, ibias);
+        if (!pr.ok) {
+            g->last = "none";
+            return;
+        }
+        use(g->device);
+        og::GemmLaunch L = make_launch(g, p, pr, a, b, za, zb, og::OUT_F32, c->ptr);
+        L.epi.int_bias = reinterpret_cast<const int32_t*>(operand_ptr(ibias));
+        L.epi.scale = reinterpret_cast<const float*>(operand_ptr(b_scale));
+        L.epi.scale_vector = b_scale->is_vector;
+        L.epi.scale_a = reinterpret_cast<const float*>(operand_ptr(a_scale));
         L.epi.float_bias = reinterpret_cast<const float*>(operand_ptr(fbias));
         record_gemm(g, enc, L, nullptr);
     });

@@ -97,7 +97,7 @@ __device__ __forceinline__ void fill_col_terms(ColTerms& t, const Epilogue& e, i
         t.zb[j] = ok ? zp_value(e.zb, e.zb_vector, e.zb_signed, n) : 0;
         t.csb[j] = csb;
         t.c[j] = static_cast<int32_t>(static_cast<uint32_t>(bias) - static_cast<uint32_t>(zas) * static_cast<uint32_t>(csb));
-        t.scale[j] = (ok && e.scale != nullptr) ? __ldg(e.scale + (e.scale_vector ? n : 0)) : 0.0f;
+        t.scale[j] = (ok && e.scale != nullptr) ? col_scale(e, n) : 0.0f;
         t.fbias[j] = (ok && e.float_bias != nullptr) ? __ldg(e.float_bias + n) : 0.0f;
     }
 }

@@ -30,6 +30,7 @@ struct Epilogue {
     const int32_t* int_bias;      // per column, or null
     const float* scale;           // float form: scale; requantized form: multiplier
     int scale_vector;
+    const float* scale_a;         // dequantize form: one scale of A multiplied into every column's scale, or null
     const float* float_bias;      // per column, or null
     int zero_point_y;
     int vec_ok;                   // every output row starts on a 16-byte boundary
@@ -70,9 +71,16 @@ __device__ __forceinline__ uint32_t corrected(const Epilogue& e, const RowTerms&
     return s;
 }
 
+// The scale of column n: scale[n] (or the single scale), times the scale of A when one is given - one float32
+// product, the same rounding as forming scaleA * scaleB[n] in a pass of its own.
+__device__ __forceinline__ float col_scale(const Epilogue& e, int n) {
+    const float s = __ldg(e.scale + (e.scale_vector ? n : 0));
+    return e.scale_a != nullptr ? __fmul_rn(__ldg(e.scale_a), s) : s;
+}
+
 // float(sum) * scale, then + float bias: two separate roundings, never fused (Int8GemmEpilogue.hlsli semantics).
 __device__ __forceinline__ float finish_float(const Epilogue& e, int n, uint32_t s) {
-    const float sc = __ldg(e.scale + (e.scale_vector ? n : 0));
+    const float sc = col_scale(e, n);
     float f = __fmul_rn(__int2float_rn(static_cast<int32_t>(s)), sc);
     if (e.float_bias != nullptr) f = __fadd_rn(f, __ldg(e.float_bias + n));
     return f;
@@ -83,7 +91,7 @@ __device__ __forceinline__ float finish_float(const Epilogue& e, int n, uint32_t
 __device__ __forceinline__ uint8_t finish_byte(const Epilogue& e, int n, uint32_t s, bool out_unsigned) {
     const int lo = out_unsigned ? 0 : -128;
     const int hi = out_unsigned ? 255 : 127;
-    const float mult = __ldg(e.scale + (e.scale_vector ? n : 0));
+    const float mult = col_scale(e, n);
     const float v = __fmul_rn(__int2float_rn(static_cast<int32_t>(s)), mult);
     if (isnan(v)) return static_cast<uint8_t>(lo & 0xFF);
     float r = rintf(v);

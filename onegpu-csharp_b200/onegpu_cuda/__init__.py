@@ -119,6 +119,8 @@ EXPORTS = {
     "og_int8_gemm_encode_float": [_P, _P, _PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD, _OPD, _OPD],
     "og_int8_gemm_encode_requantized": [_P, _P, _PROB, _BUF, _BUF, _BUF, _OPD, ctypes.c_int32, _OPD, _OPD, _OPD,
                                         _OPD],
+    "og_int8_gemm_encode_dequantize": [_P, _P, _PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD, _OPD, _OPD, _OPD],
+    "og_int8_gemm_check_dequantize": [_PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD, _OPD, _OPD, _OPD],
     "og_int8_gemm_int32_noalloc": [_P, _PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD],
     "og_int8_gemm_check_int32": [_PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD],
     "og_int8_gemm_check_float": [_PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD, _OPD, _OPD],
@@ -513,6 +515,18 @@ class Int8Gemm:
                                                     int(zero_point_y), _opd(zero_point_a), _opd(zero_point_b),
                                                     _opd(int_bias), _opd(scratch)))
 
+    def encode_dequantize(self, encoder: GpuCommandEncoder, problem: Int8GemmProblem, a: GpuBuffer, b: GpuBuffer,
+                          c: GpuBuffer, a_scale: Int8Operand, b_scale: Int8Operand,
+                          zero_point_a: Optional[Int8Operand] = None, zero_point_b: Optional[Int8Operand] = None,
+                          float_bias: Optional[Int8Operand] = None, int_bias: Optional[Int8Operand] = None) -> None:
+        """MatMulIntegerToFloat in one call: float(sum + intBias) * (aScale * bScale[n]) (+ floatBias), the scale
+        product formed in the epilogue (the reference forms it with a separate element-wise pass)."""
+        p = problem.c_struct()
+        _check(_lib.og_int8_gemm_encode_dequantize(self.handle, encoder.handle if encoder else None, ctypes.byref(p),
+                                                   _buf(a), _buf(b), _buf(c), _opd(a_scale), _opd(b_scale),
+                                                   _opd(zero_point_a), _opd(zero_point_b), _opd(float_bias),
+                                                   _opd(int_bias)))
+
     # The reference's member names.
     EncodeInt32 = encode_int32
     EncodeFloat = encode_float
@@ -571,6 +585,14 @@ def check_float(problem, a, b, c, scale, zero_point_a=None, zero_point_b=None, f
     p = problem.c_struct()
     _check(_lib.og_int8_gemm_check_float(ctypes.byref(p), _buf(a), _buf(b), _buf(c), _opd(scale),
                                          _opd(zero_point_a), _opd(zero_point_b), _opd(float_bias), _opd(int_bias)))
+
+
+def check_dequantize(problem, a, b, c, a_scale, b_scale, zero_point_a=None, zero_point_b=None, float_bias=None,
+                     int_bias=None) -> None:
+    p = problem.c_struct()
+    _check(_lib.og_int8_gemm_check_dequantize(ctypes.byref(p), _buf(a), _buf(b), _buf(c), _opd(a_scale),
+                                              _opd(b_scale), _opd(zero_point_a), _opd(zero_point_b),
+                                              _opd(float_bias), _opd(int_bias)))
 
 
 def check_requantized(problem, a, b, y, multiplier, zero_point_y, zero_point_a=None, zero_point_b=None,

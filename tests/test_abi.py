@@ -111,6 +111,20 @@ def test_float_form_checks_int_bias_only_when_there_is_work():
         og.GpuKernelShapeException, "floatBias")
 
 
+def test_dequantize_form_checks():
+    """The fused MatMulIntegerToFloat form: EncodeFloat's checks plus a single-valued aScale."""
+    a, b, f = spec(U8, 64), spec(S8, 64), spec(F32, 64)
+    sa, sb = spec(F32, 1), spec(F32, 8)
+    og.check_dequantize(P(2, 8, 2), a, b, f, Op(sa, 0), Op(sb, 0, True))
+    shape = og.GpuKernelShapeException
+    assert argument_of(og.check_dequantize, P(2, 8, 2), a, b, f, Op(sa, 0, True), Op(sb, 0, True)) == (shape, "aScale")
+    assert argument_of(og.check_dequantize, P(2, 9, 2), a, b, f, Op(sa, 0), Op(sb, 0, True)) == (shape, "bScale")
+    assert argument_of(og.check_dequantize, P(2, 8, 2), a, b, f, Op(spec(I32, 1), 0), Op(sb, 0, True)) == (
+        shape, "aScale")
+    assert argument_of(og.check_dequantize, P(2, 8, 2), a, b, f, None, Op(sb, 0, True)) == (og.ArgumentNullException,
+                                                                                          "aScale")
+
+
 def test_scratch_that_is_too_small_is_refused():
     """Int8ScratchTests.cs:68-89."""
     a = spec(U8, 64 * 8 + 4)

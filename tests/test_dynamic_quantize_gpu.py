@@ -66,6 +66,48 @@ def test_dynamic_quantize_full_size(device, count):
                 v.dispose()
 
 
+@pytest.mark.parametrize("m,n,k,trans_b,options", [
+    (128, 384, 384, True, og.Int8GemmOptions()),
+    (128, 384, 384, True, og.Int8GemmOptions(allow_packed_dot=False)),
+    (16, 384, 384, False, og.Int8GemmOptions()),           # the few-rows kernel
+    (4096, 4096, 4096, False, og.Int8GemmOptions()),       # config 2 at full size, sampled rows checked
+])
+def test_dynamic_quantize_then_fused_dequantize_product(device, m, n, k, trans_b, options):
+    """The DynamicQuantizeLinear -> MatMulIntegerToFloat chain with the scale product formed in the epilogue:
+    expected (float)sum * (a_scale * b_scale[n]) with a per-column zero point of the weights."""
+    rng = np.random.default_rng(m + n + k)
+    x = rng.standard_normal(m * k).astype(np.float32)
+    wy, wscale, wzero = oracle.dynamic_quantize(x)
+    w = rng.integers(-127, 128, size=n * k).astype(np.int8)
+    zw = rng.integers(-8, 9, size=n).astype(np.int8)
+    bscale = rng.uniform(0.001, 0.02, size=n).astype(np.float32)
+    rows = np.arange(m) if m <= 128 else rng.choice(m, size=24, replace=False)
+    p = problem(m, n, k, trans_b=trans_b)
+    sums = oracle.int8_gemm(wy.reshape(m, k)[rows].reshape(-1), False, w.view(np.uint8), True,
+                            np.array([wzero], np.uint8), False, zw.view(np.uint8), True,
+                            **dict(oracle_shape(p), m=len(rows)))
+    scale_vec = (np.float32(wscale) * bscale).astype(np.float32)
+    want = (sums.astype(np.float32) * np.tile(scale_vec, len(rows))).astype(np.float32)
+    with og.DynamicQuantizeKernels(device) as dq, og.Int8Gemm(device, options) as gemm:
+        bx = device.create_buffer(np.float32, x)
+        by = device.create_buffer(np.uint8, m * k)
+        bs = device.create_buffer(np.float32, 1)
+        bz = device.create_buffer(np.uint8, 1)
+        bw = device.create_buffer(np.int8, w)
+        bzw = device.create_buffer(np.int8, zw)
+        bbs = device.create_buffer(np.float32, bscale)
+        bc = device.create_buffer(np.float32, m * n)
+        enc = device.begin_commands()
+        dq.encode(enc, bx, 0, m * k, by, 0, bs, 0, bz, 0)
+        gemm.encode_dequantize(enc, og.Int8GemmProblem(**p), by, bw, bc, og.Int8Operand(bs, 0),
+                               og.Int8Operand(bbs, 0, True), og.Int8Operand(bz, 0), og.Int8Operand(bzw, 0, True))
+        device.submit(enc)
+        got = bc.read().reshape(m, n)[rows].reshape(-1)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), gemm.last_kernel
+        for v in (bx, by, bs, bz, bw, bzw, bbs, bc):
+            v.dispose()
+
+
 def test_dynamic_quantize_feeds_the_product_without_leaving_the_device(device):
     """DynamicQuantizeFeedsTheProductWithoutLeavingTheDevice (Int8Tests.cs:705-751): quantize, then the float form
     with the activation's zero point read from the device; expected (float)sum * (a_scale * w_scale[n])."""

@@ -439,6 +439,7 @@ og::GemmLaunch make_launch(og_int8_gemm* g, const og_int8_gemm_problem* p, const
     e.zb_vector = zb ? zb->is_vector : 0;
     e.zb_signed = b->type == OG_S8;
     e.vec_ok = ((reinterpret_cast<uintptr_t>(e.c) & 15) == 0) && ((static_cast<int64_t>(p->n) * esize) % 16 == 0);
+    e.sum_splits = 1;
     return L;
 }
 
@@ -486,7 +487,11 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
     int32_t* rows = nullptr;
     int32_t* cols = nullptr;
     if (need_rows || need_cols) {
-        const int64_t need = (need_rows ? int64_t(ba) * L.m : 0) + (need_cols ? int64_t(bb) * L.n : 0);
+        // Up to 8 partial sums over K per row / column, so that the sums pass has enough CTAs (see byte_sum_splits).
+        const int splits = og::byte_sum_splits(L, 8);
+        const int64_t row_elems = need_rows ? int64_t(ba) * L.m : 0;
+        const int64_t col_elems = need_cols ? int64_t(bb) * L.n : 0;
+        const int64_t need = splits * (row_elems + col_elems);
         int32_t* base = nullptr;
         if (caller_scratch != nullptr &&
             caller_scratch->buffer.length - caller_scratch->offset >= need)
@@ -494,12 +499,18 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
         else
             base = own_scratch(g, need);
         rows = need_rows ? base : nullptr;
-        cols = need_cols ? base + (need_rows ? int64_t(ba) * L.m : 0) : nullptr;
+        cols = need_cols ? base + splits * row_elems : nullptr;
         L.epi.row_sum_a = rows;
         L.epi.row_sum_a_stride = ba > 1 ? L.m : 0;
         L.epi.col_sum_b = cols;
         L.epi.col_sum_b_stride = bb > 1 ? L.n : 0;
-        enc->ops.push_back([L, rows, cols](cudaStream_t s) { return og::launch_byte_sums(L, rows, cols, s); });
+        L.epi.sum_splits = splits;
+        L.epi.row_sum_split_stride = row_elems;
+        L.epi.col_sum_split_stride = col_elems;
+        cudaError_t err;
+        og::LaunchFn sums = og::prepare_byte_sums(L, rows, cols, splits, &err);
+        check_cuda(err, "Int8Gemm byte sums");
+        enc->ops.push_back(std::move(sums));
         enc->dispatches += 1;
     }
     cudaError_t err;
@@ -1151,6 +1162,9 @@ OG_API og_status og_int8_gemm_int32_noalloc(void* stream, const og_int8_gemm_pro
             e.row_sum_a_stride = ba > 1 ? L.m : 0;
             e.col_sum_b = cols ? d.sums + rows : nullptr;
             e.col_sum_b_stride = bb > 1 ? L.n : 0;
+            e.sum_splits = 1;  // launch_byte_sums writes whole sums
+            e.row_sum_split_stride = rows;
+            e.col_sum_split_stride = cols;
             check_cuda(og::launch_byte_sums(L, const_cast<int32_t*>(e.row_sum_a), const_cast<int32_t*>(e.col_sum_b), s),
                        "og_int8_gemm_int32_noalloc");
         }

@@ -72,10 +72,19 @@ __global__ void __launch_bounds__(DQ_THREADS)
     }
     const int64_t nvec = (count - head) / 4;
     const float4* xv = reinterpret_cast<const float4*>(x + head);
-    for (int64_t i = tid; i < nvec; i += nthreads) {
-        const float4 v = __ldg(xv + i);
-        mn = fminf(mn, fminf(fminf(v.x, v.y), fminf(v.z, v.w)));
-        mx = fmaxf(mx, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    constexpr int U = 4;  // loads in flight per thread
+    for (int64_t i0 = tid; i0 < nvec; i0 += nthreads * U) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int64_t i = i0 + u * nthreads;
+            v[u] = i < nvec ? __ldg(xv + i) : make_float4(NAN, NAN, NAN, NAN);  // NaN is skipped by fminf/fmaxf
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            mn = fminf(mn, fminf(fminf(v[u].x, v[u].y), fminf(v[u].z, v[u].w)));
+            mx = fmaxf(mx, fmaxf(fmaxf(v[u].x, v[u].y), fmaxf(v[u].z, v[u].w)));
+        }
     }
     for (int64_t i = head + nvec * 4 + tid; i < count; i += nthreads) {
         const float v = __ldg(x + i);

@@ -53,7 +53,19 @@ cudaError_t launch_gemm_simt(const GemmLaunch& L, cudaStream_t stream);
 
 // Byte sums for the zero-point correction (og_gemm_simt.cu): row sums of A ([batchA][M], batchA = batch when A has
 // its own stride, else 1) when `row_sums` is set, column sums of B ([batchB][N]) when `col_sums` is set.
+// With the tensor-core sums the K range may be split (at most `splits` ways, see byte_sum_splits): each split writes
+// its partial sums, [split][batch][M] and [split][batch][N], and the product's epilogue adds them up
+// (Epilogue::sum_splits). The scratch then holds splits * (batchA * M + batchB * N) int32.
+int byte_sum_splits(const GemmLaunch& L, int max_splits);
+LaunchFn prepare_byte_sums(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, int splits, cudaError_t* err);
 cudaError_t launch_byte_sums(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, cudaStream_t stream);
+cudaError_t launch_byte_sums_simt(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, cudaStream_t stream);
+// Sums over K of every column of a K x cols (k_major = false) or cols x K (k_major = true) byte matrix, through the
+// tensor cores (og_gemm_rows.cu), K split `splits` ways (partials at out + split * batches * cols).
+int sums_splits(int cols, int k, int batches, int num_sms, int max_splits);
+LaunchFn prepare_byte_sums_tc(const uint8_t* mat, int cols, int k, int64_t ld, int64_t bstride, int batches,
+                              bool k_major, bool is_signed, int32_t* out, int splits, int* error_flag,
+                              cudaError_t* err);
 
 // DynamicQuantizeLinear (og_dq.cu).
 struct DqScratch;

@@ -42,6 +42,11 @@ struct RowsParams {
     const uint8_t* a;
     Epilogue epi;
     int* error_flag;
+    // Sums-only mode: no product; the column sums of B over K go to sums_out[b * sums_stride + n].
+    int32_t* sums_out;
+    int64_t sums_stride;
+    int64_t sums_split_stride;  // between the partial sums of consecutive K splits (blockIdx.z)
+    int k_blocks_total;         // K blocks of the whole product; p.k_blocks is the share of one split
 };
 
 template <int OUT>
@@ -77,7 +82,10 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
     const int lane = threadIdx.x & 31;
     const int tile = blockIdx.x;
     const int b = blockIdx.y;
-    const bool need_col_sums = p.epi.za != nullptr;  // za * colsum(B)
+    const int kb_begin = blockIdx.z * p.k_blocks;  // K split of this CTA (one split outside the sums-only mode)
+    const int kb_count = min(p.k_blocks, p.k_blocks_total - kb_begin);
+    const bool sums_only = p.sums_out != nullptr;
+    const bool need_col_sums = sums_only || p.epi.za != nullptr;  // za * colsum(B)
 
     // The block of ones (any swizzle of all-ones bytes is all ones).
     for (int i = threadIdx.x; i < rows::ONES_BYTES / 16; i += blockDim.x)
@@ -108,22 +116,23 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
     const int bb = p.b_batched ? b : 0;
 
     if (warp == 0) {
-        for (int kb = 0; kb < p.k_blocks; kb++) {
+        for (int kb = 0; kb < kb_count; kb++) {
             const int s = kb % rows::STAGES;
             const uint32_t ph = (kb / rows::STAGES) & 1;
+            const int kc = (kb_begin + kb) * rows::BK;
             if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) goto done;
             if (lane == 0) {
-                mbar_arrive_expect_tx(&full[s], rows::B_BYTES + rows::A_BYTES);
+                mbar_arrive_expect_tx(&full[s], rows::B_BYTES + (sums_only ? 0 : rows::A_BYTES));
                 if constexpr (B_KMAJOR)
-                    tma_load_3d(sB + s * rows::B_BYTES, &tmap_b, &full[s], kb * rows::BK, tile * rows::BN, bb);
+                    tma_load_3d(sB + s * rows::B_BYTES, &tmap_b, &full[s], kc, tile * rows::BN, bb);
                 else
-                    tma_load_3d(sB + s * rows::B_BYTES, &tmap_b, &full[s], tile * rows::BN, kb * rows::BK, bb);
-                tma_load_3d(sX + s * rows::A_BYTES, &tmap_a, &full[s], kb * rows::BK, 0, ba);
+                    tma_load_3d(sB + s * rows::B_BYTES, &tmap_b, &full[s], tile * rows::BN, kc, bb);
+                if (!sums_only) tma_load_3d(sX + s * rows::A_BYTES, &tmap_a, &full[s], kc, 0, ba);
             }
             __syncwarp();
         }
     } else if (warp == 1) {
-        for (int kb = 0; kb < p.k_blocks; kb++) {
+        for (int kb = 0; kb < kb_count; kb++) {
             const int s = kb % rows::STAGES;
             const uint32_t ph = (kb / rows::STAGES) & 1;
             if (!mbar_wait(&full[s], ph, abort_flag)) goto done;
@@ -137,7 +146,7 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
                     const uint64_t adesc = B_KMAJOR ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
                                                     : smem_desc_sw128(b_addr + kk * 32 * 128, rows::B_BYTES, 1024);
                     const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
-                    mma_i8(tmem_base, adesc, smem_desc_sw128(x_addr + kk * 32, 16, 1024), idesc, acc);
+                    if (!sums_only) mma_i8(tmem_base, adesc, smem_desc_sw128(x_addr + kk * 32, 16, 1024), idesc, acc);
                     if (need_col_sums)
                         mma_i8(tmem_base + rows::MAXM, adesc, smem_desc_sw128(o_addr + kk * 32, 16, 1024), idesc, acc);
                 }
@@ -152,7 +161,7 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
         const Epilogue& e = p.epi;
         // Row sums of A over K while B streams (needed for the zero point of B). Eight consecutive threads own a row
         // (16 rows x 8 = the 128 epilogue threads) and read it in 16-byte chunks, 16 loads in flight per thread.
-        if (e.zb != nullptr) {
+        if (!sums_only && e.zb != nullptr) {
             const int t = threadIdx.x - 64;  // 0..127
             const int r = t >> 3, part = t & 7;
             int32_t sum = 0;
@@ -201,7 +210,9 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16), r);
         tmem_ld_wait();
         const int n = tile * rows::BN + q * 32 + lane;
-        if (n < p.n) {
+        if (sums_only) {
+            if (n < p.n) p.sums_out[blockIdx.z * p.sums_split_stride + b * p.sums_stride + n] = static_cast<int32_t>(r[16]);
+        } else if (n < p.n) {
             const uint32_t csb = r[16];  // sum over K of B[k, n]
             const int32_t zb = zp_value(e.zb, e.zb_vector, e.zb_signed, n);
             const uint32_t bias = e.int_bias ? static_cast<uint32_t>(__ldg(e.int_bias + n)) : 0u;
@@ -234,6 +245,18 @@ done:
 
 bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint64_t stride_y,
                         uint64_t stride_z, uint32_t box_x, uint32_t box_y);
+
+// How many K splits the sums-only launch over `cols` columns and `batches` batches uses: enough CTAs for two per SM,
+// at most `max_splits`, and never an empty split.
+int sums_splits(int cols, int k, int batches, int num_sms, int max_splits) {
+    const int tiles = (cols + rows::BN - 1) / rows::BN * batches;
+    const int kb = (k + rows::BK - 1) / rows::BK;
+    int s = (2 * num_sms + tiles - 1) / tiles;
+    s = s < 1 ? 1 : (s > max_splits ? max_splits : s);
+    s = s > kb ? kb : s;
+    const int per = (kb + s - 1) / s;
+    return (kb + per - 1) / per;
+}
 
 bool rows_eligible(const GemmLaunch& L) {
     return L.m >= 1 && L.m <= rows::MAXM && L.batch <= 65535 && tc_eligible(L);
@@ -286,6 +309,10 @@ LaunchFn prepare_gemm_rows(const GemmLaunch& L, cudaError_t* err) {
     p.a = L.a;
     p.epi = L.epi;
     p.error_flag = L.error_flag;
+    p.sums_out = nullptr;
+    p.sums_stride = 0;
+    p.sums_split_stride = 0;
+    p.k_blocks_total = p.k_blocks;
     // The MMA's A operand is B (its type, MN-major unless B is stored N x K); its B operand is A (or the ones).
     const uint32_t idesc = idesc_i8(L.b_signed, L.a_signed, !L.trans_b, false, rows::BN, rows::MAXM);
     const dim3 grid((L.n + rows::BN - 1) / rows::BN, L.batch);
@@ -300,6 +327,37 @@ LaunchFn prepare_gemm_rows(const GemmLaunch& L, cudaError_t* err) {
         default: return km ? bind_rows_t<true, OUT_S8>(p, ma, mb, grid, idesc)
                            : bind_rows_t<false, OUT_S8>(p, ma, mb, grid, idesc);
     }
+}
+
+// Byte sums over K of every column of a matrix, with the few-rows kernel in its sums-only mode (the block of ones
+// times the matrix): `mat` is K x cols with columns contiguous (k_major = false; B) or cols x K with K contiguous
+// (k_major = true; the rows of A, or a B stored N x K). One result per column and batch, written (no accumulation).
+LaunchFn prepare_byte_sums_tc(const uint8_t* mat, int cols, int k, int64_t ld, int64_t bstride, int batches,
+                              bool k_major, bool is_signed, int32_t* out, int splits, int* error_flag, cudaError_t* err) {
+    *err = cudaErrorInvalidValue;
+    CUtensorMap mb;
+    const uint64_t rows_stored = k_major ? cols : k;
+    const uint64_t sb = batches > 1 ? uint64_t(bstride) : (uint64_t(ld) * rows_stored + 15) & ~uint64_t(15);
+    const bool ok = k_major ? make_tensor_map_u8(&mb, mat, k, cols, batches, ld, sb, rows::BK, rows::BN)
+                            : make_tensor_map_u8(&mb, mat, cols, k, batches, ld, sb, rows::BN, rows::BK);
+    if (!ok) return nullptr;
+    *err = cudaSuccess;
+    RowsParams p = {};
+    p.m = 0;
+    p.n = cols;
+    p.k = k;
+    p.k_blocks_total = (k + rows::BK - 1) / rows::BK;
+    p.k_blocks = (p.k_blocks_total + splits - 1) / splits;  // every split gets at least one K block (see sums_splits)
+    p.a_batched = 0;
+    p.b_batched = batches > 1;
+    p.error_flag = error_flag;
+    p.sums_out = out;
+    p.sums_stride = cols;
+    p.sums_split_stride = int64_t(batches) * cols;
+    const uint32_t idesc = idesc_i8(is_signed, false, !k_major, false, rows::BN, rows::MAXM);
+    const dim3 grid((cols + rows::BN - 1) / rows::BN, batches, splits);
+    return k_major ? bind_rows_t<true, OUT_I32>(p, mb, mb, grid, idesc)
+                   : bind_rows_t<false, OUT_I32>(p, mb, mb, grid, idesc);
 }
 
 cudaError_t launch_gemm_rows(const GemmLaunch& L, cudaStream_t stream) {

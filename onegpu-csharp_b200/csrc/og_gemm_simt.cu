@@ -136,8 +136,22 @@ cudaError_t launch_gemm_simt(const GemmLaunch& L, cudaStream_t stream) {
 
 // ---- byte sums ---------------------------------------------------------------------------------------------------
 
-// One warp per row: sum of `len` bytes of row r of batch bt at base + bt * bstride + r * ld. 16-byte loads and a
-// packed dot with 0x01010101 when the row is aligned, bytes otherwise.
+__device__ __forceinline__ int32_t byte_sum16(const uint4& w, int is_signed, int32_t s) {
+    if (is_signed) {
+        s = __dp4a(static_cast<int>(w.x), 0x01010101, s);
+        s = __dp4a(static_cast<int>(w.y), 0x01010101, s);
+        s = __dp4a(static_cast<int>(w.z), 0x01010101, s);
+        return __dp4a(static_cast<int>(w.w), 0x01010101, s);
+    }
+    unsigned u = static_cast<unsigned>(s);
+    u = __dp4a(w.x, 0x01010101u, u);
+    u = __dp4a(w.y, 0x01010101u, u);
+    u = __dp4a(w.z, 0x01010101u, u);
+    return static_cast<int32_t>(__dp4a(w.w, 0x01010101u, u));
+}
+
+// One warp per row: sum of `len` bytes of row r of batch bt at base + bt * bstride + r * ld. 16-byte loads, eight in
+// flight per lane, and a packed dot with 0x01010101 when the row is aligned; bytes otherwise.
 __global__ void row_sums_kernel(const uint8_t* __restrict__ base, int rows, int len, int64_t ld, int64_t bstride,
                                 int batches, int is_signed, int32_t* __restrict__ out) {
     const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -151,21 +165,16 @@ __global__ void row_sums_kernel(const uint8_t* __restrict__ base, int rows, int 
     if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
         const int vec = len >> 4;
         const uint4* v = reinterpret_cast<const uint4*>(row);
-        for (int i = lane; i < vec; i += 32) {
-            const uint4 w = __ldg(v + i);
-            if (is_signed) {
-                s = __dp4a(static_cast<int>(w.x), 0x01010101, s);
-                s = __dp4a(static_cast<int>(w.y), 0x01010101, s);
-                s = __dp4a(static_cast<int>(w.z), 0x01010101, s);
-                s = __dp4a(static_cast<int>(w.w), 0x01010101, s);
-            } else {
-                unsigned u = static_cast<unsigned>(s);
-                u = __dp4a(w.x, 0x01010101u, u);
-                u = __dp4a(w.y, 0x01010101u, u);
-                u = __dp4a(w.z, 0x01010101u, u);
-                u = __dp4a(w.w, 0x01010101u, u);
-                s = static_cast<int32_t>(u);
+        constexpr int U = 8;
+        for (int i0 = lane; i0 < vec; i0 += 32 * U) {
+            uint4 w[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int i = i0 + 32 * u;
+                w[u] = i < vec ? __ldg(v + i) : make_uint4(0, 0, 0, 0);
             }
+#pragma unroll
+            for (int u = 0; u < U; u++) s = byte_sum16(w[u], is_signed, s);
         }
         start = vec << 4;
     }
@@ -175,42 +184,126 @@ __global__ void row_sums_kernel(const uint8_t* __restrict__ base, int rows, int 
     if (lane == 0) out[warp_id] = s;
 }
 
-// Column sums of a K x N row-major byte matrix (columns contiguous): each thread owns four adjacent columns of a
-// slab of K rows; slabs add into the zeroed output with integer atomics (exact in any order).
-__global__ void col_sums_kernel(const uint8_t* __restrict__ base, int n, int k, int64_t ld, int64_t bstride,
-                                int is_signed, int rows_per_block, int32_t* __restrict__ out) {
+// Column sums of a K x N row-major byte matrix (columns contiguous). A block of 8 warps owns 512 adjacent columns
+// (16 per lane, one 16-byte load per row) and a slab of rows that its warps share out; the warps' sums meet in
+// shared memory and each block adds its 512 results into the zeroed output with integer atomics (exact in any
+// order). Columns that are not 16-byte aligned take byte loads.
+constexpr int COLS_PER_BLOCK = 512;
+
+__global__ void __launch_bounds__(256) col_sums_kernel(const uint8_t* __restrict__ base, int n, int k, int64_t ld,
+                                                       int64_t bstride, int is_signed, int rows_per_block,
+                                                       int32_t* __restrict__ out) {
+    __shared__ int32_t part[8][COLS_PER_BLOCK + 1];
     const int bt = blockIdx.z;
-    const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
-    if (c0 >= n) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c0 = blockIdx.x * COLS_PER_BLOCK + lane * 16;
     const int k_begin = blockIdx.y * rows_per_block;
     const int k_end = min(k, k_begin + rows_per_block);
     const uint8_t* mat = base + bt * bstride;
-    int32_t s0 = 0, s1 = 0, s2 = 0, s3 = 0;
-    const bool four = c0 + 4 <= n;
-    const bool aligned = four && ((reinterpret_cast<uintptr_t>(mat + c0) | static_cast<uintptr_t>(ld)) & 3) == 0;
-    for (int kk = k_begin; kk < k_end; kk++) {
-        const uint8_t* p = mat + static_cast<int64_t>(kk) * ld + c0;
-        if (aligned) {
-            const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(p));
-            s0 += byte_val(w & 0xFF, is_signed);
-            s1 += byte_val((w >> 8) & 0xFF, is_signed);
-            s2 += byte_val((w >> 16) & 0xFF, is_signed);
-            s3 += byte_val(w >> 24, is_signed);
-        } else {
-            s0 += byte_val(__ldg(p), is_signed);
-            if (c0 + 1 < n) s1 += byte_val(__ldg(p + 1), is_signed);
-            if (c0 + 2 < n) s2 += byte_val(__ldg(p + 2), is_signed);
-            if (c0 + 3 < n) s3 += byte_val(__ldg(p + 3), is_signed);
+    int32_t s[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) s[j] = 0;
+    const bool vec = c0 + 16 <= n && ((reinterpret_cast<uintptr_t>(mat + c0) | static_cast<uintptr_t>(ld)) & 15) == 0;
+    if (vec) {
+        constexpr int U = 4;
+        for (int k0 = k_begin + warp; k0 < k_end; k0 += 8 * U) {
+            uint4 w[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int kk = k0 + 8 * u;
+                w[u] = kk < k_end ? __ldg(reinterpret_cast<const uint4*>(mat + static_cast<int64_t>(kk) * ld + c0))
+                                  : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+                for (int q = 0; q < 4; q++)
+#pragma unroll
+                    for (int t = 0; t < 4; t++) s[4 * q + t] += byte_val((ws[q] >> (8 * t)) & 0xFF, is_signed);
+            }
+        }
+    } else if (c0 < n) {
+        for (int kk = k_begin + warp; kk < k_end; kk += 8) {
+            const uint8_t* p = mat + static_cast<int64_t>(kk) * ld + c0;
+#pragma unroll
+            for (int j = 0; j < 16; j++)
+                if (c0 + j < n) s[j] += byte_val(__ldg(p + j), is_signed);
         }
     }
-    int32_t* o = out + static_cast<int64_t>(bt) * n + c0;
-    atomicAdd(o, s0);
-    if (c0 + 1 < n) atomicAdd(o + 1, s1);
-    if (c0 + 2 < n) atomicAdd(o + 2, s2);
-    if (c0 + 3 < n) atomicAdd(o + 3, s3);
+#pragma unroll
+    for (int j = 0; j < 16; j++) part[warp][lane * 16 + j] = s[j];
+    __syncthreads();
+    for (int j = threadIdx.x; j < COLS_PER_BLOCK; j += blockDim.x) {
+        const int col = blockIdx.x * COLS_PER_BLOCK + j;
+        if (col >= n) continue;
+        int32_t t = 0;
+#pragma unroll
+        for (int w8 = 0; w8 < 8; w8++) t += part[w8][j];
+        atomicAdd(out + static_cast<int64_t>(bt) * n + col, t);
+    }
+}
+
+// The byte sums through the tensor cores (the few-rows kernel's sums-only mode: a block of ones times the matrix),
+// which stream the operand at TMA speed and write each sum once; the SIMT kernels below are the path for operands
+// TMA cannot load and for more than 65535 batches.
+static bool sums_on_tensor_cores(const GemmLaunch& L) {
+    const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
+    const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
+    return tc_eligible(L) && ba <= 65535 && bb <= 65535;
+}
+
+int byte_sum_splits(const GemmLaunch& L, int max_splits) {
+    if (!sums_on_tensor_cores(L)) return 1;
+    const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
+    const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
+    const int sa = L.epi.zb != nullptr ? sums_splits(L.m, L.k, ba, L.num_sms, max_splits) : 1;
+    const int sb = L.epi.za != nullptr ? sums_splits(L.n, L.k, bb, L.num_sms, max_splits) : 1;
+    // One count for both operands (they share K, so neither gets an empty split).
+    const int kb = (L.k + 127) / 128;
+    const int s = sa > sb ? sa : sb;
+    const int per = (kb + s - 1) / s;
+    return (kb + per - 1) / per;
+}
+
+LaunchFn prepare_byte_sums(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, int splits, cudaError_t* err) {
+    *err = cudaSuccess;
+    const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
+    const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
+    if (!sums_on_tensor_cores(L)) {
+        if (splits != 1) {
+            *err = cudaErrorInvalidValue;
+            return nullptr;
+        }
+        return [L, row_sums, col_sums](cudaStream_t s) { return launch_byte_sums_simt(L, row_sums, col_sums, s); };
+    }
+    LaunchFn rows_fn, cols_fn;
+    if (row_sums != nullptr) {
+        rows_fn = prepare_byte_sums_tc(L.a, L.m, L.k, L.lda, L.stride_a, ba, true, L.a_signed, row_sums, splits,
+                                       L.error_flag, err);
+        if (!rows_fn) return nullptr;
+    }
+    if (col_sums != nullptr) {
+        cols_fn = prepare_byte_sums_tc(L.b, L.n, L.k, L.ldb, L.stride_b, bb, L.trans_b != 0, L.b_signed, col_sums,
+                                       splits, L.error_flag, err);
+        if (!cols_fn) return nullptr;
+    }
+    return [rows_fn, cols_fn](cudaStream_t s) -> cudaError_t {
+        if (rows_fn) {
+            const cudaError_t e = rows_fn(s);
+            if (e != cudaSuccess) return e;
+        }
+        return cols_fn ? cols_fn(s) : cudaSuccess;
+    };
 }
 
 cudaError_t launch_byte_sums(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, cudaStream_t stream) {
+    cudaError_t err;
+    LaunchFn fn = prepare_byte_sums(L, row_sums, col_sums, 1, &err);
+    return fn ? fn(stream) : err;
+}
+
+cudaError_t launch_byte_sums_simt(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, cudaStream_t stream) {
     const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
     const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
     if (row_sums != nullptr) {
@@ -230,12 +323,12 @@ cudaError_t launch_byte_sums(const GemmLaunch& L, int32_t* row_sums, int32_t* co
         } else {
             cudaError_t err = cudaMemsetAsync(col_sums, 0, sizeof(int32_t) * static_cast<size_t>(L.n) * bb, stream);
             if (err != cudaSuccess) return err;
-            const int col_blocks = (L.n + 1023) / 1024;
-            // Enough slabs of K to give every SM a few blocks.
+            const int col_blocks = (L.n + COLS_PER_BLOCK - 1) / COLS_PER_BLOCK;
+            // Enough slabs of K to give every SM a few blocks, each slab at least 64 rows (8 per warp).
             int slabs = (4 * L.num_sms + col_blocks * bb - 1) / (col_blocks * bb);
             if (slabs < 1) slabs = 1;
             int rows_per_block = (L.k + slabs - 1) / slabs;
-            if (rows_per_block < 16) rows_per_block = 16;
+            if (rows_per_block < 64) rows_per_block = 64;
             slabs = (L.k + rows_per_block - 1) / rows_per_block;
             if (slabs > 65535) {
                 slabs = 65535;

@@ -92,7 +92,7 @@ __device__ __forceinline__ void fill_col_terms(ColTerms& t, const Epilogue& e, i
     for (int j = tid; j < tc::BN; j += nthreads) {
         const int n = col0 + j;
         const bool ok = n < e.n;
-        const int32_t csb = (ok && e.za != nullptr) ? __ldg(e.col_sum_b + b * e.col_sum_b_stride + n) : 0;
+        const int32_t csb = (ok && e.za != nullptr) ? static_cast<int32_t>(col_sum_of(e, b, n)) : 0;
         const int32_t bias = (ok && e.int_bias != nullptr) ? __ldg(e.int_bias + n) : 0;
         t.zb[j] = ok ? zp_value(e.zb, e.zb_vector, e.zb_signed, n) : 0;
         t.csb[j] = csb;
@@ -354,8 +354,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             uint32_t za = 0, rt = 0;  // zero point of A for this row, and K * za - rowsumA
             if (row_ok && terms) {
                 za = static_cast<uint32_t>(zp_value(e.za, e.za_vector, e.za_signed, m));
-                const uint32_t rsa = e.row_sum_a ? static_cast<uint32_t>(__ldg(e.row_sum_a + b * e.row_sum_a_stride + m))
-                                                 : 0u;
+                const uint32_t rsa = e.row_sum_a ? row_sum_of(e, b, m) : 0u;
                 rt = static_cast<uint32_t>(p.k) * za - rsa;
             }
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * tc::BN;

@@ -27,6 +27,9 @@ struct Epilogue {
     int64_t row_sum_a_stride;     // M, or 0 when every batch shares A
     const int32_t* col_sum_b;     // [batchB][N] byte sums of B, or null when no zero point of A is present
     int64_t col_sum_b_stride;     // N, or 0 when every batch shares B
+    int sum_splits;               // the sums are this many partial sums over K ranges, to be added up
+    int64_t row_sum_split_stride; // batchA * M
+    int64_t col_sum_split_stride; // batchB * N
     const int32_t* int_bias;      // per column, or null
     const float* scale;           // float form: scale; requantized form: multiplier
     int scale_vector;
@@ -42,32 +45,18 @@ __device__ __forceinline__ int32_t zp_value(const uint8_t* z, int vector, int is
     return is_signed ? static_cast<int32_t>(static_cast<int8_t>(v)) : static_cast<int32_t>(v);
 }
 
-// Row-dependent part of the correction for row m of batch b: returns za[m] and the row's byte sum.
-struct RowTerms {
-    int32_t za;
-    int32_t rsa;
-};
-
-__device__ __forceinline__ RowTerms row_terms(const Epilogue& e, int b, int m) {
-    RowTerms t;
-    t.za = zp_value(e.za, e.za_vector, e.za_signed, m);
-    t.rsa = e.row_sum_a ? __ldg(e.row_sum_a + b * e.row_sum_a_stride + m) : 0;
-    return t;
+// The byte sum of row m of A (batch b) and of column n of B: the partial sums of the K splits added up (wrapping).
+__device__ __forceinline__ uint32_t row_sum_of(const Epilogue& e, int b, int m) {
+    uint32_t s = 0;
+    for (int i = 0; i < e.sum_splits; i++)
+        s += static_cast<uint32_t>(__ldg(e.row_sum_a + i * e.row_sum_split_stride + b * e.row_sum_a_stride + m));
+    return s;
 }
 
-// The corrected int32 sum of one element (wrapping arithmetic in uint32).
-__device__ __forceinline__ uint32_t corrected(const Epilogue& e, const RowTerms& rt, int b, int n, uint32_t dot) {
-    uint32_t s = dot;
-    if (e.zb != nullptr) {
-        const int32_t zb = zp_value(e.zb, e.zb_vector, e.zb_signed, n);
-        s -= static_cast<uint32_t>(zb) * static_cast<uint32_t>(rt.rsa);
-        s += static_cast<uint32_t>(e.k) * static_cast<uint32_t>(rt.za) * static_cast<uint32_t>(zb);
-    }
-    if (e.za != nullptr) {
-        const int32_t csb = __ldg(e.col_sum_b + b * e.col_sum_b_stride + n);
-        s -= static_cast<uint32_t>(rt.za) * static_cast<uint32_t>(csb);
-    }
-    if (e.int_bias != nullptr) s += static_cast<uint32_t>(__ldg(e.int_bias + n));
+__device__ __forceinline__ uint32_t col_sum_of(const Epilogue& e, int b, int n) {
+    uint32_t s = 0;
+    for (int i = 0; i < e.sum_splits; i++)
+        s += static_cast<uint32_t>(__ldg(e.col_sum_b + i * e.col_sum_split_stride + b * e.col_sum_b_stride + n));
     return s;
 }
 

@@ -44,8 +44,11 @@ struct Cfg {
     static constexpr int B_BYTES = B_COLS * BK;       // 32 KB or 16 KB per CTA
     static constexpr int B_BOX = 128 * BK;            // one 128-column box of an MN-major B
     static constexpr int STAGES = CG == 1 ? 4 : 6;
-    static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024 /* alignment */ + 256 /* barriers */ +
-                                      5 * 4 * BN /* per-column epilogue terms */;
+    static constexpr int TERMS_BYTES = 5 * 4 * BN;     // per-column epilogue terms
+    static constexpr int BOX_BYTES = 32 * 128;          // one 32-row x 32-word store box
+    static constexpr int STAGING_BYTES = 4 * BOX_BYTES; // one box per epilogue warp
+    static constexpr int SMEM_BYTES =
+        STAGES * (A_BYTES + B_BYTES) + STAGING_BYTES + 1024 /* alignment */ + 256 /* barriers */ + TERMS_BYTES;
 };
 }  // namespace tc
 
@@ -58,6 +61,7 @@ struct TcParams {
     int total_tiles;
     Epilogue epi;
     int* error_flag;
+    int tma_store;  // int32 / float results leave through shared memory and TMA stores (C rows 16-byte aligned)
 };
 
 template <int BM>
@@ -133,6 +137,26 @@ __device__ __forceinline__ uint32_t finish_word(const ColTerms& t, const Epilogu
     }
 }
 
+// Finishes 32 consecutive int32 / float results of one row (tile columns j0..) and writes them as row `lane` of a
+// 32 x 32-word box in 128-byte-swizzled shared memory: 16-byte chunk j of the row lands at chunk j ^ (lane % 8), so the
+// eight lanes of each store phase hit eight different bank groups.
+template <int OUT>
+__device__ __forceinline__ void stage_chunk(const ColTerms& t, const Epilogue& e, bool terms, bool za_per_row,
+                                            uint32_t za, uint32_t rt, int j0, const uint32_t (&r)[32], uint8_t* box,
+                                            int lane) {
+    uint32_t w[32];
+#pragma unroll
+    for (int q = 0; q < 32; q++) w[q] = finish_word<OUT>(t, e, terms, za_per_row, za, rt, j0 + q, r[q]);
+    const uint32_t row = smem_u32(box) + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const uint32_t addr = row + ((j ^ (lane & 7)) << 4);
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * j]), "r"(w[4 * j + 1]),
+                     "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
+                     : "memory");
+    }
+}
+
 // Stores 32 consecutive results of row m (columns n0.. of the output; j0 is n0's column within the tile).
 template <int OUT>
 __device__ __forceinline__ void store_chunk(const ColTerms& t, const Epilogue& e, bool terms, bool za_per_row,
@@ -184,14 +208,15 @@ __device__ __forceinline__ void store_chunk(const ColTerms& t, const Epilogue& e
 }
 
 template <int CG, bool B_MN, int OUT>
-__device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const TcParams& p,
-                                             uint32_t idesc) {
+__device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
+                                             const CUtensorMap& tmap_c, const TcParams& p, uint32_t idesc) {
     using C = tc::Cfg<CG>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sB + C::STAGES * C::B_BYTES);
+    uint8_t* staging = sB + C::STAGES * C::B_BYTES;  // 1024-byte aligned store boxes of the epilogue warps
+    uint64_t* bars = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + C::STAGES;
     uint64_t* tfull = bars + 2 * C::STAGES;
@@ -222,6 +247,9 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
     }
+    constexpr bool WORDS = OUT == OUT_I32 || OUT == OUT_F32;
+    const bool tma_store = WORDS && p.tma_store;
+    if (tma_store && warp == 2 && lane == 0) prefetch_tmap(&tmap_c);
     if (warp == 1) {
         if constexpr (CG == 2) {
             tmem_alloc_pair(tmem_holder, tc::TMEM_COLS);
@@ -358,14 +386,38 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                 rt = static_cast<uint32_t>(p.k) * za - rsa;
             }
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * tc::BN;
+            if (tma_store) {
+                // Each 32 x 32 chunk goes through this warp's box and leaves as one TMA store of full 128-byte row
+                // segments; rows past M and columns past N are clipped by the tensor map.
+                uint8_t* box = staging + q * C::BOX_BYTES;
+                const int box_row = tm * C::BM + static_cast<int>(rank) * 128 + q * 32;
 #pragma unroll 1
-            for (int c = 0; c < tc::BN / 32; c++) {
-                const int n0 = tn * tc::BN + c * 32;
-                if (n0 >= p.n) break;
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(t_row + c * 32, r);
-                tmem_ld_wait();
-                if (row_ok) store_chunk<OUT>(terms_smem, e, terms, za_per_row, za, rt, b, m, n0, c * 32, r);
+                for (int c = 0; c < tc::BN / 32; c++) {
+                    const int n0 = tn * tc::BN + c * 32;
+                    if (n0 >= p.n || box_row >= p.m) break;  // boxes start inside C
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_row + c * 32, r);
+                    tmem_ld_wait();
+                    if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the box
+                    __syncwarp();
+                    stage_chunk<OUT>(terms_smem, e, terms, za_per_row, za, rt, c * 32, r, box, lane);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_3d(&tmap_c, box, n0, box_row, b);
+                        bulk_commit_group();
+                    }
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < tc::BN / 32; c++) {
+                    const int n0 = tn * tc::BN + c * 32;
+                    if (n0 >= p.n) break;
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_row + c * 32, r);
+                    tmem_ld_wait();
+                    if (row_ok) store_chunk<OUT>(terms_smem, e, terms, za_per_row, za, rt, b, m, n0, c * 32, r);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -379,6 +431,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
     }
 
 done:
+    if (tma_store && warp >= 2 && lane == 0) bulk_wait_group_all();  // stores finished before shared memory goes
     __syncthreads();
     if constexpr (CG == 2) cluster_sync_all();  // neither CTA frees the pair's TMEM while the other still reads it
     if (warp == 1) {
@@ -394,15 +447,15 @@ done:
 template <bool B_MN, int OUT>
 __global__ void __launch_bounds__(tc::THREADS, 1)
     int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                        const TcParams p, uint32_t idesc) {
-    gemm_tc_body<1, B_MN, OUT>(tmap_a, tmap_b, p, idesc);
+                        const __grid_constant__ CUtensorMap tmap_c, const TcParams p, uint32_t idesc) {
+    gemm_tc_body<1, B_MN, OUT>(tmap_a, tmap_b, tmap_c, p, idesc);
 }
 
 template <bool B_MN, int OUT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::THREADS, 1)
     int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                         const TcParams p, uint32_t idesc) {
-    gemm_tc_body<2, B_MN, OUT>(tmap_a, tmap_b, p, idesc);
+                         const __grid_constant__ CUtensorMap tmap_c, const TcParams p, uint32_t idesc) {
+    gemm_tc_body<2, B_MN, OUT>(tmap_a, tmap_b, tmap_c, p, idesc);
 }
 
 // ---- host side ---------------------------------------------------------------------------------------------------
@@ -431,6 +484,21 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y,
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// The output C as a 3-D tensor of 4-byte words (columns innermost) stored in 32 x 32-word boxes from 128-byte-swizzled
+// shared memory.
+static bool make_store_map(CUtensorMap* map, void* base, uint64_t n, uint64_t m, uint64_t batch, uint64_t row_bytes,
+                           uint64_t batch_bytes) {
+    auto fn = encode_fn();
+    if (fn == nullptr) return false;
+    cuuint64_t dims[3] = {n, m, batch};
+    cuuint64_t strides[2] = {row_bytes, batch_bytes};
+    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -469,7 +537,7 @@ static cudaError_t configure(K kern, int smem, uint64_t& configured) {
 // device) and launches.
 template <int CG, bool B_MN, int OUT>
 static LaunchFn bind_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensorMap& ma, const CUtensorMap& mb,
-                          int grid) {
+                          const CUtensorMap& mc, int grid) {
     using C = tc::Cfg<CG>;
     const uint32_t idesc = idesc_i8(L.a_signed, L.b_signed, false, B_MN, C::BM, tc::BN);
     return [=](cudaStream_t stream) -> cudaError_t {
@@ -478,12 +546,12 @@ static LaunchFn bind_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensor
             auto kern = int8_gemm_tc2_kernel<B_MN, OUT>;
             cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
             if (e != cudaSuccess) return e;
-            kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
+            kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, mc, p, idesc);
         } else {
             auto kern = int8_gemm_tc_kernel<B_MN, OUT>;
             cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
             if (e != cudaSuccess) return e;
-            kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
+            kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, mc, p, idesc);
         }
         return cudaGetLastError();
     };
@@ -523,18 +591,27 @@ static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
     p.total_tiles = static_cast<int>(total);
     p.epi = L.epi;
     p.error_flag = L.error_flag;
+    // int32 / float results go out through TMA stores when C's rows (and batches) start on 16-byte boundaries.
+    CUtensorMap mc;
+    std::memset(&mc, 0, sizeof(mc));
+    const bool words = L.epi.out_kind == OUT_I32 || L.epi.out_kind == OUT_F32;
+    const bool c_aligned = (reinterpret_cast<uintptr_t>(L.epi.c) & 15) == 0 && (L.epi.ldc & 3) == 0 &&
+                           (L.batch == 1 || (L.epi.batch_stride_c & 3) == 0);
+    p.tma_store = words && c_aligned &&
+                  make_store_map(&mc, L.epi.c, L.n, L.m, L.batch, uint64_t(L.epi.ldc) * 4,
+                                 L.batch > 1 ? uint64_t(L.epi.batch_stride_c) * 4 : round16(uint64_t(L.epi.ldc) * 4 * L.m));
     const int64_t workers = L.num_sms / CG;
     const int grid = static_cast<int>((total < workers ? total : workers) * CG);
     const bool bmn = !L.trans_b;
     switch (L.epi.out_kind) {
-        case OUT_I32: return bmn ? bind_tc_t<CG, true, OUT_I32>(L, p, ma, mb, grid)
-                                 : bind_tc_t<CG, false, OUT_I32>(L, p, ma, mb, grid);
-        case OUT_F32: return bmn ? bind_tc_t<CG, true, OUT_F32>(L, p, ma, mb, grid)
-                                 : bind_tc_t<CG, false, OUT_F32>(L, p, ma, mb, grid);
-        case OUT_U8: return bmn ? bind_tc_t<CG, true, OUT_U8>(L, p, ma, mb, grid)
-                                : bind_tc_t<CG, false, OUT_U8>(L, p, ma, mb, grid);
-        default: return bmn ? bind_tc_t<CG, true, OUT_S8>(L, p, ma, mb, grid)
-                            : bind_tc_t<CG, false, OUT_S8>(L, p, ma, mb, grid);
+        case OUT_I32: return bmn ? bind_tc_t<CG, true, OUT_I32>(L, p, ma, mb, mc, grid)
+                                 : bind_tc_t<CG, false, OUT_I32>(L, p, ma, mb, mc, grid);
+        case OUT_F32: return bmn ? bind_tc_t<CG, true, OUT_F32>(L, p, ma, mb, mc, grid)
+                                 : bind_tc_t<CG, false, OUT_F32>(L, p, ma, mb, mc, grid);
+        case OUT_U8: return bmn ? bind_tc_t<CG, true, OUT_U8>(L, p, ma, mb, mc, grid)
+                                : bind_tc_t<CG, false, OUT_U8>(L, p, ma, mb, mc, grid);
+        default: return bmn ? bind_tc_t<CG, true, OUT_S8>(L, p, ma, mb, mc, grid)
+                            : bind_tc_t<CG, false, OUT_S8>(L, p, ma, mb, mc, grid);
     }
 }
 

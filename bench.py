@@ -5,9 +5,10 @@
 One step is one Int8Gemm.EncodeInt32 + Submit of the workload (config 3 by default: A int8 [8192 x 8192] x B int8
 [8192 x 8192], zero points absent, int32 C) with inputs resident in HBM; L2 is flushed (a 512 MB write) before every
 step and the step itself is timed with CUDA events on the device stream. With N > 1 (torchrun, one process per GPU,
-NCCL only for the barrier and the max-over-ranks of the times) the product is N-sharded: rank g computes the columns
-[g N/G, (g+1) N/G) from the full A and its slab of B, with no collective in the data path ("strong" scaling: the
-total work is fixed). `e2e` runs the same product through the C ABI from pinned host buffers (uploads of A and the B
+NCCL only for the barrier and the max-over-ranks of the times) the product is sharded by onegpu_cuda.shard with no
+collective in the data path ("strong" scaling: the total work is fixed): a batched workload by batch (rank g computes
+its batches from its batches of A and the shared B), the others by 256-column slabs of B (rank g computes its columns
+from the full A and its slab of B). `e2e` runs the same product through the C ABI from pinned host buffers (uploads of A and the B
 slab, the product, readback of C), timed on the device. `--impl reference` times the CPU restatement of the
 reference's int8 product (oracle/, all host threads) on a bounded row sample of the same workload.
 """
@@ -179,22 +180,33 @@ def run_reference(args, rank: int, world: int):
 def run_ours(args, rank: int, world: int, local_rank: int, dist):
     import onegpu_cuda as og
 
+    from onegpu_cuda import shard as sh
+
     w = WORKLOADS[args.workload]
     dev = og.GpuDevice(local_rank)
     M, N, K, B = w["m"], w["n"], w["k"], w["batch"]
-    shard_n = N // world
-    n0 = rank * shard_n
+    # Batched products are split by batch (B shared), the others by 256-column slabs of B.
+    by_batch = B > 1
+    extent, align = (B, 1) if by_batch else (N, sh.TILE_COLUMNS)
+    if min(s.width for s in sh.split(extent, world, align)) == 0:  # decided alike on every rank
+        raise SystemExit(f"{args.workload} has fewer shards than the {world} ranks")
+    part = sh.shard_of(extent, world, rank, align)
+    shard_n = N if by_batch else part.width
+    B_local = part.width if by_batch else B
     rng = np.random.default_rng(1234)
     a_dtype = np.int8 if w["a_signed"] else np.uint8
-    # Synthetic inputs with the config's distributions, generated on the host once.
-    a_host = rng.integers(-128 if w["a_signed"] else 0, 128 if w["a_signed"] else 256, size=B * M * K,
+    # Synthetic inputs with the config's distributions, generated on the host once (each rank draws the whole
+    # operands from the same seed and keeps its shard).
+    a_full = rng.integers(-128 if w["a_signed"] else 0, 128 if w["a_signed"] else 256, size=(B, M, K),
                           dtype=np.int16).astype(a_dtype)
+    a_host = (sh.batch_slab(a_full, part) if by_batch else a_full).reshape(-1)
+    del a_full
     b_full_cols = rng.integers(-128 if args.workload == "c3" else -127, 128, size=(K, N), dtype=np.int16)
-    b_host = np.ascontiguousarray(b_full_cols[:, n0:n0 + shard_n]).astype(np.int8).reshape(-1)
+    b_host = (b_full_cols if by_batch else sh.column_slab(b_full_cols, part)).astype(np.int8).reshape(-1)
     del b_full_cols
     a = dev.create_buffer(a_dtype, a_host)
     b = dev.create_buffer(np.int8, b_host)
-    count = B * M * shard_n
+    count = B_local * M * shard_n
     out_dtype = {"i32": np.int32, "f32": np.float32}[w["out"]]
     c = dev.create_buffer(out_dtype, count)
     zpa = zpb = scale = None
@@ -223,7 +235,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         scale = og.Int8Operand(s, 0, True)
         extra.append(s)
     flush = dev.create_buffer(np.uint8, 512 << 20)
-    prob = og.Int8GemmProblem(M, shard_n, K, batch=B, stride_a=M * K if B > 1 else 0, stride_b=0)
+    prob = og.Int8GemmProblem(M, shard_n, K, batch=B_local, stride_a=M * K if B_local > 1 else 0, stride_b=0)
     gemm = og.Int8Gemm(dev)
 
     def encode(enc):
@@ -321,19 +333,14 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         except Exception as exc:  # noqa: BLE001 - context only
             lib_tops = f"unavailable: {type(exc).__name__}"
 
-    local = np.array([gemm_ns, e2e_ns], dtype=np.float64)
     if dist is not None:
-        import torch
-        t = torch.tensor(local, device=f"cuda:{local_rank}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        local = t.cpu().numpy()
-    gemm_ns, e2e_ns = float(local[0]), float(local[1])
+        gemm_ns, e2e_ns = sh.max_over_ranks(dist, [gemm_ns, e2e_ns], device=f"cuda:{local_rank}")
 
     total_ops = 2.0 * B * M * N * K
     ms_per_step = gemm_ns / args.steps / 1e6
     value = total_ops / (ms_per_step * 1e-3) / 1e12
     per_launch_s = statistics.mean(per_step_ns) * 1e-9
-    shard_ops = 2.0 * B * M * shard_n * K
+    shard_ops = 2.0 * B_local * M * shard_n * K
     achieved = shard_ops / per_launch_s / 1e12
     # Bytes one launch must move at least: A, the B slab, C, and the zero-point / scale vectors.
     algo_bytes = (a_host.nbytes + b_host.nbytes + count * np.dtype(out_dtype).itemsize
@@ -359,7 +366,8 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": f"{args.workload}: {w['desc']}", "m": M, "n": N, "k": K, "batch": B,
-                       "parallelism": f"N-shard x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"{'batch' if by_batch else 'N'}-shard x{world}" if world > 1
+                                       else "single GPU"),
                        "l2": "flushed before every step (512 MB write), steps timed by CUDA events",
                        "kernel": kernel, "variant": gemm.variant},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 1), "unit": "TOPS",

@@ -111,6 +111,13 @@ OG_API og_status og_device_destroy(og_device* device);
 OG_API og_status og_device_info_get(og_device* device, og_device_info* out);
 /* GpuDevice.WaitIdle. Also reports (once) a failure a kernel recorded since the last check. */
 OG_API og_status og_device_wait_idle(og_device* device);
+/* Watchdog self-test (no counterpart in the reference, whose device-lost and watchdog failures come from the
+ * driver: GpuDevice.cs:337-377). Queues on the device's stream a kernel whose bounded wait on an mbarrier, the same
+ * wait every pipeline stage of the product kernels uses, runs out after limit_us microseconds (1 .. 2,000,000)
+ * because nothing ever arrives. The kernel then raises the device's failure word and returns, exactly as a product
+ * kernel whose pipeline stalled would; the next og_device_wait_idle or readback reports OG_ERROR_COMMAND_FAILED
+ * (GpuCommandFailedException, reason Watchdog), clears the word, and the device stays usable. */
+OG_API og_status og_device_watchdog_selftest(og_device* device, uint32_t limit_us);
 /* The cudaStream_t submissions run on; og_device_set_stream binds an external one (e.g. a framework's). */
 OG_API og_status og_device_stream(og_device* device, void** stream);
 OG_API og_status og_device_set_stream(og_device* device, void* stream);

@@ -14,6 +14,7 @@
 
 #include "../../include/onegpu_cuda.h"
 #include "og_gemm.h"
+#include "og_ptx.cuh"
 
 // ---- errors ---------------------------------------------------------------------------------------------------------
 
@@ -162,7 +163,8 @@ void check_device_status(og_device* d) {
         check_cuda(cudaMemsetAsync(d->status, 0, sizeof(int), d->stream), "status reset");
         check_cuda(cudaStreamSynchronize(d->stream), "cudaStreamSynchronize");
         throw OgError{OG_ERROR_COMMAND_FAILED, "GpuDevice", "",
-                      "a kernel gave up waiting on its own pipeline (watchdog) and skipped its work", "", "", ""};
+                      "a kernel gave up waiting on its own pipeline (watchdog) and skipped its work", "Watchdog", "",
+                      ""};
     }
 }
 
@@ -616,6 +618,33 @@ OG_API og_status og_device_wait_idle(og_device* d) {
         if (d == nullptr) null_arg("GpuDevice", "device");
         use(d);
         check_device_status(d);
+    });
+}
+
+namespace og {
+// One thread waits, with the kernels' own bounded wait, on an mbarrier that expects an arrival nobody makes. The wait
+// gives up after limit_ns, the kernel raises the device's failure word the way a stalled product kernel does, and it
+// returns: no fault, no trap, nothing left in flight.
+__global__ void watchdog_selftest_kernel(int* status, uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x != 0) return;
+    abort_flag = 0;
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    if (!mbar_wait(&bar, 0, &abort_flag, limit_ns)) atomicExch(status, 1);
+}
+}  // namespace og
+
+OG_API og_status og_device_watchdog_selftest(og_device* d, uint32_t limit_us) {
+    return guard([&] {
+        if (d == nullptr) null_arg("GpuDevice", "device");
+        if (limit_us < 1 || limit_us > 2000000)
+            throw OgError{OG_ERROR_ARGUMENT_RANGE, "GpuDevice", "limitMicroseconds",
+                          "the self-test wait limit is 1 .. 2000000 microseconds", "", "", ""};
+        use(d);
+        og::watchdog_selftest_kernel<<<1, 32, 0, d->stream>>>(d->status, uint64_t(limit_us) * 1000);
+        check_cuda(cudaGetLastError(), "watchdog self-test launch");
     });
 }
 

@@ -51,13 +51,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Waits for the phase of `parity` to complete. Returns false (and raises *abort) when *abort was already raised by
 // another role or when the wait ran past the limit.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t limit_ns = OG_WAIT_LIMIT_NS) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_timer_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort) return false;
-        if (global_timer_ns() - t0 > OG_WAIT_LIMIT_NS) {
+        if (global_timer_ns() - t0 > limit_ns) {
             *abort = 1;
             return false;
         }

@@ -90,6 +90,7 @@ EXPORTS = {
     "og_device_destroy": [_P],
     "og_device_info_get": [_P, ctypes.POINTER(og_device_info)],
     "og_device_wait_idle": [_P],
+    "og_device_watchdog_selftest": [_P, ctypes.c_uint32],
     "og_device_stream": [_P, _PP],
     "og_device_set_stream": [_P, _P],
     "og_buffer_alloc": [_P, ctypes.c_uint64, _PP],
@@ -185,7 +186,11 @@ class GpuDeviceLostException(GpuException):
 
 
 class GpuCommandFailedException(GpuException):
-    pass
+    """A submission failed; ``reason`` is "Watchdog" when a kernel's bounded wait ran out (GpuDevice.cs:337-374)."""
+
+    def __init__(self, message: str, reason: str = ""):
+        super().__init__(message)
+        self.reason = reason
 
 
 def _raise(status: int) -> None:
@@ -208,7 +213,7 @@ def _raise(status: int) -> None:
     if status == OG_ERROR_DEVICE_LOST:
         raise GpuDeviceLostException(f"{op}: {msg}")
     if status == OG_ERROR_COMMAND_FAILED:
-        raise GpuCommandFailedException(f"{op}: {msg}")
+        raise GpuCommandFailedException(f"{op}: {msg}", info.capability.decode())
     raise GpuException(f"status {status}: {op}: {msg}")
 
 
@@ -359,6 +364,11 @@ class GpuDevice:
     def wait_idle(self) -> None:
         _check(_lib.og_device_wait_idle(self.handle))
         self._keep.clear()
+
+    def watchdog_selftest(self, limit_us: int) -> None:
+        """Queues a kernel whose bounded wait runs out after ``limit_us``; the next wait_idle raises
+        GpuCommandFailedException with reason "Watchdog" and the device stays usable."""
+        _check(_lib.og_device_watchdog_selftest(self.handle, limit_us))
 
     @property
     def stream(self) -> int:

@@ -70,7 +70,10 @@ typedef enum og_element_type {
     OG_I32 = 2, /* int */
     OG_F32 = 3, /* float */
     OG_F16 = 4, /* Half */
-    OG_U32 = 5  /* uint */
+    OG_U32 = 5, /* uint */
+    OG_U16 = 6, /* ushort: no kernel takes it; named so that a caller's type is reported, not guessed */
+    OG_I16 = 7, /* short: likewise */
+    OG_I64 = 8  /* long: likewise */
 } og_element_type;
 
 /* A GpuBuffer<T> (src/RecursiveAI.OneGpu/GpuBufferOfT.cs:11): device pointer of element 0, element count, type. */
@@ -285,6 +288,82 @@ OG_API og_status og_dynamic_quantize_encode(og_dynamic_quantize* dq, og_encoder*
 OG_API og_status og_dynamic_quantize_check(const og_buffer* x, int32_t offset_x, int32_t count, const og_buffer* y,
                                            int32_t offset_y, const og_buffer* scale, int32_t offset_scale,
                                            const og_buffer* zero_point, int32_t offset_zero_point);
+
+/* ---- DequantizeKernels (src/RecursiveAI.OneGpu.Kernels/DequantizeKernels.cs:29-298) ------------------------------ */
+
+typedef struct og_dequantize og_dequantize;
+
+/* new DequantizeKernels(device) (DequantizeKernels.cs:46-51). */
+OG_API og_status og_dequantize_create(og_device* device, og_dequantize** out);
+OG_API og_status og_dequantize_destroy(og_dequantize* kernels);
+/* DequantizeKernels.Encode<TIn, TOut> (DequantizeKernels.cs:69-130), ONNX DequantizeLinear:
+ * output = float(x - zeroPoint) * scale. x is uint8, int8 or int32 (TIn); output float32 or half (TOut); scale float32;
+ * zero_point (nullable) has x's type. shape has `rank` dimensions; with per_axis the scale and zero point hold one
+ * value per index of `axis` (in [-rank, rank)), otherwise one value. Offsets are in elements. */
+OG_API og_status og_dequantize_encode(og_dequantize* kernels, og_encoder* encoder, const og_buffer* x, int32_t offset_x,
+                                      const int32_t* shape, int32_t rank, int32_t axis, int32_t per_axis,
+                                      const og_buffer* scale, int32_t offset_scale, const og_buffer* zero_point,
+                                      int32_t offset_zero_point, const og_buffer* output, int32_t offset_output);
+/* DequantizeKernels.EncodeQuantize<TIn, TOut> (DequantizeKernels.cs:184-240), ONNX QuantizeLinear:
+ * output = saturate(round_half_even(x / scale) + zeroPoint), NaN to the lowest value. x float32 or half (TIn); output
+ * uint8 or int8 (TOut); zero_point (nullable) has the output's type. */
+OG_API og_status og_dequantize_encode_quantize(og_dequantize* kernels, og_encoder* encoder, const og_buffer* x,
+                                               int32_t offset_x, const int32_t* shape, int32_t rank, int32_t axis,
+                                               int32_t per_axis, const og_buffer* scale, int32_t offset_scale,
+                                               const og_buffer* zero_point, int32_t offset_zero_point,
+                                               const og_buffer* output, int32_t offset_output);
+/* The checks of DequantizeKernels.Encode / EncodeQuantize alone, in the reference's order. */
+OG_API og_status og_dequantize_check(const og_buffer* x, int32_t offset_x, const int32_t* shape, int32_t rank,
+                                     int32_t axis, int32_t per_axis, const og_buffer* scale, int32_t offset_scale,
+                                     const og_buffer* zero_point, int32_t offset_zero_point, const og_buffer* output,
+                                     int32_t offset_output);
+OG_API og_status og_dequantize_check_quantize(const og_buffer* x, int32_t offset_x, const int32_t* shape,
+                                              int32_t rank, int32_t axis, int32_t per_axis, const og_buffer* scale,
+                                              int32_t offset_scale, const og_buffer* zero_point,
+                                              int32_t offset_zero_point, const og_buffer* output,
+                                              int32_t offset_output);
+
+/* ---- ConvIntegerKernels (src/RecursiveAI.OneGpu.Kernels/ConvIntegerKernels.cs:25-351) --------------------------- */
+
+/* ConvProblem (src/RecursiveAI.OneGpu.Kernels/ConvProblem.cs): NCHW input, OIHW weights, strides, dilations,
+ * asymmetric padding, groups; offsets in elements. activation must be 0; offset_bias / offset_residual are unused. A
+ * 1-D convolution is height 1 (ConvProblem.Conv1D). */
+typedef struct og_conv_problem {
+    int32_t batch, in_channels, height, width, out_channels, kernel_height, kernel_width;
+    int32_t stride_height, stride_width, dilation_height, dilation_width;
+    int32_t pad_top, pad_left, pad_bottom, pad_right;
+    int32_t groups;
+    int32_t activation;
+    int32_t offset_x, offset_w, offset_bias, offset_residual, offset_y;
+} og_conv_problem;
+
+typedef struct og_conv_integer og_conv_integer;
+
+/* new ConvIntegerKernels(device, options) (ConvIntegerKernels.cs:46-63): options of the underlying Int8Gemm, NULL for
+ * the defaults. */
+OG_API og_status og_conv_integer_create(og_device* device, const og_int8_gemm_options* options, og_conv_integer** out);
+OG_API og_status og_conv_integer_destroy(og_conv_integer* conv);
+/* ConvIntegerKernels.Variant (ConvIntegerKernels.cs:66): the underlying product's variant. */
+OG_API og_status og_conv_integer_variant(og_conv_integer* conv, char* buffer, uint64_t capacity);
+/* ConvIntegerKernels.BindGroupsCreated (ConvIntegerKernels.cs:69): the product's count plus the device buffers the
+ * instance allocated; a warm call with a problem already seen adds nothing. */
+OG_API og_status og_conv_integer_bind_groups_created(og_conv_integer* conv, int32_t* count);
+/* ConvIntegerKernels.ScratchBytesPerImage (ConvIntegerKernels.cs:79-83): Groups * K * ceil(OH * OW / 4) * 4. Scratch
+ * of this size per image runs the problem; a buffer that also holds the 16-byte-padded rows
+ * (Groups * K * ceil(OH * OW / 16) * 16 per image) keeps the product on the tensor cores. */
+OG_API og_status og_conv_integer_scratch_bytes_per_image(const og_conv_problem* problem, int64_t* bytes);
+/* ConvIntegerKernels.Encode<TX, TW> (ConvIntegerKernels.cs:104-264): x and w uint8 / int8 in any mix, y int32;
+ * x_zero_point one value of x's type, w_zero_point one value or one per output channel of w's type (either NULL for
+ * 0); scratch (NULL: the instance's own) has x's type and scratch_offset is a non-negative multiple of 4. */
+OG_API og_status og_conv_integer_encode(og_conv_integer* conv, og_encoder* encoder, const og_conv_problem* problem,
+                                        const og_buffer* x, const og_buffer* w, const og_buffer* y,
+                                        const og_operand* x_zero_point, const og_operand* w_zero_point,
+                                        const og_buffer* scratch, int32_t scratch_offset);
+/* The checks of Encode alone, in the reference's order. */
+OG_API og_status og_conv_integer_check(const og_conv_problem* problem, const og_buffer* x, const og_buffer* w,
+                                       const og_buffer* y, const og_operand* x_zero_point,
+                                       const og_operand* w_zero_point, const og_buffer* scratch,
+                                       int32_t scratch_offset);
 
 #ifdef __cplusplus
 }

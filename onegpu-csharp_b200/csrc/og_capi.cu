@@ -14,16 +14,12 @@
 
 #include "../../include/onegpu_cuda.h"
 #include "og_gemm.h"
+#include "og_host.h"
 #include "og_ptx.cuh"
 
 // ---- errors ---------------------------------------------------------------------------------------------------------
 
-namespace {
-
-struct OgError {
-    og_status status;
-    std::string operation, argument, message, capability, expected, actual;
-};
+namespace og_host {
 
 thread_local og_error_info g_last = {};
 
@@ -85,49 +81,57 @@ void check_cuda(cudaError_t e, const char* what) {
     throw OgError{st, what, "", std::string(cudaGetErrorName(e)) + ": " + cudaGetErrorString(e), "", "", ""};
 }
 
-template <class F>
-og_status guard(F&& f) {
-    try {
-        f();
-        return OG_OK;
-    } catch (const OgError& e) {
-        set_last(e);
-        return e.status;
-    } catch (const std::bad_alloc&) {
-        set_last(OgError{OG_ERROR_OUT_OF_MEMORY, "host", "", "host allocation failed", "", "", ""});
-        return OG_ERROR_OUT_OF_MEMORY;
-    } catch (...) {
-        set_last(OgError{OG_ERROR_CUDA, "host", "", "unexpected failure", "", "", ""});
-        return OG_ERROR_CUDA;
-    }
-}
 
 void put_string(char* buf, uint64_t cap, const std::string& s) {
     if (buf == nullptr || cap == 0) return;
     copy_field(buf, static_cast<size_t>(cap), s);
 }
 
-}  // namespace
+void use(og_device* d) { check_cuda(cudaSetDevice(d->ordinal), "cudaSetDevice"); }
+
+const char* type_name(int32_t t) {
+    switch (t) {
+        case OG_U8: return "Byte";
+        case OG_S8: return "SByte";
+        case OG_I32: return "Int32";
+        case OG_F32: return "Single";
+        case OG_F16: return "Half";
+        case OG_U32: return "UInt32";
+        case OG_U16: return "UInt16";
+        case OG_I16: return "Int16";
+        case OG_I64: return "Int64";
+        default: return "Unknown";
+    }
+}
+
+int elem_size(int32_t t) {
+    switch (t) {
+        case OG_U8:
+        case OG_S8: return 1;
+        case OG_F16:
+        case OG_U16:
+        case OG_I16: return 2;
+        case OG_I64: return 8;
+        default: return 4;
+    }
+}
+
+// Check.Range: offset not negative, [offset, offset + extent) inside the buffer.
+void range(const char* op, const std::string& name, int64_t length, int32_t offset, int64_t extent) {
+    if (offset < 0) shape(op, name + "Offset", "offset " + std::to_string(offset) + " is negative");
+    if (extent < 0 || static_cast<int64_t>(offset) + extent > length)
+        shape(op, name,
+              "elements " + std::to_string(offset) + ".." + std::to_string(static_cast<int64_t>(offset) + extent) +
+                  " reach past the buffer of " + std::to_string(length));
+}
+
+}  // namespace og_host
+
+using namespace og_host;
 
 // ---- objects ----------------------------------------------------------------------------------------------------
 
-struct og_device {
-    int ordinal = 0;
-    cudaStream_t stream = nullptr;
-    bool own_stream = true;
-    int sm_count = 0;
-    cudaDeviceProp prop = {};
-    int* status = nullptr;       // device word a kernel sets when a bounded wait gave up
-    int* status_host = nullptr;  // pinned mirror for readbacks
-};
-
-using Op = std::function<cudaError_t(cudaStream_t)>;
-
-struct og_encoder {
-    og_device* device = nullptr;
-    std::vector<Op> ops;
-    int64_t dispatches = 0;
-};
+using Op = OgOp;
 
 struct og_timestamps {
     og_device* device = nullptr;
@@ -152,8 +156,6 @@ struct og_dynamic_quantize {
 
 namespace {
 
-void use(og_device* d) { check_cuda(cudaSetDevice(d->ordinal), "cudaSetDevice"); }
-
 // Reads the kernels' failure word of the device (after the stream has drained) and clears it.
 void check_device_status(og_device* d) {
     check_cuda(cudaMemcpyAsync(d->status_host, d->status, sizeof(int), cudaMemcpyDeviceToHost, d->stream),
@@ -172,37 +174,8 @@ void check_device_status(og_device* d) {
 
 const char* kGemm = "Int8Gemm";
 const char* kDq = "DynamicQuantizeLinear";
-constexpr int64_t kMaxElements = INT_MAX;  // Check.MaxElements
 
-const char* type_name(int32_t t) {
-    switch (t) {
-        case OG_U8: return "Byte";
-        case OG_S8: return "SByte";
-        case OG_I32: return "Int32";
-        case OG_F32: return "Single";
-        case OG_F16: return "Half";
-        case OG_U32: return "UInt32";
-        default: return "Unknown";
-    }
-}
 
-int elem_size(int32_t t) {
-    switch (t) {
-        case OG_U8:
-        case OG_S8: return 1;
-        case OG_F16: return 2;
-        default: return 4;
-    }
-}
-
-// Check.Range: offset not negative, [offset, offset + extent) inside the buffer.
-void range(const char* op, const std::string& name, int64_t length, int32_t offset, int64_t extent) {
-    if (offset < 0) shape(op, name + "Offset", "offset " + std::to_string(offset) + " is negative");
-    if (extent < 0 || static_cast<int64_t>(offset) + extent > length)
-        shape(op, name,
-              "elements " + std::to_string(offset) + ".." + std::to_string(static_cast<int64_t>(offset) + extent) +
-                  " reach past the buffer of " + std::to_string(length));
-}
 
 void require_int8(const og_buffer* b, const char* arg) {
     if (b->type != OG_U8 && b->type != OG_S8)

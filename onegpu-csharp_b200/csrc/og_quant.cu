@@ -1,0 +1,378 @@
+// DequantizeKernels (DequantizeKernels.cs:29-298): ONNX DequantizeLinear and QuantizeLinear, per tensor or per axis,
+// with their argument checks and C ABI.
+//
+//   DequantizeLinear: y = float(x - zeroPoint) * scale   (Shaders/Dequantize.hlsl:42-57)
+//     x uint8 / int8 / int32; the subtraction wraps in 32 bits, the conversion rounds to nearest even, then one float32
+//     multiply; half output rounds that float32 to the nearest half (even on ties).
+//   QuantizeLinear: y = saturate(round_half_even(x / scale) + zeroPoint)   (Shaders/Quantize.hlsl:54-81)
+//     x float32 / half (widened exactly); the division is IEEE round-to-nearest, the zero point is added in float32,
+//     NaN gives the output type's lowest value, then the result is clamped to uint8 / int8.
+//
+// The tensor is seen as [outer, axisLen, inner]; element j uses parameter (j / inner) % axisLen. Both kernels are
+// HBM-bound streams: each thread owns one 16-byte piece of the output (aligned to the output's 16-byte boundaries,
+// so every store of a whole piece is one vector store and no two threads share a byte), reads the inputs it needs
+// and finishes them.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "og_host.h"
+
+namespace og {
+
+constexpr int QTHREADS = 256;
+
+struct QuantArgs {
+    const void* x;        // first element
+    int64_t count;
+    const float* scale;   // first scale
+    const void* zp;       // first zero point, or null
+    int per_axis;
+    uint32_t axis_len;
+    uint32_t inner;
+    void* out;            // first output element
+    int64_t pieces;       // 16-byte pieces of the output touched
+    int lead;             // output elements before the first 16-byte boundary at or below out
+};
+
+__device__ __forceinline__ uint32_t param_index(const QuantArgs& a, int64_t j) {
+    return a.per_axis ? (static_cast<uint32_t>(j) / a.inner) % a.axis_len : 0u;  // counts stay below 2^31
+}
+
+template <int KIND>  // 0 uint8, 1 int8, 2 int32
+__device__ __forceinline__ int32_t load_q(const void* p, int64_t i) {
+    if constexpr (KIND == 0) return static_cast<int32_t>(__ldg(static_cast<const uint8_t*>(p) + i));
+    else if constexpr (KIND == 1) return static_cast<int32_t>(static_cast<int8_t>(__ldg(static_cast<const uint8_t*>(p) + i)));
+    else return __ldg(static_cast<const int32_t*>(p) + i);
+}
+
+template <int KIND>
+__device__ __forceinline__ float dequantize_one(const QuantArgs& a, int64_t j) {
+    const uint32_t pi = param_index(a, j);
+    const int32_t zp = a.zp != nullptr ? load_q<KIND>(a.zp, pi) : 0;
+    const int32_t q = load_q<KIND>(a.x, j);
+    const int32_t d = static_cast<int32_t>(static_cast<uint32_t>(q) - static_cast<uint32_t>(zp));
+    return __fmul_rn(__int2float_rn(d), __ldg(a.scale + pi));
+}
+
+template <int KIND, bool HALF>
+__global__ void __launch_bounds__(QTHREADS) dequantize_kernel(const QuantArgs a) {
+    constexpr int V = HALF ? 8 : 4;  // output elements per 16-byte piece
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= a.pieces) return;
+    const int64_t first = t * V - a.lead;
+    if (first >= 0 && first + V <= a.count) {
+        uint32_t w[4];
+        if constexpr (HALF) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const __half lo = __float2half_rn(dequantize_one<KIND>(a, first + 2 * q));
+                const __half hi = __float2half_rn(dequantize_one<KIND>(a, first + 2 * q + 1));
+                w[q] = static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
+            }
+            __stcs(reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + first), make_uint4(w[0], w[1], w[2], w[3]));
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; q++) w[q] = __float_as_uint(dequantize_one<KIND>(a, first + q));
+            __stcs(reinterpret_cast<uint4*>(static_cast<float*>(a.out) + first), make_uint4(w[0], w[1], w[2], w[3]));
+        }
+    } else {
+        for (int q = 0; q < V; q++) {
+            const int64_t j = first + q;
+            if (j < 0 || j >= a.count) continue;
+            const float v = dequantize_one<KIND>(a, j);
+            if constexpr (HALF)
+                static_cast<__half*>(a.out)[j] = __float2half_rn(v);
+            else
+                static_cast<float*>(a.out)[j] = v;
+        }
+    }
+}
+
+template <bool HALF>
+__device__ __forceinline__ float load_x(const void* p, int64_t i) {
+    if constexpr (HALF) return __half2float(__ushort_as_half(__ldg(static_cast<const unsigned short*>(p) + i)));
+    else return __ldg(static_cast<const float*>(p) + i);
+}
+
+template <bool SIGNED, bool HALF>
+__device__ __forceinline__ uint32_t quantize_one(const QuantArgs& a, int64_t j) {
+    const uint32_t pi = param_index(a, j);
+    int32_t zp = 0;
+    if (a.zp != nullptr) {
+        const uint8_t z = __ldg(static_cast<const uint8_t*>(a.zp) + pi);
+        zp = SIGNED ? static_cast<int32_t>(static_cast<int8_t>(z)) : static_cast<int32_t>(z);
+    }
+    const float lo = SIGNED ? -128.0f : 0.0f;
+    const float hi = SIGNED ? 127.0f : 255.0f;
+    float v = __fadd_rn(rintf(__fdiv_rn(load_x<HALF>(a.x, j), __ldg(a.scale + pi))), static_cast<float>(zp));
+    if (isnan(v)) v = lo;
+    v = v < lo ? lo : (v > hi ? hi : v);
+    return static_cast<uint32_t>(static_cast<int32_t>(v)) & 0xFFu;
+}
+
+template <bool SIGNED, bool HALF>
+__global__ void __launch_bounds__(QTHREADS) quantize_kernel(const QuantArgs a) {
+    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (t >= a.pieces) return;
+    const int64_t first = t * 16 - a.lead;
+    uint8_t* y = static_cast<uint8_t*>(a.out);
+    if (first >= 0 && first + 16 <= a.count) {
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            w[q] = quantize_one<SIGNED, HALF>(a, first + 4 * q) | (quantize_one<SIGNED, HALF>(a, first + 4 * q + 1) << 8) |
+                   (quantize_one<SIGNED, HALF>(a, first + 4 * q + 2) << 16) |
+                   (quantize_one<SIGNED, HALF>(a, first + 4 * q + 3) << 24);
+        }
+        __stcs(reinterpret_cast<uint4*>(y + first), make_uint4(w[0], w[1], w[2], w[3]));
+    } else {
+        for (int q = 0; q < 16; q++) {
+            const int64_t j = first + q;
+            if (j >= 0 && j < a.count) y[j] = static_cast<uint8_t>(quantize_one<SIGNED, HALF>(a, j));
+        }
+    }
+}
+
+// The 16-byte pieces covering `count` elements of `esize` bytes at `out`, and the elements before the first boundary.
+static void pieces_of(QuantArgs& a, int esize) {
+    const uintptr_t o = reinterpret_cast<uintptr_t>(a.out);
+    const uintptr_t base = o & ~uintptr_t(15);
+    const uintptr_t end = o + static_cast<uintptr_t>(a.count) * esize;
+    a.lead = static_cast<int>((o - base) / esize);
+    a.pieces = static_cast<int64_t>((end - base + 15) / 16);
+}
+
+static cudaError_t launch_dequantize(QuantArgs a, int kind, bool half, cudaStream_t s) {
+    pieces_of(a, half ? 2 : 4);
+    const unsigned blocks = static_cast<unsigned>((a.pieces + QTHREADS - 1) / QTHREADS);
+    switch (kind * 2 + (half ? 1 : 0)) {
+        case 0: dequantize_kernel<0, false><<<blocks, QTHREADS, 0, s>>>(a); break;
+        case 1: dequantize_kernel<0, true><<<blocks, QTHREADS, 0, s>>>(a); break;
+        case 2: dequantize_kernel<1, false><<<blocks, QTHREADS, 0, s>>>(a); break;
+        case 3: dequantize_kernel<1, true><<<blocks, QTHREADS, 0, s>>>(a); break;
+        case 4: dequantize_kernel<2, false><<<blocks, QTHREADS, 0, s>>>(a); break;
+        default: dequantize_kernel<2, true><<<blocks, QTHREADS, 0, s>>>(a); break;
+    }
+    return cudaGetLastError();
+}
+
+static cudaError_t launch_quantize(QuantArgs a, bool is_signed, bool half, cudaStream_t s) {
+    pieces_of(a, 1);
+    const unsigned blocks = static_cast<unsigned>((a.pieces + QTHREADS - 1) / QTHREADS);
+    switch ((is_signed ? 2 : 0) + (half ? 1 : 0)) {
+        case 0: quantize_kernel<false, false><<<blocks, QTHREADS, 0, s>>>(a); break;
+        case 1: quantize_kernel<false, true><<<blocks, QTHREADS, 0, s>>>(a); break;
+        case 2: quantize_kernel<true, false><<<blocks, QTHREADS, 0, s>>>(a); break;
+        default: quantize_kernel<true, true><<<blocks, QTHREADS, 0, s>>>(a); break;
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace og
+
+// ---- argument checks and C ABI ------------------------------------------------------------------------------------
+
+struct og_dequantize {
+    og_device* device = nullptr;
+};
+
+namespace {
+
+using namespace og_host;
+
+const char* kDequant = "DequantizeLinear";
+const char* kQuant = "QuantizeLinear";
+
+// KernelTypes.IsHalf<T> (KernelSupport.cs:50-65, with KernelTypes.Of's message for types outside its list).
+bool is_half(const char* op, int32_t t) {
+    if (t == OG_F32) return false;
+    if (t == OG_F16) return true;
+    if (t == OG_I32 || t == OG_U32 || t == OG_I64)
+        shape(op, "T", std::string("element type ") + type_name(t) + " is not supported; use float or Half");
+    shape(op, "T", std::string("element type ") + type_name(t) +
+                       " is not supported; use float, Half, int, long or uint as the operation allows");
+}
+
+struct Geometry {
+    int64_t count = 0;
+    int64_t axis_len = 1;
+    int64_t inner = 1;
+};
+
+Geometry geometry(const char* op, const int32_t* dims, int32_t rank, int32_t axis, int32_t per_axis) {
+    if (rank < 0) shape(op, "shape", "rank " + std::to_string(rank) + " is negative");
+    if (rank > 0 && dims == nullptr) null_arg(op, "shape");
+    Geometry g;
+    g.count = product(op, "shape", dims, rank);
+    if (per_axis) {
+        const int32_t ax = axis_of(op, axis, rank);
+        g.axis_len = dims[ax];
+        for (int32_t i = ax + 1; i < rank; i++) g.inner *= dims[i];
+    }
+    return g;
+}
+
+void require_float_scale(const char* op, const og_buffer* scale) {
+    if (scale->type != OG_F32)
+        shape(op, "scale", std::string("element type ") + type_name(scale->type) + " is not supported; use float");
+}
+
+// DequantizeKernels.Encode's checks in the reference's order (DequantizeKernels.cs:64-130). Returns the input kind
+// (0 uint8, 1 int8, 2 int32) and whether the output is half.
+Geometry check_dequantize(const og_buffer* x, int32_t offset_x, const int32_t* dims, int32_t rank, int32_t axis,
+                          int32_t per_axis, const og_buffer* scale, int32_t offset_scale, const og_buffer* zp,
+                          int32_t offset_zp, const og_buffer* out, int32_t offset_out, int* kind, bool* half) {
+    if (x == nullptr) null_arg(kDequant, "x");
+    if (scale == nullptr) null_arg(kDequant, "scale");
+    if (out == nullptr) null_arg(kDequant, "output");
+    if (x->type == OG_U8) *kind = 0;
+    else if (x->type == OG_S8) *kind = 1;
+    else if (x->type == OG_I32) *kind = 2;
+    else
+        shape(kDequant, "TIn", std::string("element type ") + type_name(x->type) +
+                                   " is not supported; use byte (uint8), sbyte (int8) or int");
+    *half = is_half(kDequant, out->type);
+    const Geometry g = geometry(kDequant, dims, rank, axis, per_axis);
+    const int64_t params = per_axis ? g.axis_len : 1;
+    require_float_scale(kDequant, scale);
+    range(kDequant, "scale", scale->length, offset_scale, params);
+    if (*kind == 2) range(kDequant, "x", x->length, offset_x, g.count);
+    else range_bytes(kDequant, "x", x->length, offset_x, g.count);
+    if (zp != nullptr) {
+        if (zp->type != x->type)
+            shape(kDequant, "zeroPoint", std::string("element type ") + type_name(zp->type) +
+                                             " differs from the type of x, " + type_name(x->type));
+        if (*kind == 2) range(kDequant, "zeroPoint", zp->length, offset_zp, params);
+        else range_bytes(kDequant, "zeroPoint", zp->length, offset_zp, params);
+    }
+    if (*half) range_half(kDequant, "output", out->length, offset_out, g.count);
+    else range(kDequant, "output", out->length, offset_out, g.count);
+    return g;
+}
+
+// DequantizeKernels.EncodeQuantize's checks in the reference's order (DequantizeKernels.cs:184-240).
+Geometry check_quantize(const og_buffer* x, int32_t offset_x, const int32_t* dims, int32_t rank, int32_t axis,
+                        int32_t per_axis, const og_buffer* scale, int32_t offset_scale, const og_buffer* zp,
+                        int32_t offset_zp, const og_buffer* out, int32_t offset_out, bool* is_signed, bool* half) {
+    if (x == nullptr) null_arg(kQuant, "x");
+    if (scale == nullptr) null_arg(kQuant, "scale");
+    if (out == nullptr) null_arg(kQuant, "output");
+    if (out->type == OG_U8) *is_signed = false;
+    else if (out->type == OG_S8) *is_signed = true;
+    else
+        shape(kQuant, "TOut", std::string("element type ") + type_name(out->type) +
+                                  " is not supported; use byte (uint8) or sbyte (int8)");
+    *half = is_half(kQuant, x->type);
+    const Geometry g = geometry(kQuant, dims, rank, axis, per_axis);
+    const int64_t params = per_axis ? g.axis_len : 1;
+    if (*half) range_half(kQuant, "x", x->length, offset_x, g.count);
+    else range(kQuant, "x", x->length, offset_x, g.count);
+    require_float_scale(kQuant, scale);
+    range(kQuant, "scale", scale->length, offset_scale, params);
+    if (zp != nullptr) {
+        if (zp->type != out->type)
+            shape(kQuant, "zeroPoint", std::string("element type ") + type_name(zp->type) +
+                                           " differs from the output's, " + type_name(out->type));
+        range_bytes(kQuant, "zeroPoint", zp->length, offset_zp, params);
+    }
+    range_bytes(kQuant, "output", out->length, offset_out, g.count);
+    return g;
+}
+
+og::QuantArgs args_of(const Geometry& g, const og_buffer* x, int32_t offset_x, int x_esize, const og_buffer* scale,
+                      int32_t offset_scale, const og_buffer* zp, int32_t offset_zp, int zp_esize, int32_t per_axis,
+                      const og_buffer* out, int32_t offset_out, int out_esize) {
+    og::QuantArgs a{};
+    a.x = static_cast<const uint8_t*>(x->ptr) + static_cast<int64_t>(offset_x) * x_esize;
+    a.count = g.count;
+    a.scale = static_cast<const float*>(scale->ptr) + offset_scale;
+    a.zp = zp != nullptr ? static_cast<const uint8_t*>(zp->ptr) + static_cast<int64_t>(offset_zp) * zp_esize : nullptr;
+    a.per_axis = per_axis ? 1 : 0;
+    a.axis_len = static_cast<uint32_t>(g.axis_len > 0 ? g.axis_len : 1);
+    a.inner = static_cast<uint32_t>(g.inner > 0 ? g.inner : 1);
+    a.out = static_cast<uint8_t*>(out->ptr) + static_cast<int64_t>(offset_out) * out_esize;
+    return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+OG_API og_status og_dequantize_create(og_device* d, og_dequantize** out) {
+    return guard([&] {
+        if (d == nullptr) null_arg(kDequant, "device");
+        if (out == nullptr) null_arg(kDequant, "out");
+        auto* k = new og_dequantize();
+        k->device = d;
+        *out = k;
+    });
+}
+
+OG_API og_status og_dequantize_destroy(og_dequantize* k) {
+    return guard([&] { delete k; });
+}
+
+OG_API og_status og_dequantize_check(const og_buffer* x, int32_t offset_x, const int32_t* shape_, int32_t rank,
+                                     int32_t axis, int32_t per_axis, const og_buffer* scale, int32_t offset_scale,
+                                     const og_buffer* zero_point, int32_t offset_zero_point, const og_buffer* output,
+                                     int32_t offset_output) {
+    return guard([&] {
+        int kind;
+        bool half;
+        check_dequantize(x, offset_x, shape_, rank, axis, per_axis, scale, offset_scale, zero_point, offset_zero_point,
+                         output, offset_output, &kind, &half);
+    });
+}
+
+OG_API og_status og_dequantize_check_quantize(const og_buffer* x, int32_t offset_x, const int32_t* shape_,
+                                              int32_t rank, int32_t axis, int32_t per_axis, const og_buffer* scale,
+                                              int32_t offset_scale, const og_buffer* zero_point,
+                                              int32_t offset_zero_point, const og_buffer* output,
+                                              int32_t offset_output) {
+    return guard([&] {
+        bool is_signed, half;
+        check_quantize(x, offset_x, shape_, rank, axis, per_axis, scale, offset_scale, zero_point, offset_zero_point,
+                       output, offset_output, &is_signed, &half);
+    });
+}
+
+OG_API og_status og_dequantize_encode(og_dequantize* k, og_encoder* enc, const og_buffer* x, int32_t offset_x,
+                                      const int32_t* shape_, int32_t rank, int32_t axis, int32_t per_axis,
+                                      const og_buffer* scale, int32_t offset_scale, const og_buffer* zero_point,
+                                      int32_t offset_zero_point, const og_buffer* output, int32_t offset_output) {
+    return guard([&] {
+        if (k == nullptr) throw OgError{OG_ERROR_INVALID_HANDLE, kDequant, "kernels", "null handle", "", "", ""};
+        if (enc == nullptr) null_arg(kDequant, "encoder");
+        int kind;
+        bool half;
+        const Geometry g = check_dequantize(x, offset_x, shape_, rank, axis, per_axis, scale, offset_scale,
+                                            zero_point, offset_zero_point, output, offset_output, &kind, &half);
+        if (g.count == 0) return;
+        const int xs = kind == 2 ? 4 : 1;
+        const og::QuantArgs a = args_of(g, x, offset_x, xs, scale, offset_scale, zero_point, offset_zero_point, xs,
+                                        per_axis, output, offset_output, half ? 2 : 4);
+        enc->ops.push_back([=](cudaStream_t s) { return og::launch_dequantize(a, kind, half, s); });
+        enc->dispatches += 1;
+    });
+}
+
+OG_API og_status og_dequantize_encode_quantize(og_dequantize* k, og_encoder* enc, const og_buffer* x,
+                                               int32_t offset_x, const int32_t* shape_, int32_t rank, int32_t axis,
+                                               int32_t per_axis, const og_buffer* scale, int32_t offset_scale,
+                                               const og_buffer* zero_point, int32_t offset_zero_point,
+                                               const og_buffer* output, int32_t offset_output) {
+    return guard([&] {
+        if (k == nullptr) throw OgError{OG_ERROR_INVALID_HANDLE, kQuant, "kernels", "null handle", "", "", ""};
+        if (enc == nullptr) null_arg(kQuant, "encoder");
+        bool is_signed, half;
+        const Geometry g = check_quantize(x, offset_x, shape_, rank, axis, per_axis, scale, offset_scale, zero_point,
+                                          offset_zero_point, output, offset_output, &is_signed, &half);
+        if (g.count == 0) return;
+        const og::QuantArgs a = args_of(g, x, offset_x, half ? 2 : 4, scale, offset_scale, zero_point,
+                                        offset_zero_point, 1, per_axis, output, offset_output, 1);
+        enc->ops.push_back([=](cudaStream_t s) { return og::launch_quantize(a, is_signed, half, s); });
+        enc->dispatches += 1;
+    });
+}
+
+}  // extern "C"

@@ -39,10 +39,10 @@ OG_ERROR_COMMAND_FAILED = 7
 OG_ERROR_CUDA = 8
 OG_ERROR_INVALID_HANDLE = 9
 
-U8, S8, I32, F32, F16, U32 = 0, 1, 2, 3, 4, 5
-_NP = {U8: np.uint8, S8: np.int8, I32: np.int32, F32: np.float32, F16: np.float16, U32: np.uint32}
-_FROM_NP = {np.dtype(np.uint8): U8, np.dtype(np.int8): S8, np.dtype(np.int32): I32, np.dtype(np.float32): F32,
-            np.dtype(np.float16): F16, np.dtype(np.uint32): U32}
+U8, S8, I32, F32, F16, U32, U16, I16, I64 = 0, 1, 2, 3, 4, 5, 6, 7, 8
+_NP = {U8: np.uint8, S8: np.int8, I32: np.int32, F32: np.float32, F16: np.float16, U32: np.uint32, U16: np.uint16,
+       I16: np.int16, I64: np.int64}
+_FROM_NP = {np.dtype(v): k for k, v in _NP.items()}
 
 KERNEL_AUTO, KERNEL_TENSOR_CORE, KERNEL_PORTABLE = 0, 1, 2
 
@@ -82,6 +82,10 @@ _PP = ctypes.POINTER(ctypes.c_void_p)
 _BUF = ctypes.POINTER(og_buffer)
 _OPD = ctypes.POINTER(og_operand)
 _PROB = ctypes.POINTER(og_int8_gemm_problem)
+
+# x, offset, shape, rank, axis, per_axis, scale, offset, zero point, offset, output, offset
+_QUANT_ARGS = [_BUF, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+               _BUF, ctypes.c_int32, _BUF, ctypes.c_int32, _BUF, ctypes.c_int32]
 
 EXPORTS = {
     "og_last_error": [ctypes.POINTER(og_error_info)],
@@ -132,6 +136,19 @@ EXPORTS = {
                                    ctypes.c_int32, _BUF, ctypes.c_int32],
     "og_dynamic_quantize_check": [_BUF, ctypes.c_int32, ctypes.c_int32, _BUF, ctypes.c_int32, _BUF, ctypes.c_int32,
                                   _BUF, ctypes.c_int32],
+    "og_dequantize_create": [_P, _PP],
+    "og_dequantize_destroy": [_P],
+    "og_dequantize_encode": [_P, _P] + _QUANT_ARGS,
+    "og_dequantize_encode_quantize": [_P, _P] + _QUANT_ARGS,
+    "og_dequantize_check": _QUANT_ARGS,
+    "og_dequantize_check_quantize": _QUANT_ARGS,
+    "og_conv_integer_create": [_P, _P, _PP],
+    "og_conv_integer_destroy": [_P],
+    "og_conv_integer_variant": [_P, ctypes.c_char_p, ctypes.c_uint64],
+    "og_conv_integer_bind_groups_created": [_P, ctypes.POINTER(ctypes.c_int32)],
+    "og_conv_integer_scratch_bytes_per_image": [_P, ctypes.POINTER(ctypes.c_int64)],
+    "og_conv_integer_encode": [_P, _P, _P, _BUF, _BUF, _BUF, _OPD, _OPD, _BUF, ctypes.c_int32],
+    "og_conv_integer_check": [_P, _BUF, _BUF, _BUF, _OPD, _OPD, _BUF, ctypes.c_int32],
 }
 
 for _name, _args in EXPORTS.items():
@@ -617,6 +634,203 @@ def check_dynamic_quantize(x, offset_x, count, y, offset_y, scale, offset_scale,
                            offset_zero_point) -> None:
     _check(_lib.og_dynamic_quantize_check(_buf(x), offset_x, count, _buf(y), offset_y, _buf(scale), offset_scale,
                                           _buf(zero_point), offset_zero_point))
+
+
+def _shape(shape):
+    dims = [int(v) for v in shape]
+    return (ctypes.c_int32 * max(len(dims), 1))(*dims), len(dims)
+
+
+def _quant_args(x, offset_x, shape, axis, per_axis, scale, offset_scale, zero_point, offset_zero_point, output,
+                offset_output):
+    dims, rank = _shape(shape)
+    return [_buf(x), offset_x, dims, rank, axis, int(bool(per_axis)), _buf(scale), offset_scale, _buf(zero_point),
+            offset_zero_point, _buf(output), offset_output]
+
+
+def check_dequantize_linear(x, offset_x, shape, axis, per_axis, scale, offset_scale, zero_point, offset_zero_point,
+                            output, offset_output) -> None:
+    """The argument checks of DequantizeKernels.Encode alone (no device needed)."""
+    _check(_lib.og_dequantize_check(*_quant_args(x, offset_x, shape, axis, per_axis, scale, offset_scale, zero_point,
+                                                 offset_zero_point, output, offset_output)))
+
+
+def check_quantize_linear(x, offset_x, shape, axis, per_axis, scale, offset_scale, zero_point, offset_zero_point,
+                          output, offset_output) -> None:
+    """The argument checks of DequantizeKernels.EncodeQuantize alone (no device needed)."""
+    _check(_lib.og_dequantize_check_quantize(*_quant_args(x, offset_x, shape, axis, per_axis, scale, offset_scale,
+                                                          zero_point, offset_zero_point, output, offset_output)))
+
+
+# ---- DequantizeKernels ----------------------------------------------------------------------------------------------
+
+class DequantizeKernels:
+    """DequantizeKernels (DequantizeKernels.cs:29-298) on the CUDA backend: DequantizeLinear (encode) and
+    QuantizeLinear (encode_quantize)."""
+
+    def __init__(self, device: GpuDevice):
+        self.device = device
+        h = ctypes.c_void_p()
+        _check(_lib.og_dequantize_create(device.handle, ctypes.byref(h)))
+        self.handle = h.value
+
+    def encode(self, encoder: GpuCommandEncoder, x: GpuBuffer, offset_x: int, shape, axis: int, per_axis: bool,
+               scale: GpuBuffer, offset_scale: int, zero_point: Optional[GpuBuffer], offset_zero_point: int,
+               output: GpuBuffer, offset_output: int) -> None:
+        _check(_lib.og_dequantize_encode(self.handle, encoder.handle if encoder else None,
+                                         *_quant_args(x, offset_x, shape, axis, per_axis, scale, offset_scale,
+                                                      zero_point, offset_zero_point, output, offset_output)))
+
+    def encode_quantize(self, encoder: GpuCommandEncoder, x: GpuBuffer, offset_x: int, shape, axis: int,
+                        per_axis: bool, scale: GpuBuffer, offset_scale: int, zero_point: Optional[GpuBuffer],
+                        offset_zero_point: int, output: GpuBuffer, offset_output: int) -> None:
+        _check(_lib.og_dequantize_encode_quantize(self.handle, encoder.handle if encoder else None,
+                                                  *_quant_args(x, offset_x, shape, axis, per_axis, scale,
+                                                               offset_scale, zero_point, offset_zero_point, output,
+                                                               offset_output)))
+
+    Encode = encode
+    EncodeQuantize = encode_quantize
+
+    def dispose(self) -> None:
+        if self.handle:
+            _check(_lib.og_dequantize_destroy(self.handle))
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.dispose()
+
+
+# ---- ConvIntegerKernels ---------------------------------------------------------------------------------------------
+
+class og_conv_problem(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int32) for name in
+                ("batch", "in_channels", "height", "width", "out_channels", "kernel_height", "kernel_width",
+                 "stride_height", "stride_width", "dilation_height", "dilation_width", "pad_top", "pad_left",
+                 "pad_bottom", "pad_right", "groups", "activation", "offset_x", "offset_w", "offset_bias",
+                 "offset_residual", "offset_y")]
+
+
+@dataclass
+class ConvProblem:
+    """ConvProblem (ConvProblem.cs): NCHW / OIHW geometry, offsets in elements."""
+    batch: int
+    in_channels: int
+    height: int
+    width: int
+    out_channels: int
+    kernel_height: int
+    kernel_width: int
+    stride_height: int = 1
+    stride_width: int = 1
+    dilation_height: int = 1
+    dilation_width: int = 1
+    pad_top: int = 0
+    pad_left: int = 0
+    pad_bottom: int = 0
+    pad_right: int = 0
+    groups: int = 1
+    activation: int = 0
+    offset_x: int = 0
+    offset_w: int = 0
+    offset_bias: int = 0
+    offset_residual: int = 0
+    offset_y: int = 0
+
+    @staticmethod
+    def conv1d(batch, in_channels, length, out_channels, kernel, stride=1, dilation=1, pad_begin=0, pad_end=0,
+               groups=1) -> "ConvProblem":
+        """ConvProblem.Conv1D: height 1."""
+        return ConvProblem(batch, in_channels, 1, length, out_channels, 1, kernel, stride_width=stride,
+                           dilation_width=dilation, pad_left=pad_begin, pad_right=pad_end, groups=groups)
+
+    @staticmethod
+    def _extent(input_, kernel, stride, dilation, pad_begin, pad_end) -> int:
+        if input_ < 1 or kernel < 1 or stride < 1 or dilation < 1:
+            return 0
+        span = input_ + pad_begin + pad_end - (dilation * (kernel - 1) + 1)
+        return 0 if span < 0 else span // stride + 1
+
+    @property
+    def out_height(self) -> int:
+        return self._extent(self.height, self.kernel_height, self.stride_height, self.dilation_height, self.pad_top,
+                            self.pad_bottom)
+
+    @property
+    def out_width(self) -> int:
+        return self._extent(self.width, self.kernel_width, self.stride_width, self.dilation_width, self.pad_left,
+                            self.pad_right)
+
+    def c_struct(self) -> og_conv_problem:
+        return og_conv_problem(*[int(getattr(self, name)) for name, _ in og_conv_problem._fields_])
+
+
+def conv_scratch_bytes_per_image(problem: ConvProblem) -> int:
+    """ConvIntegerKernels.ScratchBytesPerImage."""
+    p = problem.c_struct()
+    out = ctypes.c_int64()
+    _check(_lib.og_conv_integer_scratch_bytes_per_image(ctypes.byref(p), ctypes.byref(out)))
+    return out.value
+
+
+def check_conv_integer(problem: ConvProblem, x, w, y, x_zero_point=None, w_zero_point=None, scratch=None,
+                       scratch_offset: int = 0) -> None:
+    """The argument checks of ConvIntegerKernels.Encode alone (no device needed)."""
+    p = problem.c_struct()
+    _check(_lib.og_conv_integer_check(ctypes.byref(p), _buf(x), _buf(w), _buf(y), _opd(x_zero_point),
+                                      _opd(w_zero_point), _buf(scratch), scratch_offset))
+
+
+class ConvIntegerKernels:
+    """ConvIntegerKernels (ConvIntegerKernels.cs:25-351) on the CUDA backend."""
+
+    def __init__(self, device: GpuDevice, options: Optional[Int8GemmOptions] = None):
+        self.device = device
+        h = ctypes.c_void_p()
+        opt = None
+        if options is not None:
+            opt = ctypes.byref(og_int8_gemm_options(int(bool(options.allow_packed_dot)), int(options.kernel),
+                                                    int(options.tile)))
+        _check(_lib.og_conv_integer_create(device.handle, opt, ctypes.byref(h)))
+        self.handle = h.value
+
+    @property
+    def variant(self) -> str:
+        buf = ctypes.create_string_buffer(256)
+        _check(_lib.og_conv_integer_variant(self.handle, buf, 256))
+        return buf.value.decode()
+
+    @property
+    def bind_groups_created(self) -> int:
+        n = ctypes.c_int32()
+        _check(_lib.og_conv_integer_bind_groups_created(self.handle, ctypes.byref(n)))
+        return n.value
+
+    scratch_bytes_per_image = staticmethod(conv_scratch_bytes_per_image)
+
+    def encode(self, encoder: GpuCommandEncoder, problem: ConvProblem, x: GpuBuffer, w: GpuBuffer, y: GpuBuffer,
+               x_zero_point=None, w_zero_point=None, scratch: Optional[GpuBuffer] = None,
+               scratch_offset: int = 0) -> None:
+        p = problem.c_struct()
+        _check(_lib.og_conv_integer_encode(self.handle, encoder.handle if encoder else None, ctypes.byref(p), _buf(x),
+                                           _buf(w), _buf(y), _opd(x_zero_point), _opd(w_zero_point), _buf(scratch),
+                                           scratch_offset))
+
+    Encode = encode
+
+    def dispose(self) -> None:
+        if self.handle:
+            _check(_lib.og_conv_integer_destroy(self.handle))
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.dispose()
 
 
 # ---- DynamicQuantizeKernels -----------------------------------------------------------------------------------------

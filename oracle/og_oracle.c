@@ -283,3 +283,156 @@ float og_oracle_div_exact(float x, float s) {
     if (e < 1 || e > 254) return x / s;
     return u2f(((xb ^ sb) & 0x80000000u) | ((uint32_t)e << 23) | (m & 0x7FFFFFu));
 }
+
+/* IEEE 754 binary32 -> binary16, round to nearest even (the C# (Half) cast): overflow to infinity, results below
+ * the smallest normal become subnormals or zero, NaN stays NaN (quiet, top payload bits kept). */
+uint16_t og_oracle_float_to_half(float f) {
+    const uint32_t x = f2u(f);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const uint32_t exp = (x >> 23) & 0xFFu;
+    uint32_t man = x & 0x7FFFFFu;
+    if (exp == 0xFFu) return (uint16_t)(sign | 0x7C00u | (man != 0u ? 0x200u | (man >> 13) : 0u));
+    const int32_t e = (int32_t)exp - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7C00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        man |= 0x800000u;
+        const uint32_t shift = (uint32_t)(14 - e);
+        uint32_t h = man >> shift;
+        const uint32_t rest = man & ((1u << shift) - 1u), half = 1u << (shift - 1u);
+        if (rest > half || (rest == half && (h & 1u))) h++;
+        return (uint16_t)(sign | h);
+    }
+    uint32_t h = sign | ((uint32_t)e << 10) | (man >> 13);
+    const uint32_t rest = man & 0x1FFFu;
+    if (rest > 0x1000u || (rest == 0x1000u && (h & 1u))) h++;  /* a carry moves into the exponent (or to infinity) */
+    return (uint16_t)h;
+}
+
+/* IEEE 754 binary16 -> binary32, exact. */
+float og_oracle_half_to_float(uint16_t h) {
+    const uint32_t sign = ((uint32_t)h & 0x8000u) << 16;
+    const uint32_t exp = ((uint32_t)h >> 10) & 0x1Fu;
+    uint32_t man = (uint32_t)h & 0x3FFu;
+    if (exp == 0x1Fu) return u2f(sign | 0x7F800000u | (man << 13));
+    if (exp != 0u) return u2f(sign | ((exp - 15u + 127u) << 23) | (man << 13));
+    if (man == 0u) return u2f(sign);
+    int32_t e = -1;
+    do {
+        e++;
+        man <<= 1;
+    } while ((man & 0x400u) == 0u);
+    return u2f(sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3FFu) << 13));
+}
+
+static inline int32_t quant_value(int32_t kind, const void* p, int64_t i) {
+    if (kind == 0) return (int32_t)((const uint8_t*)p)[i];
+    if (kind == 1) return (int32_t)((const int8_t*)p)[i];
+    return ((const int32_t*)p)[i];
+}
+
+/* DequantizeTests.cs:57-68: want = (float)unchecked(x - zp) * scale, then (Half)want for half outputs. */
+void og_oracle_dequantize(int32_t kind, const void* x, int64_t count, int32_t per_axis, int64_t axis_len, int64_t inner,
+                          const float* scale, const void* zero_point, int32_t half_out, void* out) {
+    for (int64_t j = 0; j < count; j++) {
+        const int64_t a = per_axis ? (j / inner) % axis_len : 0;
+        const int32_t zp = zero_point != NULL ? quant_value(kind, zero_point, a) : 0;
+        const int32_t d = (int32_t)((uint32_t)quant_value(kind, x, j) - (uint32_t)zp);
+        const float want = (float)d * scale[a];
+        if (half_out) ((uint16_t*)out)[j] = og_oracle_float_to_half(want);
+        else ((float*)out)[j] = want;
+    }
+}
+
+/* DequantizeTests.cs:138-148 (QuantizeOne): v = MathF.Round(x / scale) + zeroPoint in binary32, NaN -> lo, clamp. */
+void og_oracle_quantize(int32_t is_signed, int32_t half_in, const void* x, int64_t count, int32_t per_axis,
+                        int64_t axis_len, int64_t inner, const float* scale, const uint8_t* zero_point, uint8_t* out) {
+    const int32_t lo = is_signed ? -128 : 0, hi = is_signed ? 127 : 255;
+    for (int64_t j = 0; j < count; j++) {
+        const int64_t a = per_axis ? (j / inner) % axis_len : 0;
+        const int32_t zp = zero_point != NULL ? val8(zero_point[a], is_signed) : 0;
+        const float xv = half_in ? og_oracle_half_to_float(((const uint16_t*)x)[j]) : ((const float*)x)[j];
+        const float q = xv / scale[a];
+        const float v = nearbyintf(q) + (float)zp;
+        int32_t r;
+        if (isnan(v)) r = lo;
+        else r = v < (float)lo ? lo : (v > (float)hi ? hi : (int32_t)v);
+        out[j] = (uint8_t)(r & 0xFF);
+    }
+}
+
+/* ConvProblem.OutHeight / OutWidth (GpuWindow.OutputExtent without auto padding or ceil mode). */
+int32_t og_oracle_conv_out_extent(int32_t input, int32_t kernel, int32_t stride, int32_t dilation, int32_t pad_begin,
+                                  int32_t pad_end) {
+    if (input < 1 || kernel < 1 || stride < 1 || dilation < 1) return 0;
+    const int64_t effective = (int64_t)dilation * (kernel - 1) + 1;
+    const int64_t span = (int64_t)input + pad_begin + pad_end - effective;
+    if (span < 0) return 0;
+    const int64_t extent = span / stride + 1;
+    return extent > 2147483647 ? 0 : (int32_t)extent;
+}
+
+typedef struct conv_job {
+    const og_oracle_conv* p;
+    const uint8_t *x, *w, *xz, *wz;
+    int32_t xs, ws, wz_vector;
+    int32_t* y;
+    int64_t row0, row1;  /* rows (image, output channel) of this thread */
+} conv_job;
+
+static void* conv_rows(void* arg) {
+    const conv_job* j = (const conv_job*)arg;
+    const og_oracle_conv* p = j->p;
+    const int32_t oh = og_oracle_conv_out_extent(p->h, p->kh, p->stride_h, p->dilation_h, p->pad_top, p->pad_bottom);
+    const int32_t ow = og_oracle_conv_out_extent(p->w, p->kw, p->stride_w, p->dilation_w, p->pad_left, p->pad_right);
+    const int32_t cin_g = p->cin / p->groups, cout_g = p->cout / p->groups;
+    const int32_t xzv = j->xz != NULL ? val8(j->xz[0], j->xs) : 0;
+    for (int64_t row = j->row0; row < j->row1; row++) {
+        const int64_t n = row / p->cout, m = row % p->cout, g = m / cout_g;
+        const int32_t wzv = j->wz != NULL ? val8(j->wz[j->wz_vector ? m : 0], j->ws) : 0;
+        for (int32_t i = 0; i < oh; i++) {
+            for (int32_t jj = 0; jj < ow; jj++) {
+                uint32_t acc = 0;
+                for (int32_t c = 0; c < cin_g; c++) {
+                    for (int32_t kh = 0; kh < p->kh; kh++) {
+                        const int64_t ih = (int64_t)i * p->stride_h + (int64_t)kh * p->dilation_h - p->pad_top;
+                        if (ih < 0 || ih >= p->h) continue;
+                        for (int32_t kw = 0; kw < p->kw; kw++) {
+                            const int64_t iw = (int64_t)jj * p->stride_w + (int64_t)kw * p->dilation_w - p->pad_left;
+                            if (iw < 0 || iw >= p->w) continue;
+                            const int64_t xi = p->offset_x + ((((n * p->cin) + g * cin_g + c) * p->h + ih) * p->w + iw);
+                            const int64_t wi = p->offset_w + ((((m * cin_g) + c) * p->kh + kh) * p->kw + kw);
+                            const int32_t xv = val8(j->x[xi], j->xs) - xzv;
+                            const int32_t wv = val8(j->w[wi], j->ws) - wzv;
+                            acc += (uint32_t)xv * (uint32_t)wv;
+                        }
+                    }
+                }
+                j->y[((n * p->cout + m) * oh + i) * ow + jj] = (int32_t)acc;
+            }
+        }
+    }
+    return NULL;
+}
+
+/* ConvIntegerTests.cs:41-88 (Reference), rows (image, output channel) split over POSIX threads. */
+void og_oracle_conv_integer(const og_oracle_conv* p, const uint8_t* x, int32_t x_signed, const uint8_t* w,
+                            int32_t w_signed, const uint8_t* xz, const uint8_t* wz, int32_t wz_vector, int32_t* y,
+                            int32_t threads) {
+    const int64_t rows = (int64_t)p->batch * p->cout;
+    if (rows <= 0) return;
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    if (threads > rows) threads = (int32_t)rows;
+    conv_job jobs[256];
+    pthread_t tids[256];
+    for (int32_t t = 0; t < threads; t++)
+        jobs[t] = (conv_job){p, x, w, xz, wz, x_signed, w_signed, wz_vector, y, rows * t / threads,
+                             rows * (t + 1) / threads};
+    if (threads == 1) {
+        conv_rows(&jobs[0]);
+        return;
+    }
+    for (int32_t t = 0; t < threads; t++) pthread_create(&tids[t], NULL, conv_rows, &jobs[t]);
+    for (int32_t t = 0; t < threads; t++) pthread_join(tids[t], NULL);
+}

@@ -14,6 +14,12 @@
  *   og_oracle_requant          tests/RecursiveAI.OneGpu.Kernels.Tests/Int8Tests.cs:84-97   (Requant: QLinearMatMul byte)
  *   og_oracle_float_epilogue   tests/RecursiveAI.OneGpu.Kernels.Tests/Int8Tests.cs:356-373 (float form, two roundings)
  *   og_oracle_dynamic_quantize tests/RecursiveAI.OneGpu.Kernels.Tests/Int8Tests.cs:577-615 (DynamicReference)
+ *   og_oracle_dequantize       tests/RecursiveAI.OneGpu.Kernels.Tests/DequantizeTests.cs:57-68 (float(x - zp) * scale)
+ *   og_oracle_quantize         tests/RecursiveAI.OneGpu.Kernels.Tests/DequantizeTests.cs:138-148 (QuantizeOne)
+ *   og_oracle_conv_integer     tests/RecursiveAI.OneGpu.Kernels.Tests/ConvIntegerTests.cs:41-88 (Reference: direct
+ *                              convolution, padded taps skipped, wrapping int32 sums)
+ * with the IEEE binary16 conversions the C# (Half) casts perform (og_oracle_float_to_half: round to nearest even;
+ * og_oracle_half_to_float: exact),
  * and two independent cross-checks of the oracle itself:
  *   og_oracle_int8_gemm_signed_domain  src/RecursiveAI.OneGpu.Kernels/Shaders/Int8GemmDot.hlsl:4-10,134-140,301
  *                                      (operands moved to the signed domain, zero points applied from byte sums)
@@ -63,6 +69,32 @@ float og_oracle_float_epilogue(int32_t acc, int32_t has_int_bias, int32_t int_bi
 
 void og_oracle_dynamic_quantize(const float* x, int64_t count, uint8_t* y, float* scale, uint8_t* zero_point);
 float og_oracle_div_exact(float x, float s);
+
+uint16_t og_oracle_float_to_half(float f);
+float og_oracle_half_to_float(uint16_t h);
+
+/* DequantizeLinear over `count` elements viewed as [outer, axis_len, inner]: kind 0 uint8, 1 int8, 2 int32 (x and
+ * zero_point, which may be NULL); `out` receives float32 or, with half_out, binary16 bits. */
+void og_oracle_dequantize(int32_t kind, const void* x, int64_t count, int32_t per_axis, int64_t axis_len, int64_t inner,
+                          const float* scale, const void* zero_point, int32_t half_out, void* out);
+/* QuantizeLinear: x float32 or, with half_in, binary16 bits; zero_point (uint8 / int8 by is_signed) may be NULL. */
+void og_oracle_quantize(int32_t is_signed, int32_t half_in, const void* x, int64_t count, int32_t per_axis,
+                        int64_t axis_len, int64_t inner, const float* scale, const uint8_t* zero_point, uint8_t* out);
+
+/* ConvInteger over NCHW x and OIHW w (bytes; x_signed / w_signed give their types), zero point of x one value
+ * (NULL: 0), of w one value or one per output channel (NULL: 0). `y` receives [batch, cout, oh, ow] int32. */
+typedef struct og_oracle_conv {
+    int32_t batch, cin, h, w, cout, kh, kw;
+    int32_t stride_h, stride_w, dilation_h, dilation_w;
+    int32_t pad_top, pad_left, pad_bottom, pad_right;
+    int32_t groups;
+    int32_t offset_x, offset_w;
+} og_oracle_conv;
+int32_t og_oracle_conv_out_extent(int32_t input, int32_t kernel, int32_t stride, int32_t dilation, int32_t pad_begin,
+                                  int32_t pad_end);
+void og_oracle_conv_integer(const og_oracle_conv* p, const uint8_t* x, int32_t x_signed, const uint8_t* w,
+                            int32_t w_signed, const uint8_t* xz, const uint8_t* wz, int32_t wz_vector, int32_t* y,
+                            int32_t threads);
 
 #ifdef __cplusplus
 }

@@ -29,6 +29,12 @@ class Problem(ctypes.Structure):
                  "stride_b")]
 
 
+class Conv(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int32) for name in
+                ("batch", "cin", "h", "w", "cout", "kh", "kw", "stride_h", "stride_w", "dilation_h", "dilation_w",
+                 "pad_top", "pad_left", "pad_bottom", "pad_right", "groups", "offset_x", "offset_w")]
+
+
 _lib = None
 
 
@@ -54,6 +60,19 @@ def lib():
         _lib.og_oracle_dynamic_quantize.argtypes = [f32p, ctypes.c_int64, u8p, f32p, u8p]
         _lib.og_oracle_div_exact.argtypes = [ctypes.c_float, ctypes.c_float]
         _lib.og_oracle_div_exact.restype = ctypes.c_float
+        _lib.og_oracle_float_to_half.argtypes = [ctypes.c_float]
+        _lib.og_oracle_float_to_half.restype = ctypes.c_uint16
+        _lib.og_oracle_half_to_float.argtypes = [ctypes.c_uint16]
+        _lib.og_oracle_half_to_float.restype = ctypes.c_float
+        vp = ctypes.c_void_p
+        _lib.og_oracle_dequantize.argtypes = [ctypes.c_int32, vp, ctypes.c_int64, ctypes.c_int32, ctypes.c_int64,
+                                              ctypes.c_int64, f32p, vp, ctypes.c_int32, vp]
+        _lib.og_oracle_quantize.argtypes = [ctypes.c_int32, ctypes.c_int32, vp, ctypes.c_int64, ctypes.c_int32,
+                                            ctypes.c_int64, ctypes.c_int64, f32p, u8p, u8p]
+        _lib.og_oracle_conv_out_extent.argtypes = [ctypes.c_int32] * 6
+        _lib.og_oracle_conv_out_extent.restype = ctypes.c_int32
+        _lib.og_oracle_conv_integer.argtypes = [ctypes.POINTER(Conv), u8p, ctypes.c_int32, u8p, ctypes.c_int32, u8p,
+                                                u8p, ctypes.c_int32, i32p, ctypes.c_int32]
     return _lib
 
 
@@ -152,3 +171,78 @@ def dynamic_quantize(x: np.ndarray):
 def div_exact(x: float, s: float) -> float:
     """DivExact (DivExact.hlsli:28-99)."""
     return float(lib().og_oracle_div_exact(float(np.float32(x)), float(np.float32(s))))
+
+
+def float_to_half(f: float) -> int:
+    """The C# (Half) cast: binary16 bits, round to nearest even."""
+    return int(lib().og_oracle_float_to_half(float(np.float32(f))))
+
+
+def half_to_float(h: int) -> float:
+    return float(lib().og_oracle_half_to_float(int(h)))
+
+
+def _params(shape, axis, per_axis):
+    count = int(np.prod(shape)) if len(shape) else 1
+    if not per_axis:
+        return count, 1, 1
+    ax = axis + len(shape) if axis < 0 else axis
+    inner = int(np.prod(shape[ax + 1:])) if ax + 1 < len(shape) else 1
+    return count, int(shape[ax]), inner
+
+
+def dequantize(x: np.ndarray, shape, axis: int, per_axis: bool, scale: np.ndarray, zero_point=None,
+               half_out: bool = False) -> np.ndarray:
+    """DequantizeTests.cs:57-68 over x (uint8, int8 or int32 elements, already offset): float32 values, or binary16
+    bits as uint16 with half_out."""
+    kind = {np.dtype(np.uint8): 0, np.dtype(np.int8): 1, np.dtype(np.int32): 2}[np.dtype(x.dtype)]
+    count, axis_len, inner = _params(shape, axis, per_axis)
+    x = np.ascontiguousarray(x[:count])
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    zp = None if zero_point is None else np.ascontiguousarray(zero_point, dtype=x.dtype)
+    out = np.empty(count, dtype=np.uint16 if half_out else np.float32)
+    lib().og_oracle_dequantize(kind, x.ctypes.data, count, int(bool(per_axis)), axis_len, inner,
+                               _p(scale, ctypes.c_float), None if zp is None else zp.ctypes.data, int(bool(half_out)),
+                               out.ctypes.data)
+    return out
+
+
+def quantize(x: np.ndarray, shape, axis: int, per_axis: bool, scale: np.ndarray, zero_point=None,
+             signed: bool = False) -> np.ndarray:
+    """DequantizeTests.cs:138-148 over x (float32, or float16 taken as its binary16 bits): uint8 bytes of the
+    uint8 / int8 results."""
+    half_in = np.dtype(x.dtype) == np.dtype(np.float16)
+    count, axis_len, inner = _params(shape, axis, per_axis)
+    x = np.ascontiguousarray(x[:count])
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    zp = None if zero_point is None else np.ascontiguousarray(zero_point).view(np.uint8)
+    out = np.empty(count, dtype=np.uint8)
+    lib().og_oracle_quantize(int(bool(signed)), int(half_in), x.ctypes.data, count, int(bool(per_axis)), axis_len,
+                             inner, _p(scale, ctypes.c_float), _p(zp, ctypes.c_uint8), _p(out, ctypes.c_uint8))
+    return out
+
+
+def conv_out_extent(input_, kernel, stride, dilation, pad_begin, pad_end) -> int:
+    return int(lib().og_oracle_conv_out_extent(input_, kernel, stride, dilation, pad_begin, pad_end))
+
+
+def conv_integer(p: dict, x: np.ndarray, x_signed: bool, w: np.ndarray, w_signed: bool, xz=None, wz=None,
+                 wz_vector: bool = False, threads: int = 0) -> np.ndarray:
+    """ConvIntegerTests.cs:41-88 (Reference): y [batch, cout, oh, ow] int32. `p` holds the fields of Conv (missing
+    ones default: strides and dilations 1, paddings and offsets 0, groups 1)."""
+    d = dict(stride_h=1, stride_w=1, dilation_h=1, dilation_w=1, pad_top=0, pad_left=0, pad_bottom=0, pad_right=0,
+             groups=1, offset_x=0, offset_w=0)
+    d.update(p)
+    c = Conv(**{k: int(d[k]) for k, _ in Conv._fields_})
+    oh = conv_out_extent(c.h, c.kh, c.stride_h, c.dilation_h, c.pad_top, c.pad_bottom)
+    ow = conv_out_extent(c.w, c.kw, c.stride_w, c.dilation_w, c.pad_left, c.pad_right)
+    y = np.zeros(max(c.batch * c.cout * oh * ow, 1), dtype=np.int32)
+    x = np.ascontiguousarray(x).view(np.uint8)
+    w = np.ascontiguousarray(w).view(np.uint8)
+    xz = None if xz is None else np.ascontiguousarray(xz).view(np.uint8)
+    wz = None if wz is None else np.ascontiguousarray(wz).view(np.uint8)
+    lib().og_oracle_conv_integer(ctypes.byref(c), _p(x, ctypes.c_uint8), int(bool(x_signed)), _p(w, ctypes.c_uint8),
+                                 int(bool(w_signed)), _p(xz, ctypes.c_uint8), _p(wz, ctypes.c_uint8),
+                                 int(bool(wz_vector)), _p(y, ctypes.c_int32),
+                                 threads if threads > 0 else (os.cpu_count() or 1))
+    return y[: c.batch * c.cout * oh * ow].reshape(c.batch, c.cout, oh, ow)

@@ -118,3 +118,83 @@ def requant_bias(n: int) -> np.ndarray:
     """RequantCase's bias (Int8Tests.cs:401-405)."""
     i = np.arange(n, dtype=np.int64)
     return (((i * 6007) % 4001) - 2000).astype(np.int32)
+
+
+# ---- DequantizeTests / ConvIntegerTests data (DequantizeTests.cs:8-33,150-170; ConvIntegerTests.cs:19-30) -------------
+
+def quantized(kind: str, n: int, seed: int) -> np.ndarray:
+    """DequantizeTests.Quantized<T>: int32 values (mostly large, the extremes every 17th / 19th element) or bytes, the
+    byte arrays padded to a whole 32-bit word. kind: "u8", "s8" or "i32"."""
+    length = n if kind == "i32" else max(n, 1) + (-max(n, 1)) % 4
+    h = (seed * 2654435761 + 1) & 0xFFFFFFFF
+    raw = np.empty(length, dtype=np.uint32)
+    for i in range(length):
+        h = (h * 1664525 + 1013904223) & 0xFFFFFFFF
+        raw[i] = h
+    if kind != "i32":
+        b = ((raw >> 16) & 0xFF).astype(np.uint8)
+        return b if kind == "u8" else b.view(np.int8)
+    i = np.arange(length)
+    v = raw.view(np.int32) >> (i % 7).astype(np.int32)
+    v[i % 19 == 0] = np.iinfo(np.int32).max
+    v[i % 17 == 0] = np.iinfo(np.int32).min
+    return v.astype(np.int32)
+
+
+def quantize_input(n: int, seed: int, special: bool = True) -> np.ndarray:
+    """DequantizeTests.QuantizeInput: Rig.Random(n, seed, -40, 40) with ties, saturating values and (special) NaN,
+    infinities, a subnormal and signed zeros at fixed positions."""
+    import og_oracle as oracle
+
+    x = oracle.random(n, seed, -40.0, 40.0).astype(np.float32)
+    i = np.arange(n)
+    r = i % 13
+    x[r == 3] = ((i[r == 3] % 5 - 2).astype(np.float32) * np.float32(0.25))
+    m5 = r == 5
+    x[m5] = np.where(i[m5] % 2 == 0, 1, -1).astype(np.float32) * (np.float32(100.0) + i[m5].astype(np.float32))
+    x[r == 7] = (i[r == 7] % 9 - 4).astype(np.float32) + np.float32(0.5)
+    if special:
+        m9 = r == 9
+        sp = np.array([np.nan, np.inf, -np.inf, np.float32(1e-42)], dtype=np.float32)
+        x[m9] = sp[i[m9] % 4]
+        m11 = r == 11
+        x[m11] = np.where(i[m11] % 2 == 0, np.float32(0.0), np.float32(-0.0))
+    return x
+
+
+def axis_params(shape, axis: int, per_axis: bool) -> tuple[int, int, int]:
+    """(count, axis length, inner) of a tensor seen as [outer, axisLen, inner]."""
+    count = int(np.prod(shape)) if len(shape) else 1
+    if not per_axis:
+        return count, 1, 1
+    ax = axis + len(shape) if axis < 0 else axis
+    return count, int(shape[ax]), int(np.prod(shape[ax + 1:])) if ax + 1 < len(shape) else 1
+
+
+def conv_problem_dict(p: dict) -> dict:
+    """A golden conv geometry as ConvProblem keyword arguments."""
+    return dict(batch=p["batch"], in_channels=p["cin"], height=p["h"], width=p["w"], out_channels=p["cout"],
+                kernel_height=p["kh"], kernel_width=p["kw"], stride_height=p["stride_h"], stride_width=p["stride_w"],
+                dilation_height=p["dilation_h"], dilation_width=p["dilation_w"], pad_top=p["pad_top"],
+                pad_left=p["pad_left"], pad_bottom=p["pad_bottom"], pad_right=p["pad_right"], groups=p["groups"],
+                offset_x=p["offset_x"], offset_w=p["offset_w"], offset_y=p["offset_y"])
+
+
+def conv_case_data(p: dict, seed: int, xz_mode: int, wz_mode: int, fill: int, bytes_fn):
+    """ConvIntegerTests.Run's inputs: x = Bytes(xLen, seed), w = Bytes(wLen, seed + 1), zero points from seed + 2 and
+    seed + 3, every byte replaced by the fill (w by fill ^ 0xFF, its zero points by fill ^ 0x80) when fill >= 0."""
+    cin_g = p["cin"] // p["groups"]
+    x_len = p["offset_x"] + p["batch"] * p["cin"] * p["h"] * p["w"] + 4
+    w_len = p["offset_w"] + p["cout"] * cin_g * p["kh"] * p["kw"] + 4
+    x = bytes_fn(x_len, seed)
+    w = bytes_fn(w_len, seed + 1)
+    xz = None if xz_mode == 0 else bytes_fn(1, seed + 2)
+    wz = None if wz_mode == 0 else bytes_fn(p["cout"] if wz_mode == 2 else 1, seed + 3)
+    if fill >= 0:
+        x[:] = fill
+        w[:] = fill ^ 0xFF
+        if xz is not None:
+            xz[:] = fill
+        if wz is not None:
+            wz[:] = fill ^ 0x80
+    return x, w, xz, wz

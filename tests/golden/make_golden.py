@@ -140,6 +140,144 @@ def dynamic_reference(x: list[float]):
     return y, float(scale), zp
 
 
+def quantized(kind: str, n: int, seed: int) -> list[int]:
+    """DequantizeTests.Quantized<T> (DequantizeTests.cs:8-33): int32 values (mostly large, plus the extremes) or bytes;
+    byte tensors are padded to a whole 32-bit word."""
+    length = n if kind == "i32" else max(n, 1) + (-max(n, 1)) % 4
+    h = (seed * 2654435761 + 1) & 0xFFFFFFFF
+    out = []
+    for i in range(length):
+        h = (h * 1664525 + 1013904223) & 0xFFFFFFFF
+        if kind == "i32":
+            out.append(-2**31 if i % 17 == 0 else 2**31 - 1 if i % 19 == 0 else wrap32(h) >> (i % 7))
+        elif kind == "u8":
+            out.append((h >> 16) & 0xFF)
+        else:
+            b = (h >> 16) & 0xFF
+            out.append(b - 256 if b >= 128 else b)
+    return out
+
+
+def rig_random(n: int, seed: int, lo: float, hi: float) -> list[float]:
+    """Rig.Random (Rig.cs:8-19), every step in binary32."""
+    s = (seed * 2654435761 + 12345) & 0xFFFFFFFF
+    lo32, hi32 = np.float32(lo), np.float32(hi)
+    out = []
+    for _ in range(n):
+        s = (s * 1664525 + 1013904223) & 0xFFFFFFFF
+        u = np.float32(s >> 8) / np.float32(16777216.0)
+        out.append(float(lo32 + (hi32 - lo32) * u))
+    return out
+
+
+def quantize_input(n: int, seed: int, special: bool = True) -> list[float]:
+    """DequantizeTests.QuantizeInput (DequantizeTests.cs:150-170)."""
+    x = rig_random(n, seed, -40.0, 40.0)
+    for i in range(n):
+        r = i % 13
+        if r == 3:
+            x[i] = float(np.float32(i % 5 - 2) * np.float32(0.25))
+        elif r == 5:
+            x[i] = float(np.float32(1 if i % 2 == 0 else -1) * np.float32(100.0 + i))
+        elif r == 7:
+            x[i] = float(np.float32(i % 9 - 4) + np.float32(0.5))
+        elif r == 9 and special:
+            x[i] = [float("nan"), float("inf"), float("-inf"), float(np.float32(1e-42))][i % 4]
+        elif r == 11 and special:
+            x[i] = 0.0 if i % 2 == 0 else -0.0
+    return x
+
+
+def digest(values, dtype) -> str:
+    import hashlib
+    return hashlib.sha256(np.asarray(values, dtype=dtype).tobytes()).hexdigest()
+
+
+def dequantize_reference(x, zp, scale, half):
+    """DequantizeTests.cs:57-68: (float)unchecked(x - zp) * scale, then (Half) for half outputs."""
+    want = np.float32(wrap32(x - zp)) * np.float32(scale)
+    return np.float16(want).view(np.uint16).item() if half else np.float32(want).view(np.uint32).item()
+
+
+def quantize_reference(x: float, scale: float, zp: int, lo: int, hi: int) -> int:
+    """DequantizeTests.QuantizeOne (DequantizeTests.cs:138-148)."""
+    with np.errstate(all="ignore"):
+        v = np.float32(np.rint(np.float32(x) / np.float32(scale))) + np.float32(zp)
+    if np.isnan(v):
+        return lo
+    return lo if v < lo else hi if v > hi else int(v)
+
+
+def cs_call_args(text: str) -> tuple[list[int], dict]:
+    pos, named = [], {}
+    for tok in text.split(","):
+        tok = tok.strip()
+        if ":" in tok:
+            k, v = tok.split(":")
+            named[k.strip()] = int(v)
+        elif tok:
+            pos.append(int(tok))
+    return pos, named
+
+
+def conv_p(pos, named) -> dict:
+    """ConvIntegerTests.P (ConvIntegerTests.cs:191-203)."""
+    batch, cin, h, w, cout, kh, kw = pos
+    st, dl, pad = named.get("stride", 1), named.get("dilation", 1), named.get("pad", 0)
+    return dict(batch=batch, cin=cin, h=h, w=w, cout=cout, kh=kh, kw=kw, stride_h=st, stride_w=st, dilation_h=dl,
+                dilation_w=dl, pad_top=pad, pad_left=pad, pad_bottom=pad, pad_right=pad, groups=named.get("groups", 1),
+                offset_x=0, offset_w=0, offset_y=0)
+
+
+def conv_1d(pos, named) -> dict:
+    """ConvProblem.Conv1D: height 1."""
+    batch, cin, length, cout, kernel = pos
+    return dict(batch=batch, cin=cin, h=1, w=length, cout=cout, kh=1, kw=kernel, stride_h=1,
+                stride_w=named.get("stride", 1), dilation_h=1, dilation_w=named.get("dilation", 1), pad_top=0,
+                pad_left=named.get("padBegin", 0), pad_bottom=0, pad_right=named.get("padEnd", 0),
+                groups=named.get("groups", 1), offset_x=0, offset_w=0, offset_y=0)
+
+
+CS_PROPS = {"PadTop": "pad_top", "PadBottom": "pad_bottom", "PadLeft": "pad_left", "PadRight": "pad_right",
+            "StrideHeight": "stride_h", "StrideWidth": "stride_w", "OffsetX": "offset_x", "OffsetW": "offset_w",
+            "OffsetY": "offset_y"}
+
+
+def conv_extent(inp, k, s, d, pb, pe) -> int:
+    span = inp + pb + pe - (d * (k - 1) + 1)
+    return 0 if span < 0 else span // s + 1
+
+
+def conv_reference(p, x, xs, w, ws, xz, wz, wz_vec) -> list[int]:
+    """ConvIntegerTests.Reference (ConvIntegerTests.cs:41-88), pure Python."""
+    oh = conv_extent(p["h"], p["kh"], p["stride_h"], p["dilation_h"], p["pad_top"], p["pad_bottom"])
+    ow = conv_extent(p["w"], p["kw"], p["stride_w"], p["dilation_w"], p["pad_left"], p["pad_right"])
+    cin_g, cout_g = p["cin"] // p["groups"], p["cout"] // p["groups"]
+    xzv = 0 if xz is None else val(xz[0], xs)
+    y = []
+    for n in range(p["batch"]):
+        for m in range(p["cout"]):
+            g = m // cout_g
+            wzv = 0 if wz is None else val(wz[m if wz_vec else 0], ws)
+            for i in range(oh):
+                for j in range(ow):
+                    acc = 0
+                    for c in range(cin_g):
+                        for kh in range(p["kh"]):
+                            ih = i * p["stride_h"] + kh * p["dilation_h"] - p["pad_top"]
+                            if not 0 <= ih < p["h"]:
+                                continue
+                            for kw in range(p["kw"]):
+                                iw = j * p["stride_w"] + kw * p["dilation_w"] - p["pad_left"]
+                                if not 0 <= iw < p["w"]:
+                                    continue
+                                xi = p["offset_x"] + (((n * p["cin"] + g * cin_g + c) * p["h"] + ih) * p["w"] + iw)
+                                wi = p["offset_w"] + (((m * cin_g + c) * p["kh"] + kh) * p["kw"] + kw)
+                                acc += (val(x[xi], xs) - xzv) * (val(w[wi], ws) - wzv)
+                    y.append(wrap32(acc))
+    return y
+
+
 def problem(m, n, k, batch=1, trans_b=False, off_a=0, off_b=0, off_c=0, lda_extra=0, ldb_extra=0, share_b=False):
     """Int8Tests.Problem (Int8Tests.cs:198-212)."""
     lda = k + lda_extra
@@ -258,9 +396,142 @@ def main() -> None:
                 seed += 1
     out["edge_cases_small"] = {"cite": f"{REF_TESTS}/Int8Tests.cs:214-232", "cases": cases}
 
+    # DequantizeTests: the case table, offsets and scale sets, and restated results of small cases.
+    dq = read(ref, f"{REF_TESTS}/DequantizeTests.cs")
+    ln_off, loff = find(dq, r"const int OffX = ")
+    offsets = {k: int(v) for k, v in re.findall(r"(Off\w)\s*=\s*(\d+)", loff)}
+    ln_c, _ = find(dq, r"\(int\[\] Shape, int Axis, bool PerAxis\)\[\] cases =")
+    body = " ".join(dq[ln_c - 1: ln_c + 4])
+    qcases = [([int(v) for v in sh.split(",")], int(ax), cs_bool(pa))
+              for sh, ax, pa in re.findall(r"\(\[([\d,\s]+)\],\s*(-?\d+),\s*(true|false)\)", body)]
+    ln_s, ls = find(dq, r"float\[\]\[\] scaleSets = ")
+    sets = []
+    for grp in re.findall(r"\[([^\[\]]+)\]", ls[ls.index("= [") + 2:]):
+        vals = []
+        for tok in grp.split(","):
+            tok = tok.strip()
+            if "/" in tok:
+                num, den = tok.split("/")
+                vals.append(float(np.float32(cs_float(num)) / np.float32(cs_float(den))))
+            else:
+                vals.append(cs_float(tok))
+        sets.append(vals)
+    dq_expect = []
+    for kind, seed0 in (("u8", 1), ("s8", 100), ("i32", 200)):
+        seed = seed0
+        for shape_, axis, per_axis in qcases:
+            for with_zero in (True, False):
+                for half in (False, True):
+                    n = int(np.prod(shape_))
+                    if n <= 64:
+                        ax = axis + len(shape_) if axis < 0 else axis
+                        axis_len = shape_[ax] if per_axis else 1
+                        inner = int(np.prod(shape_[ax + 1:])) if per_axis and ax + 1 < len(shape_) else 1
+                        x = quantized(kind, n + offsets["OffX"], seed)
+                        sc = rig_random(axis_len + offsets["OffS"], seed + 1, 0.001, 2.0)
+                        zs = quantized(kind, axis_len + offsets["OffZ"], seed + 2)
+                        out_vals = []
+                        for j in range(n):
+                            a = (j // inner) % axis_len if per_axis else 0
+                            zp = zs[offsets["OffZ"] + a] if with_zero else 0
+                            out_vals.append(dequantize_reference(x[offsets["OffX"] + j], zp, sc[offsets["OffS"] + a],
+                                                                 half))
+                        dq_expect.append(dict(kind=kind, shape=shape_, axis=axis, per_axis=per_axis,
+                                              with_zero=with_zero, half=half, seed=seed,
+                                              sha256=digest(out_vals, np.uint16 if half else np.uint32)))
+                    seed += 1
+    q_expect = []
+    count = 0
+    seed = 1
+    for shape_, axis, per_axis in qcases:
+        for with_zero in (True, False):
+            scales = sets[count % len(sets)]
+            for signed, half_in in ((False, False), (True, False), (False, True), (True, True)):
+                n = int(np.prod(shape_))
+                if n <= 64:
+                    ax = axis + len(shape_) if axis < 0 else axis
+                    axis_len = shape_[ax] if per_axis else 1
+                    inner = int(np.prod(shape_[ax + 1:])) if per_axis and ax + 1 < len(shape_) else 1
+                    x = quantize_input(n + offsets["OffX"], seed)
+                    if half_in:
+                        x = [float(np.float32(np.float16(np.float32(v)))) for v in x]
+                    sc = [scales[i % len(scales)] for i in range(axis_len + offsets["OffS"])]
+                    zs = quantized("s8" if signed else "u8", axis_len + offsets["OffZ"], seed + 2)
+                    lo, hi = (-128, 127) if signed else (0, 255)
+                    out_vals = []
+                    for j in range(n):
+                        a = (j // inner) % axis_len if per_axis else 0
+                        zp = zs[offsets["OffZ"] + a] if with_zero else 0
+                        out_vals.append(quantize_reference(x[offsets["OffX"] + j], sc[offsets["OffS"] + a], zp, lo, hi)
+                                        & 0xFF)
+                    q_expect.append(dict(signed=signed, half_in=half_in, shape=shape_, axis=axis, per_axis=per_axis,
+                                         with_zero=with_zero, scales=scales, seed=seed,
+                                         sha256=digest(out_vals, np.uint8)))
+                seed += 1
+            count += 4
+    out["dequantize"] = {"cite": f"{REF_TESTS}/DequantizeTests.cs:{ln_off},{ln_c},{ln_s}", "offsets": offsets,
+                         "cases": qcases, "scale_sets": sets, "dequantize_small": dq_expect,
+                         "quantize_small": q_expect}
+
+    # ConvIntegerTests: the geometries of EdgeGeometriesAreBitExact / WhisperStemIsBitExact / ResNetShapesAreBitExact.
+    cv = read(ref, f"{REF_TESTS}/ConvIntegerTests.cs")
+    spreads, named_p = [], {}
+    for i, line in enumerate(cv):
+        m = re.search(r'var (\w+) = P\(([^)]*)\);', line)
+        if m:
+            named_p[m.group(1)] = conv_p(*cs_call_args(m.group(2)))
+        m = re.search(r'^\s*(\w+)\.(\w+) = (-?\d+);', line)
+        if m and m.group(1) in named_p:
+            named_p[m.group(1)][CS_PROPS[m.group(2)]] = int(m.group(3))
+        m = re.search(r'Spread\("([^"]+)",\s*(P|ConvProblem\.Conv1D)\(([^)]*)\)\)', line)
+        if m:
+            maker = conv_p if m.group(2) == "P" else conv_1d
+            spreads.append(dict(name=m.group(1), p=maker(*cs_call_args(m.group(3))), line=i + 1))
+            continue
+        m = re.search(r'Spread\("([^"]+)",\s*(\w+)\)\)', line)
+        if m and m.group(2) in named_p:
+            spreads.append(dict(name=m.group(1), p=dict(named_p[m.group(2)]), line=i + 1))
+    singles = []
+    for i, line in enumerate(cv):
+        m = re.search(r'Name = (\$?)"([^"]+)", P = (P|ConvProblem\.Conv1D)\(([^)]*)\)(.*)\}', line)
+        if not m:
+            continue
+        maker = conv_p if m.group(3) == "P" else conv_1d
+        props = {k: (v == "true" if v in ("true", "false") else v) for k, v in
+                 re.findall(r"(\w+) = (true|false|\d+|fill|\(s & \d\) != 0)", m.group(5))}
+        singles.append(dict(name=m.group(2), templated=bool(m.group(1)), p=maker(*cs_call_args(m.group(4))),
+                            props=props, line=i + 1))
+    ln_f, lf = find(cv, r"foreach \(var fill in new\[\] \{")
+    fills = [int(v) for v in re.findall(r"\d+", lf[lf.index("{"):])]
+    conv_expect = []
+    seed = 100
+    for sp in spreads:
+        for s_ in range(4):
+            c = dict(name=f"{sp['name']} s{s_}", p=sp["p"], x_signed=bool(s_ & 1), w_signed=bool(s_ & 2),
+                     xz_mode=1 - (s_ & 1), wz_mode=(s_ + 1) % 3, seed=seed)
+            p_ = c["p"]
+            oh = conv_extent(p_["h"], p_["kh"], p_["stride_h"], p_["dilation_h"], p_["pad_top"], p_["pad_bottom"])
+            ow = conv_extent(p_["w"], p_["kw"], p_["stride_w"], p_["dilation_w"], p_["pad_left"], p_["pad_right"])
+            macs = p_["batch"] * p_["cout"] * oh * ow * (p_["cin"] // p_["groups"]) * p_["kh"] * p_["kw"]
+            if macs <= 60000:
+                x_len = p_["offset_x"] + p_["batch"] * p_["cin"] * p_["h"] * p_["w"] + 4
+                w_len = p_["offset_w"] + p_["cout"] * (p_["cin"] // p_["groups"]) * p_["kh"] * p_["kw"] + 4
+                x = lcg_bytes(x_len, seed)
+                w = lcg_bytes(w_len, seed + 1)
+                xz = None if c["xz_mode"] == 0 else lcg_bytes(1, seed + 2)
+                wz = None if c["wz_mode"] == 0 else lcg_bytes(p_["cout"] if c["wz_mode"] == 2 else 1, seed + 3)
+                y = conv_reference(p_, x, c["x_signed"], w, c["w_signed"], xz, wz, c["wz_mode"] == 2)
+                c["sha256"] = digest(y, np.int32)
+                conv_expect.append(c)
+            seed += 1
+    out["conv_integer"] = {"cite": f"{REF_TESTS}/ConvIntegerTests.cs:{spreads[0]['line']}-{singles[-1]['line']}",
+                           "spreads": spreads, "singles": singles, "fills": fills, "spread_small": conv_expect}
+
     with open(args.out, "w", encoding="utf-8") as f:
         json.dump(out, f, separators=(",", ":"))
-    print(f"wrote {args.out}: {len(cases)} edge cases, {len(tie_cases)} tie cases")
+    print(f"wrote {args.out}: {len(cases)} edge cases, {len(tie_cases)} tie cases, {len(dq_expect)} dequantize, "
+          f"{len(q_expect)} quantize, {len(conv_expect)} conv cases restated; {len(spreads)} spreads, "
+          f"{len(singles)} single conv cases")
 
 
 if __name__ == "__main__":

@@ -152,3 +152,79 @@ def test_dynamic_quantize_checks():
     assert argument_of(og.check_dynamic_quantize, spec(I32, 16), 0, 4, y, 0, s, 0, z, 0) == (shape, "x")
     assert argument_of(og.check_dynamic_quantize, x, 0, 4, spec(U8, 4, null=True), 0, s, 0, z, 0) == (
         og.ArgumentNullException, "y")
+
+
+def _shape_arg(fn, *args):
+    with pytest.raises(og.GpuKernelShapeException) as info:
+        fn(*args)
+    return info.value.argument
+
+
+def test_dequantize_linear_checks():
+    """DequantizeTests.BadArgumentsAreRejected (DequantizeTests.cs:113-133) on the argument checks alone."""
+    spec = og.buffer_spec
+    x, s, o = spec(np.uint8, 16), spec(np.float32, 4), spec(np.float32, 16)
+    big, ox = spec(np.uint32, 16), spec(np.uint16, 16)
+    chk = og.check_dequantize_linear
+    chk(x, 0, [4, 4], 1, True, s, 0, None, 0, o, 0)
+    assert _shape_arg(chk, x, 0, [4, 4], 1, True, s, 1, None, 0, o, 0) == "scale"
+    assert _shape_arg(chk, x, 0, [4, 4], 5, True, s, 0, None, 0, o, 0) == "axis"
+    assert _shape_arg(chk, x, 8, [4, 4], 0, False, s, 0, None, 0, o, 0) == "x"
+    assert _shape_arg(chk, big, 0, [4], 0, False, s, 0, None, 0, o, 0) == "TIn"
+    assert _shape_arg(chk, x, 0, [4], 0, False, s, 0, None, 0, ox, 0) == "T"
+    # Byte tensors end on a 32-bit word; half outputs too (Check.RangeBytes / Check.Range with half).
+    assert _shape_arg(chk, spec(np.uint8, 6), 0, [5], 0, False, s, 0, None, 0, o, 0) == "x"
+    assert _shape_arg(chk, x, 0, [3], 0, False, s, 0, None, 0, spec(np.float16, 3), 0) == "output"
+    chk(x, 0, [3], 0, False, s, 0, None, 0, spec(np.float16, 4), 0)
+    assert _shape_arg(chk, x, 0, [-1, 4], 0, False, s, 0, None, 0, o, 0) == "shape[0]"
+    assert _shape_arg(chk, x, 0, [4], 0, False, s, 0, spec(np.int8, 4), 0, o, 0) == "zeroPoint"
+    assert _shape_arg(chk, x, 0, [4, 4], -3, True, s, 0, None, 0, o, 0) == "axis"
+    chk(spec(np.int32, 16), 0, [16], 0, False, s, 0, spec(np.int32, 1), 0, o, 0)  # int32: plain ranges
+    with pytest.raises(og.ArgumentNullException):
+        chk(x, 0, [4], 0, False, None, 0, None, 0, o, 0)
+
+
+def test_quantize_linear_checks():
+    """DequantizeTests.QuantizeRejectsBadArguments (DequantizeTests.cs:289-310) on the argument checks alone."""
+    spec = og.buffer_spec
+    x, s, o = spec(np.float32, 16), spec(np.float32, 4), spec(np.uint8, 16)
+    chk = og.check_quantize_linear
+    chk(x, 0, [4, 4], 1, True, s, 0, None, 0, o, 0)
+    assert _shape_arg(chk, x, 0, [4, 4], 1, True, s, 1, None, 0, o, 0) == "scale"
+    assert _shape_arg(chk, x, 0, [4, 4], 5, True, s, 0, None, 0, o, 0) == "axis"
+    assert _shape_arg(chk, x, 8, [4, 4], 0, False, s, 0, None, 0, o, 0) == "x"
+    assert _shape_arg(chk, x, 0, [4, 4], 0, False, s, 0, None, 0, o, 3) == "output"
+    assert _shape_arg(chk, x, 0, [4], 0, False, s, 0, None, 0, spec(np.int16, 16), 0) == "TOut"
+    assert _shape_arg(chk, spec(np.int32, 16), 0, [4], 0, False, s, 0, None, 0, o, 0) == "T"
+    assert _shape_arg(chk, x, 0, [4], 0, False, s, 0, spec(np.int8, 4), 0, o, 0) == "zeroPoint"
+    chk(spec(np.float16, 16), 0, [4, 4], 0, True, s, 0, spec(np.uint8, 4), 0, o, 0)
+
+
+def test_conv_integer_checks():
+    """ConvIntegerTests.BadShapesThrowTypedErrors (ConvIntegerTests.cs:299-323) and the scratch size rule."""
+    spec = og.buffer_spec
+    x, w, y, f = spec(np.uint8, 64), spec(np.int8, 64), spec(np.int32, 64), spec(np.float32, 64)
+    P = og.ConvProblem
+    chk = og.check_conv_integer
+    assert _shape_arg(chk, P(1, 3, 4, 4, 4, 3, 3, groups=2), x, w, y) == "Groups"
+    assert _shape_arg(chk, P(1, 3, 2, 2, 4, 3, 3), x, w, y) == "height"
+    assert _shape_arg(chk, P(1, 3, 8, 8, 4, 3, 3), x, w, y) == "x"
+    assert _shape_arg(chk, P(1, 1, 4, 4, 1, 1, 1), x, w, y, None, og.Int8Operand(w, 64, True)) == "wZeroPoint"
+    assert _shape_arg(chk, P(1, 1, 4, 4, 1, 1, 1), f, w, y) == "x"
+    assert _shape_arg(chk, P(1, 1, 4, 4, 1, 1, 1), x, w, y, None, None, x, 2) == "scratchOffset"
+    chk(P(1, 1, 4, 4, 1, 1, 1), x, w, y, og.Int8Operand(x, 0), og.Int8Operand(w, 0), x, 4)
+    assert _shape_arg(chk, P(1, 1, 4, 4, 1, 1, 1), x, w, y, og.Int8Operand(x, 0, True)) == "xZeroPoint"
+    assert _shape_arg(chk, P(1, 1, 4, 4, 1, 1, 1, activation=1), x, w, y) == "Activation"
+    assert _shape_arg(chk, P(0, 1, 4, 4, 1, 1, 1), x, w, y) == "Batch"
+    assert _shape_arg(chk, P(1, 1, 4, 4, 1, 1, 1, stride_width=0), x, w, y) == "width stride"
+    assert _shape_arg(chk, P(1, 1, 4, 4, 1, 1, 1, pad_top=-1), x, w, y) == "height padding"
+    assert _shape_arg(chk, P(1, 1, 4, 4, 1, 1, 1), x, w, spec(np.float32, 64)) == "y"
+    # One image's columns: Groups * K * ceil(OH * OW / 4) * 4 bytes.
+    assert og.conv_scratch_bytes_per_image(P(2, 4, 9, 11, 5, 3, 3, stride_height=2, stride_width=2, pad_top=1,
+                                                pad_left=1, pad_bottom=1, pad_right=1)) == 36 * 32
+    assert og.conv_scratch_bytes_per_image(P(1, 4, 8, 8, 6, 3, 3, groups=2, pad_top=1, pad_left=1, pad_bottom=1,
+                                                pad_right=1)) == 2 * 18 * 64
+    small = P(3, 3, 8, 8, 4, 3, 3, pad_top=1, pad_left=1, pad_bottom=1, pad_right=1)
+    one = og.conv_scratch_bytes_per_image(small)
+    assert _shape_arg(chk, small, spec(np.uint8, 600), spec(np.int8, 200), spec(np.int32, 800), None, None,
+                      spec(np.uint8, one + 7), 8) == "scratch"

@@ -1,0 +1,144 @@
+"""DequantizeLinear and QuantizeLinear on the GPU against the oracle, bit for bit (DequantizeTests.cs:99-111,
+252-287): every case of the reference's table, per tensor and per axis, with and without a zero point, float32 and
+half, odd offsets, sentinel values around every output."""
+import numpy as np
+import pytest
+
+import og_oracle as oracle
+import onegpu_cuda as og
+from cases import axis_params, golden, quantize_input, quantized
+
+TABLE = golden()["dequantize"]
+OFF = TABLE["offsets"]
+OFFX, OFFS, OFFZ, OFFO = OFF["OffX"], OFF["OffS"], OFF["OffZ"], OFF["OffO"]
+NP = {"u8": np.uint8, "s8": np.int8, "i32": np.int32}
+
+
+def _dequantize_case(device, k, kind, shape, axis, per_axis, with_zero, half, seed):
+    count, axis_len, _ = axis_params(shape, axis, per_axis)
+    x = quantized(kind, count + OFFX, seed)
+    scale = oracle.random(axis_len + OFFS, seed + 1, 0.001, 2.0).astype(np.float32)
+    zeros = quantized(kind, axis_len + OFFZ, seed + 2)
+    out_len = count + OFFO + 1
+    out_len += out_len % 2 if half else 0
+    sentinel = np.full(out_len, -77.0, np.float16 if half else np.float32)
+    bufs = [device.create_buffer(NP[kind], x), device.create_buffer(np.float32, scale),
+            device.create_buffer(NP[kind], zeros), device.create_buffer(sentinel.dtype, sentinel)]
+    bx, bs, bz, bo = bufs
+    try:
+        enc = device.begin_commands()
+        k.encode(enc, bx, OFFX, shape, axis, per_axis, bs, OFFS, bz if with_zero else None, OFFZ, bo, OFFO)
+        device.submit(enc)
+        got = bo.read()
+    finally:
+        for b in bufs:
+            b.dispose()
+    want = oracle.dequantize(x[OFFX:], shape, axis, per_axis, scale[OFFS:], zeros[OFFZ:] if with_zero else None, half)
+    bits = np.uint16 if half else np.uint32
+    bad = int(np.count_nonzero(got[OFFO:OFFO + count].view(bits) != want.view(bits)))
+    guard = np.concatenate([got[:OFFO], got[OFFO + count:]]).view(bits)
+    return bad + int(np.count_nonzero(guard != sentinel[:guard.size].view(bits)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind,seed0", [("u8", 1), ("s8", 100), ("i32", 200)])
+def test_dequantize_is_exact(device, kind, seed0):
+    k = og.DequantizeKernels(device)
+    try:
+        bad, runs, seed = 0, 0, seed0
+        for shape, axis, per_axis in TABLE["cases"]:
+            for with_zero in (True, False):
+                for half in (False, True):
+                    bad += _dequantize_case(device, k, kind, shape, axis, per_axis, with_zero, half, seed)
+                    seed += 1
+                    runs += 1
+        assert runs == 4 * len(TABLE["cases"])
+        assert bad == 0
+    finally:
+        k.dispose()
+
+
+def _quantize_case(device, k, shape, axis, per_axis, with_zero, signed, half_in, scales, seed):
+    count, axis_len, _ = axis_params(shape, axis, per_axis)
+    x = quantize_input(count + OFFX, seed)
+    if half_in:  # Rig.ToHalf: padded to a whole 32-bit word
+        with np.errstate(over="ignore"):
+            x = np.concatenate([x, np.zeros(x.size % 2, np.float32)]).astype(np.float16)
+    scale = np.array([scales[i % len(scales)] for i in range(axis_len + OFFS)], np.float32)
+    zeros = quantized("s8" if signed else "u8", axis_len + OFFZ, seed + 2)
+    out_len = count + OFFO + 3
+    out_len += (-out_len) % 4
+    fill = np.full(out_len, 177, np.uint8) if not signed else np.full(out_len, -77, np.int8)
+    out_t = np.int8 if signed else np.uint8
+    bufs = [device.create_buffer(x.dtype, x), device.create_buffer(np.float32, scale),
+            device.create_buffer(out_t, zeros.view(out_t)), device.create_buffer(out_t, fill)]
+    bx, bs, bz, bo = bufs
+    try:
+        enc = device.begin_commands()
+        k.encode_quantize(enc, bx, OFFX, shape, axis, per_axis, bs, OFFS, bz if with_zero else None, OFFZ, bo, OFFO)
+        device.submit(enc)
+        got = bo.read().view(np.uint8)
+    finally:
+        for b in bufs:
+            b.dispose()
+    want = oracle.quantize(x[OFFX:], shape, axis, per_axis, scale[OFFS:], zeros[OFFZ:] if with_zero else None, signed)
+    bad = int(np.count_nonzero(got[OFFO:OFFO + count] != want))
+    guard = np.concatenate([got[:OFFO], got[OFFO + count:]])
+    return bad + int(np.count_nonzero(guard != fill.view(np.uint8)[:guard.size]))
+
+
+@pytest.mark.gpu
+def test_quantize_is_exact(device):
+    k = og.DequantizeKernels(device)
+    try:
+        sets = TABLE["scale_sets"]
+        bad, count, seed = 0, 0, 1
+        for shape, axis, per_axis in TABLE["cases"]:
+            for with_zero in (True, False):
+                scales = sets[count % len(sets)]
+                for signed, half_in in ((False, False), (True, False), (False, True), (True, True)):
+                    bad += _quantize_case(device, k, shape, axis, per_axis, with_zero, signed, half_in, scales, seed)
+                    seed += 1
+                count += 4
+        assert count == 8 * len(TABLE["cases"])
+        assert bad == 0
+    finally:
+        k.dispose()
+
+
+@pytest.mark.gpu
+def test_large_tensors_per_axis(device):
+    """A 64 Mi-element tensor each way (per-axis over the middle axis, odd offsets), against the oracle."""
+    k = og.DequantizeKernels(device)
+    shape, axis = [64, 1025, 1024], 1
+    count, axis_len, _ = axis_params(shape, axis, True)
+    rng = np.random.default_rng(5)
+    try:
+        # Byte tensors end on a whole 32-bit word (GpuKernelBuffers.PaddedBoolLength).
+        x = rng.integers(-128, 128, size=count + 4, dtype=np.int16).astype(np.int8)
+        scale = rng.uniform(0.001, 2.0, size=axis_len).astype(np.float32)
+        zp = rng.integers(-128, 128, size=axis_len + 3, dtype=np.int16).astype(np.int8)
+        bx, bs, bz = device.create_buffer(np.int8, x), device.create_buffer(np.float32, scale), \
+            device.create_buffer(np.int8, zp)
+        bo = device.create_buffer(np.float16, count + 2)
+        enc = device.begin_commands()
+        k.encode(enc, bx, 3, shape, axis, True, bs, 0, bz, 0, bo, 1)
+        device.submit(enc)
+        got = bo.read()[1:1 + count].view(np.uint16)
+        want = oracle.dequantize(x[3:], shape, axis, True, scale, zp[:axis_len], True)
+        assert np.array_equal(got, want)
+        for b in (bx, bo):
+            b.dispose()
+
+        xf = (rng.standard_normal(count + 5).astype(np.float32) * np.float32(30.0))
+        bx, by = device.create_buffer(np.float32, xf), device.create_buffer(np.int8, count + 8)
+        enc = device.begin_commands()
+        k.encode_quantize(enc, bx, 5, shape, axis, True, bs, 0, bz, 0, by, 7)
+        device.submit(enc)
+        got = by.read().view(np.uint8)[7:7 + count]
+        want = oracle.quantize(xf[5:], shape, axis, True, scale, zp[:axis_len], True)
+        assert np.array_equal(got, want)
+        for b in (bx, by, bs, bz):
+            b.dispose()
+    finally:
+        k.dispose()

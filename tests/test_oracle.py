@@ -150,3 +150,102 @@ def test_dynamic_quantize_edge_values():
     assert s == 1.0 and z == 255 and y.tolist() == [0, 255, 254]
     y, s, z = oracle.dynamic_quantize(np.array([np.inf, 1.0], np.float32))
     assert math.isinf(s) and z == 0 and y.tolist() == [0, 0]
+
+
+# ---- DequantizeLinear / QuantizeLinear / ConvInteger restatements ----------------------------------------------------
+
+def _sha(a) -> str:
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def test_half_conversions_match_ieee():
+    """The oracle's binary16 conversions against numpy's (IEEE round to nearest even), every half and random
+    floats including ties, subnormal results and overflow."""
+    h = np.arange(65536, dtype=np.uint16)
+    h = h[~np.isnan(h.view(np.float16))]
+    got = np.array([oracle.half_to_float(v) for v in h[::7]], np.float32)
+    assert np.array_equal(got.view(np.uint32), h[::7].view(np.float16).astype(np.float32).view(np.uint32))
+    rng = np.random.default_rng(3)
+    f = rng.integers(0, 2**32, size=6000, dtype=np.uint64).astype(np.uint32).view(np.float32)
+    f = np.concatenate([f[~np.isnan(f)], np.array([65504, 65519.99, 65520, 2**-25, 2**-24, 3 * 2**-26, 6.1e-5, -0.0],
+                                                  np.float32)])
+    with np.errstate(over="ignore"):
+        want = f.astype(np.float16).view(np.uint16)
+    assert [oracle.float_to_half(v) for v in f] == want.tolist()
+
+
+def test_dequantize_matches_the_python_restatement():
+    from cases import axis_params, quantized
+
+    g = golden()["dequantize"]
+    off = g["offsets"]
+    assert g["dequantize_small"]
+    for c in g["dequantize_small"]:
+        count, axis_len, inner = axis_params(c["shape"], c["axis"], c["per_axis"])
+        x = quantized(c["kind"], count + off["OffX"], c["seed"])
+        scale = oracle.random(axis_len + off["OffS"], c["seed"] + 1, 0.001, 2.0)
+        zs = quantized(c["kind"], axis_len + off["OffZ"], c["seed"] + 2)
+        got = oracle.dequantize(x[off["OffX"]:], c["shape"], c["axis"], c["per_axis"], scale[off["OffS"]:],
+                                zs[off["OffZ"]:] if c["with_zero"] else None, c["half"])
+        assert _sha(got) == c["sha256"], c
+
+
+def test_quantize_matches_the_python_restatement():
+    from cases import axis_params, quantize_input, quantized
+
+    g = golden()["dequantize"]
+    off = g["offsets"]
+    assert g["quantize_small"]
+    for c in g["quantize_small"]:
+        count, axis_len, inner = axis_params(c["shape"], c["axis"], c["per_axis"])
+        x = quantize_input(count + off["OffX"], c["seed"])
+        if c["half_in"]:
+            with np.errstate(over="ignore"):
+                x = x.astype(np.float16)
+        scale = np.array([c["scales"][i % len(c["scales"])] for i in range(axis_len + off["OffS"])], np.float32)
+        zs = quantized("s8" if c["signed"] else "u8", axis_len + off["OffZ"], c["seed"] + 2)
+        got = oracle.quantize(x[off["OffX"]:], c["shape"], c["axis"], c["per_axis"], scale[off["OffS"]:],
+                              zs[off["OffZ"]:] if c["with_zero"] else None, c["signed"])
+        assert _sha(got) == c["sha256"], c
+
+
+def test_conv_integer_matches_the_python_restatement():
+    from cases import conv_case_data
+
+    cases = golden()["conv_integer"]["spread_small"]
+    assert len(cases) >= 30
+    for c in cases:
+        x, w, xz, wz = conv_case_data(c["p"], c["seed"], c["xz_mode"], c["wz_mode"], -1, oracle.bytes_)
+        y = oracle.conv_integer(c["p"], x, c["x_signed"], w, c["w_signed"], xz, wz, c["wz_mode"] == 2, threads=2)
+        assert _sha(y.astype(np.int32)) == c["sha256"], c["name"]
+
+
+def test_conv_integer_equals_the_int8_product_of_its_columns():
+    """A second route to the same sums: unfold the windows on the host (padding with the zero point of x) and run the
+    oracle's int8 product, as the GPU path does."""
+    p = dict(batch=2, cin=4, h=7, w=6, cout=6, kh=3, kw=2, stride_h=2, stride_w=1, dilation_h=1, dilation_w=2,
+             pad_top=1, pad_left=0, pad_bottom=2, pad_right=1, groups=2, offset_x=0, offset_w=0)
+    rng = np.random.default_rng(9)
+    x = rng.integers(0, 256, size=2 * 4 * 7 * 6, dtype=np.uint16).astype(np.uint8)
+    w = rng.integers(0, 256, size=6 * 2 * 3 * 2, dtype=np.uint16).astype(np.uint8)
+    xz, wz = np.array([131], np.uint8), rng.integers(0, 256, size=6, dtype=np.uint16).astype(np.uint8)
+    want = oracle.conv_integer(p, x, False, w, True, xz, wz, True, threads=1)
+    oh = oracle.conv_out_extent(7, 3, 2, 1, 1, 2)
+    ow = oracle.conv_out_extent(6, 2, 1, 2, 0, 1)
+    xs = x.reshape(2, 4, 7, 6)
+    for n in range(2):
+        for g in range(2):
+            cols = np.full((2 * 3 * 2, oh * ow), 131, np.uint8)
+            for c in range(2):
+                for kh in range(3):
+                    for kw in range(2):
+                        for i in range(oh):
+                            for j in range(ow):
+                                ih, iw = i * 2 + kh - 1, j + kw * 2
+                                if 0 <= ih < 7 and 0 <= iw < 6:
+                                    cols[(c * 3 + kh) * 2 + kw, i * ow + j] = xs[n, g * 2 + c, ih, iw]
+            a = w.reshape(6, 12)[g * 3:(g + 1) * 3]
+            got = oracle.int8_gemm(a.reshape(-1), True, cols.reshape(-1), False, wz[g * 3:(g + 1) * 3], True, xz,
+                                   False, threads=1, m=3, n=oh * ow, k=12)
+            assert np.array_equal(got.reshape(3, oh, ow), want[n, g * 3:(g + 1) * 3])

@@ -1,10 +1,12 @@
 """Benchmark of the int8 GEMM path (BASELINE.json metric: Int8Gemm TOPS at 8192^3 s8 x s8 -> s32).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3|c2|c4|c5|dq] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3|c2|c4|c5|conv|dequant|quant]
+                    [--impl ours|reference]
 
 One step is one Int8Gemm.EncodeInt32 + Submit of the workload (config 3 by default: A int8 [8192 x 8192] x B int8
-[8192 x 8192], zero points absent, int32 C) with inputs resident in HBM; L2 is flushed (a 512 MB write) before every
-step and the step itself is timed with CUDA events on the device stream. With N > 1 (torchrun, one process per GPU,
+[8192 x 8192], zero points absent, int32 C) with inputs resident in HBM; L2 is left cold and clean before every step
+(a 512 MB write, then a 256 MB read of other data, stream-ordered) and the step itself is timed with CUDA events on
+the device stream. With N > 1 (torchrun, one process per GPU,
 NCCL only for the barrier and the max-over-ranks of the times) the product is sharded by onegpu_cuda.shard with no
 collective in the data path ("strong" scaling: the total work is fixed): a batched workload by batch (rank g computes
 its batches from its batches of A and the shared B), the others by 256-column slabs of B (rank g computes its columns
@@ -42,6 +44,20 @@ WORKLOADS = {
                desc="batched QKV u8 (zp) x shared s8 (per-column zp) -> s32, 8 x 2048 x 12288 x 4096"),
     "c5": dict(m=16, n=28672, k=8192, batch=1, a_signed=False, zp=True, out="i32",
                desc="decode u8 (zp 128) x s8 (per-column zp) -> s32, 16 x 28672 x 8192"),
+}
+
+# The other kernel families of the path (not BASELINE configs): measured the same way, one JSON line each.
+FAMILIES = {
+    "conv": dict(metric="ConvInteger TOPS", unit="TOPS", bound="tensor",
+                 desc="ConvInteger, Whisper-small encoder conv2 at batch 8: u8 x [8, 768, 3000] (zp) * s8 "
+                      "[768, 768, 3] (per-channel zp), stride 2, pad 1 -> int32 [8, 768, 1500]",
+                 batch=8, cin=768, length=3000, cout=768, kernel=3, stride=2, pad=1),
+    "dequant": dict(metric="DequantizeLinear GB/s", unit="GB/s", bound="hbm",
+                    desc="DequantizeLinear int8 [8192, 8192] per axis 1 (scale + int8 zero point per column) -> "
+                         "float32", shape=[8192, 8192], axis=1),
+    "quant": dict(metric="QuantizeLinear GB/s", unit="GB/s", bound="hbm",
+                  desc="QuantizeLinear float32 [8192, 8192] ~ N(0, 30) per tensor -> uint8 with zero point 128",
+                  shape=[8192, 8192], axis=0),
 }
 
 
@@ -150,6 +166,256 @@ def cpu_gemm_tops(n: int, k: int, threads: int, target_s: float, max_rows: int, 
         rows = int(min(max_rows, max(rows * 2, rows * target_s / max(dt, 1e-3) * 0.9)))
 
 
+class L2Flush:
+    """Leaves L2 cold and clean before a timed step: a 512 MB write evicts the workload's lines, then a 256 MB read
+    of other data evicts the write's dirty lines (their write-back happens here, outside the timed region, instead of
+    inside the first kernel of the step). Runs on the library device's own stream, so it is stream-ordered before
+    the step without host synchronisation."""
+
+    def __init__(self, dev, local_rank: int):
+        import torch
+
+        self.torch = torch
+        d = torch.device(f"cuda:{local_rank}")
+        self.stream = torch.cuda.ExternalStream(dev.stream, device=d)
+        self.write = torch.empty(512 << 20, dtype=torch.uint8, device=d)
+        self.read = torch.ones((256 << 20) // 4, dtype=torch.float32, device=d)
+        self.sink = torch.empty((), dtype=torch.float32, device=d)
+        torch.cuda.synchronize(d)
+
+    def __call__(self, i: int = 0) -> None:
+        with self.torch.cuda.stream(self.stream):
+            self.write.fill_(i & 0xFF)
+            self.torch.sum(self.read, dim=0, out=self.sink)
+
+    DESCRIPTION = "flushed before every step (512 MB write, then a 256 MB read of other data so that no dirty line " \
+                  "remains), steps timed by CUDA events"
+
+
+def family_inputs(name: str):
+    """Seeded synthetic inputs of a family workload (host arrays) and its algorithmic work per step."""
+    f = FAMILIES[name]
+    rng = np.random.default_rng(77)
+    if name == "conv":
+        B, C, L, O, Kw = f["batch"], f["cin"], f["length"], f["cout"], f["kernel"]
+        ow = (L + 2 * f["pad"] - Kw) // f["stride"] + 1
+        x = rng.integers(0, 256, size=B * C * L, dtype=np.int16).astype(np.uint8)
+        w = rng.integers(-127, 128, size=O * C * Kw, dtype=np.int16).astype(np.int8)
+        wz = rng.integers(-8, 9, size=O, dtype=np.int16).astype(np.int8)
+        return dict(x=x, w=w, xz=np.array([128, 0, 0, 0], np.uint8), wz=wz, ow=ow,
+                    work=2.0 * B * O * ow * C * Kw, y_elems=B * O * ow)
+    shape = f["shape"]
+    count = int(np.prod(shape))
+    if name == "dequant":
+        x = rng.integers(-128, 128, size=count, dtype=np.int16).astype(np.int8)
+        scale = rng.uniform(0.001, 0.02, size=shape[1]).astype(np.float32)
+        zp = rng.integers(-8, 9, size=shape[1], dtype=np.int16).astype(np.int8)
+        return dict(x=x, scale=scale, zp=zp, count=count, work=5.0 * count)
+    x = (rng.standard_normal(count, dtype=np.float32) * np.float32(30.0))
+    return dict(x=x, scale=np.array([0.25], np.float32), zp=np.array([128, 0, 0, 0], np.uint8), count=count,
+                work=5.0 * count)
+
+
+def cpu_family(name: str, threads: int, target_s: float):
+    """The oracle's restatement of the reference's CPU definition on a bounded sample: (value, cores, sample)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import og_oracle as oracle
+
+    f = FAMILIES[name]
+    d = family_inputs(name)
+    if name == "conv":
+        p = dict(batch=1, cin=f["cin"], h=1, w=f["length"], cout=f["cout"], kh=1, kw=f["kernel"], stride_h=1,
+                 stride_w=f["stride"], pad_left=f["pad"], pad_right=f["pad"])
+        one = d["x"][: f["cin"] * f["length"]]
+        t0 = time.perf_counter()
+        oracle.conv_integer(p, one, False, d["w"], True, d["xz"][:1], d["wz"], True, threads=threads)
+        dt = time.perf_counter() - t0
+        return d["work"] / f["batch"] / dt / 1e12, threads, f"1 of {f['batch']} images ({dt:.1f} s), direct " \
+            f"convolution og_oracle_conv_integer (restates ConvIntegerTests.Reference) on {threads} threads"
+    n = min(d["count"], 1 << 23)
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        if name == "dequant":
+            oracle.dequantize(d["x"][:n], [n // f["shape"][1], f["shape"][1]], 1, True, d["scale"], d["zp"])
+        else:
+            oracle.quantize(d["x"][:n], [n], 0, False, d["scale"], d["zp"][:1])
+        reps += 1
+        dt = time.perf_counter() - t0
+        if dt >= target_s:
+            break
+    return 5.0 * n * reps / dt / 1e9, 1, f"{reps} x {n} elements ({dt:.1f} s) through the oracle's scalar " \
+        f"restatement of the reference's CPU definition, 1 thread"
+
+
+def run_family_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    f = FAMILIES[args.workload]
+    threads = os.cpu_count() or 1
+    values, cores, sample = [], 1, ""
+    for _ in range(args.warmup):
+        cpu_family(args.workload, threads, 0.05)
+    for _ in range(args.steps):
+        v, cores, sample = cpu_family(args.workload, threads, max(0.5, args.cpu_seconds / max(args.steps, 1)))
+        values.append(v)
+    v = statistics.median(values)
+    d = family_inputs(args.workload)
+    line = {"metric": f["metric"], "impl": "reference", "value": round(v, 6), "unit": f["unit"], "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(d["work"] / (v * (1e12 if f["unit"] == "TOPS" else 1e9)) * 1e3, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "data": "synthetic",
+            "dtype": "int8" if args.workload == "conv" else "f32/u8",
+            "config": {"workload": f"{args.workload}: {f['desc']}", "parallelism": "host threads"},
+            "cpu_baseline": {"value": round(v, 6), "unit": f["unit"], "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(v, 6), "unit": f["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_family(args, rank: int, world: int, local_rank: int):
+    """One step = one encode + submit of the family's operation on inputs resident in HBM, L2 flushed before it."""
+    import ctypes
+
+    import onegpu_cuda as og
+
+    if world > 1:
+        raise SystemExit(f"{args.workload} is measured on one GPU")
+    f = FAMILIES[args.workload]
+    d = family_inputs(args.workload)
+    dev = og.GpuDevice(local_rank)
+    bufs = []
+
+    def buf(dtype, data_or_len):
+        b = dev.create_buffer(dtype, data_or_len)
+        bufs.append(b)
+        return b
+
+    if args.workload == "conv":
+        problem = og.ConvProblem.conv1d(f["batch"], f["cin"], f["length"], f["cout"], f["kernel"], stride=f["stride"],
+                                        pad_begin=f["pad"], pad_end=f["pad"])
+        x, w = buf(np.uint8, d["x"]), buf(np.int8, d["w"])
+        xz, wz = buf(np.uint8, d["xz"]), buf(np.int8, d["wz"])
+        y = buf(np.int32, d["y_elems"])
+        op = og.ConvIntegerKernels(dev)
+        inputs, outputs = [(x, d["x"])], [(y, d["y_elems"] * 4)]
+
+        def encode(enc):
+            op.encode(enc, problem, x, w, y, og.Int8Operand(xz, 0), og.Int8Operand(wz, 0, True))
+    else:
+        op = og.DequantizeKernels(dev)
+        shape = f["shape"]
+        if args.workload == "dequant":
+            x, s, z = buf(np.int8, d["x"]), buf(np.float32, d["scale"]), buf(np.int8, d["zp"])
+            y = buf(np.float32, d["count"])
+            outputs = [(y, d["count"] * 4)]
+
+            def encode(enc):
+                op.encode(enc, x, 0, shape, f["axis"], True, s, 0, z, 0, y, 0)
+        else:
+            x, s, z = buf(np.float32, d["x"]), buf(np.float32, d["scale"]), buf(np.uint8, d["zp"])
+            y = buf(np.uint8, d["count"])
+            outputs = [(y, d["count"])]
+
+            def encode(enc):
+                op.encode_quantize(enc, x, 0, shape, f["axis"], False, s, 0, z, 0, y, 0)
+        inputs = [(x, d["x"])]
+
+    flush = L2Flush(dev, local_rank)
+    stamps = og.GpuTimestampSet(dev, 2 * args.steps)
+
+    def step(i=None):
+        flush(i if i is not None else 0)
+        enc = dev.begin_commands()
+        if i is not None:
+            enc.write_timestamp(stamps, 2 * i)
+        encode(enc)
+        if i is not None:
+            enc.write_timestamp(stamps, 2 * i + 1)
+        n = enc.dispatch_count
+        dev.submit(enc)
+        return n
+
+    for _ in range(args.warmup):
+        step()
+    dev.wait_idle()
+    launches = 0
+    with ClockSampler(local_rank) as clocks:
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            launches += step(i)
+        dev.wait_idle()
+        wall = time.perf_counter() - t0
+    ts = stamps.read(0)
+    per_step = [ts[2 * i + 1] - ts[2 * i] for i in range(args.steps)]
+    total_ns = sum(per_step)
+    scale_unit = 1e12 if f["unit"] == "TOPS" else 1e9
+    value = d["work"] * args.steps / (total_ns * 1e-9) / scale_unit
+
+    # e2e: the same operation through the C ABI from pinned host memory, inputs uploaded and outputs read back.
+    h2d = sum(a.nbytes for _, a in inputs)
+    d2h = sum(n for _, n in outputs)
+    pin = ctypes.c_void_p()
+    og._check(og._lib.og_host_alloc(h2d + d2h, ctypes.byref(pin)))
+    off = 0
+    for _, a in inputs:
+        ctypes.memmove(pin.value + off, a.ctypes.data, a.nbytes)
+        off += a.nbytes
+    e2e_steps = min(args.steps, 20)
+    e2e_stamps = og.GpuTimestampSet(dev, 2 * e2e_steps)
+    for i in range(-1, e2e_steps):
+        if i >= 0:
+            dev.timestamp(e2e_stamps, 2 * i)
+        off = 0
+        for b, a in inputs:
+            og._check(og._lib.og_buffer_write(dev.handle, b.ptr, pin.value + off, a.nbytes))
+            off += a.nbytes
+        enc = dev.begin_commands()
+        encode(enc)
+        dev.submit(enc)
+        for b, n in outputs:
+            og._check(og._lib.og_buffer_read(dev.handle, pin.value + h2d, b.ptr, n))
+        if i >= 0:
+            dev.timestamp(e2e_stamps, 2 * i + 1)
+    ets = e2e_stamps.read(0)
+    e2e_ns = sum(ets[2 * i + 1] - ets[2 * i] for i in range(e2e_steps)) / e2e_steps
+    og._check(og._lib.og_host_free(pin))
+
+    peaks = load_peaks()
+    sustained = total_ns * 1e-9 > 1.0 or wall > 1.0
+    if f["bound"] == "tensor":
+        peak = 2.0 * (peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"])
+        roof = {"bound": "tensor", "unit": "TOPS", "peak_source": f"2 x {peaks['source']} dense bf16 "
+                f"{'sustained' if sustained else 'burst'}: the int8 dense rate is twice bf16 on B200"}
+    else:
+        peak = peaks["hbm_gbs"]
+        roof = {"bound": "hbm", "unit": "GB/s", "peak_source": f"{peaks['source']} HBM copy bandwidth"}
+    achieved = d["work"] / (statistics.mean(per_step) * 1e-9) / scale_unit
+    roof.update({"achieved": round(achieved, 3), "peak": round(peak, 1), "frac": round(achieved / peak, 4),
+                 "traffic": None})
+    cpu = None
+    if not args.no_cpu:
+        v, cores, sample = cpu_family(args.workload, os.cpu_count() or 1, args.cpu_seconds)
+        cpu = {"value": round(v, 6), "unit": f["unit"], "cores": cores, "kind": "port", "sample": sample}
+    line = {"metric": f["metric"], "value": round(value, 3), "unit": f["unit"], "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ns / args.steps / 1e6, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8" if args.workload == "conv" else "f32/u8",
+            "data": "synthetic",
+            "config": {"workload": f"{args.workload}: {f['desc']}", "parallelism": "single GPU",
+                       "l2": L2Flush.DESCRIPTION},
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": round(d["work"] / (e2e_ns * 1e-9) / scale_unit, 3), "unit": f["unit"],
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": int(launches), "clocks": clocks.summary(), "wall_s": round(wall, 3)}
+    print(json.dumps(line), flush=True)
+    op.dispose()
+    stamps.dispose()
+    e2e_stamps.dispose()
+    for b in bufs:
+        b.dispose()
+    dev.dispose()
+
+
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
@@ -234,7 +500,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         s = dev.create_buffer(np.float32, rng.uniform(0.001, 0.02, size=shard_n).astype(np.float32) * 0.02)
         scale = og.Int8Operand(s, 0, True)
         extra.append(s)
-    flush = dev.create_buffer(np.uint8, 512 << 20)
+    flush = L2Flush(dev, local_rank)
     prob = og.Int8GemmProblem(M, shard_n, K, batch=B_local, stride_a=M * K if B_local > 1 else 0, stride_b=0)
     gemm = og.Int8Gemm(dev)
 
@@ -251,7 +517,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
     stamps = og.GpuTimestampSet(dev, 2 * args.steps)
 
     def step(i=None):
-        flush.fill(i if i is not None else 0)
+        flush(i if i is not None else 0)
         enc = dev.begin_commands()
         if i is not None:
             enc.write_timestamp(stamps, 2 * i)
@@ -368,7 +634,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
             "config": {"workload": f"{args.workload}: {w['desc']}", "m": M, "n": N, "k": K, "batch": B,
                        "parallelism": (f"{'batch' if by_batch else 'N'}-shard x{world}" if world > 1
                                        else "single GPU"),
-                       "l2": "flushed before every step (512 MB write), steps timed by CUDA events",
+                       "l2": L2Flush.DESCRIPTION,
                        "kernel": kernel, "variant": gemm.variant},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 1), "unit": "TOPS",
                          "frac": round(achieved / peak, 4), "traffic": profile_traffic(args.workload),
@@ -386,7 +652,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
             "wall_s": round(wall, 3),
         }
         print(json.dumps(line), flush=True)
-    for v in [a, b, c, flush] + extra:
+    for v in [a, b, c] + extra:
         v.dispose()
     if dq is not None:
         dq.dispose()
@@ -402,7 +668,7 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="c3", choices=sorted(WORKLOADS) + sorted(FAMILIES))
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-library", action="store_true")
@@ -410,6 +676,12 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.workload in FAMILIES:
+        if args.impl == "reference":
+            run_family_reference(args, rank, world)
+        else:
+            run_family(args, rank, world, local_rank)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return

@@ -187,6 +187,8 @@ typedef struct og_int8_gemm_options {
     int32_t allow_packed_dot;
     int32_t kernel;
     int32_t tile;
+    int32_t stream_k;  /* test hook: 0 and 1 give every SM pair whole tiles; 2 splits the (tile, K block) work evenly
+                        * across the SM pairs (stream-K) whenever the shape allows */
 } og_int8_gemm_options;
 
 /* new Int8Gemm(device, options) (Int8Gemm.cs:153-177). options may be NULL (defaults). */
@@ -195,7 +197,8 @@ OG_API og_status og_int8_gemm_create(og_device* device, const og_int8_gemm_optio
 OG_API og_status og_int8_gemm_destroy(og_int8_gemm* gemm);
 /* Int8Gemm.Variant (Int8Gemm.cs:215). */
 OG_API og_status og_int8_gemm_variant(og_int8_gemm* gemm, char* buffer, uint64_t capacity);
-/* The kernel the last encode call recorded ("tensor-core-2sm", "tensor-core-1sm", "portable" or "none"). */
+/* The kernel the last encode call recorded: "tensor-core-2sm" or "tensor-core-1sm" (with "-stream-k" when the
+ * product's (tile, K block) work was split evenly across the SMs), "tensor-core-rows", "portable" or "none". */
 OG_API og_status og_int8_gemm_last_kernel(og_int8_gemm* gemm, char* buffer, uint64_t capacity);
 /* Int8Gemm.ScratchElements (Int8Gemm.cs:531). */
 OG_API int64_t og_int8_gemm_scratch_elements(const og_int8_gemm_problem* problem);

@@ -143,10 +143,13 @@ struct og_int8_gemm {
     bool allow_dot = true;
     int kernel = OG_KERNEL_AUTO;
     int tile = 0;
+    int stream_k = 0;  // 0 by size, 1 never, 2 whenever possible
     std::string variant;
     std::string last = "none";
     std::vector<void*> scratch;  // int32 byte-sum buffers; older ones live until destroy (recorded work may name them)
     int64_t scratch_elements = 0;
+    void* sk_buf = nullptr;      // stream-K hand-over buffer of the tensor-core product, allocated on first need
+    int64_t sk_bytes = 0;
 };
 
 struct og_dynamic_quantize {
@@ -398,6 +401,7 @@ og::GemmLaunch make_launch(og_int8_gemm* g, const og_int8_gemm_problem* p, const
     L.num_sms = g->device->sm_count;
     L.error_flag = g->device->status;
     L.tile = g->tile;
+    L.stream_k = g->stream_k;
     og::Epilogue& e = L.epi;
     e.out_kind = out_kind;
     const int esize = out_kind == og::OUT_I32 || out_kind == og::OUT_F32 ? 4 : 1;
@@ -488,10 +492,24 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
         enc->ops.push_back(std::move(sums));
         enc->dispatches += 1;
     }
+    const bool stream_k = og::sk_wanted(L);
+    if (stream_k) {
+        // Products whose last wave of tiles would leave SMs idle split the (tile, K block) work evenly across the
+        // workers; split tiles meet through this buffer. Recorded launches of one instance run in stream order, so
+        // they share it.
+        if (g->sk_buf == nullptr) {
+            const int64_t bytes = og::sk_bytes_needed(L.num_sms);
+            check_cuda(cudaMalloc(&g->sk_buf, static_cast<size_t>(bytes)), "Int8Gemm stream-K buffer");
+            check_cuda(cudaMemset(g->sk_buf, 0, static_cast<size_t>(bytes)), "Int8Gemm stream-K buffer");
+            g->sk_bytes = bytes;
+        }
+        og::sk_bind(L, g->sk_buf, g->sk_bytes);
+    }
     cudaError_t err;
     og::LaunchFn fn = og::prepare_gemm_tc(L, &err);  // tensor maps built now, at record time
     check_cuda(err, "Int8Gemm tensor maps");
-    g->last = og::tc_cta_group(L) == 2 ? "tensor-core-2sm" : "tensor-core-1sm";
+    g->last = std::string(og::tc_cta_group(L) == 2 ? "tensor-core-2sm" : "tensor-core-1sm") +
+              (stream_k ? "-stream-k" : "");
     enc->ops.push_back(std::move(fn));
     enc->dispatches += 1;
 }
@@ -807,6 +825,9 @@ OG_API og_status og_int8_gemm_create(og_device* d, const og_int8_gemm_options* o
         g->allow_dot = options == nullptr || options->allow_packed_dot != 0;
         g->kernel = options == nullptr ? OG_KERNEL_AUTO : options->kernel;
         g->tile = options == nullptr ? 0 : options->tile;
+        g->stream_k = options == nullptr ? 0 : options->stream_k;
+        if (g->stream_k < 0 || g->stream_k > 2)
+            throw OgError{OG_ERROR_ARGUMENT_RANGE, kGemm, "StreamK", "the stream-K hook takes 0, 1 or 2", "", "", ""};
         if (g->tile != 0 && g->tile != 128 && g->tile != 256) {
             delete g;
             throw OgError{OG_ERROR_ARGUMENT_RANGE, kGemm, "Tile", "the tile hook takes 0, 128 or 256", "", "", ""};
@@ -832,6 +853,7 @@ OG_API og_status og_int8_gemm_destroy(og_int8_gemm* g) {
         use(g->device);
         cudaStreamSynchronize(g->device->stream);
         for (void* p : g->scratch) cudaFree(p);
+        if (g->sk_buf != nullptr) cudaFree(g->sk_buf);
         delete g;
     });
 }

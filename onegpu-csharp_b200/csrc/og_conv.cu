@@ -84,13 +84,86 @@ __global__ void __launch_bounds__(PACK_THREADS) conv_pack_kernel(const PackArgs 
         *reinterpret_cast<uint32_t*>(dst) = word[0];
 }
 
-static cudaError_t launch_conv_pack(const PackArgs& a, cudaStream_t s) {
-    const unsigned blocks = static_cast<unsigned>((a.units + PACK_THREADS - 1) / PACK_THREADS);
-    if (a.ld % 16 == 0 && (reinterpret_cast<uintptr_t>(a.cols) & 15) == 0) {
-        conv_pack_kernel<16><<<blocks, PACK_THREADS, 0, s>>>(a);
+constexpr int PLANE_SMEM_MAX = 48 * 1024;  // planes up to this size are staged in shared memory
+
+// One CTA per input plane (image, group, channel c): the plane is read once, with coalesced loads, into shared
+// memory; then the CTA writes the KH * KW rows of the column matrix that plane feeds (rows c * KH * KW ..), BYTES
+// columns per thread and store, every byte gathered from shared memory.
+template <int BYTES>
+__global__ void __launch_bounds__(PACK_THREADS) conv_pack_plane_kernel(const PackArgs a) {
+    extern __shared__ uint8_t plane_s[];
+    const int64_t plane = blockIdx.x;  // (image * groups + g) * cin_g + c
+    const int32_t c = static_cast<int32_t>(plane % a.cin_g);
+    const int64_t ig = plane / a.cin_g;
+    const int64_t img = ig / a.groups;
+    const int32_t g = static_cast<int32_t>(ig - img * a.groups);
+    const int32_t hw = a.h * a.w;
+    const uint8_t* src = a.x + (img * a.cin + g * a.cin_g + c) * static_cast<int64_t>(hw);
+    if ((reinterpret_cast<uintptr_t>(src) & 3) == 0) {
+        const int32_t words = hw >> 2;
+        for (int32_t i = threadIdx.x; i < words; i += PACK_THREADS)
+            reinterpret_cast<uint32_t*>(plane_s)[i] = __ldg(reinterpret_cast<const uint32_t*>(src) + i);
+        for (int32_t i = (words << 2) + threadIdx.x; i < hw; i += PACK_THREADS) plane_s[i] = __ldg(src + i);
     } else {
-        conv_pack_kernel<4><<<blocks, PACK_THREADS, 0, s>>>(a);
+        for (int32_t i = threadIdx.x; i < hw; i += PACK_THREADS) plane_s[i] = __ldg(src + i);
     }
+    __syncthreads();
+    const uint32_t pad = a.zp != nullptr ? __ldg(a.zp) : 0u;
+    const int32_t taps = a.kh * a.kw;
+    const int32_t ncols = a.oh * a.ow;
+    const int64_t items = static_cast<int64_t>(taps) * a.units_per_row;
+    uint8_t* rows0 = a.cols + (ig * a.rows + static_cast<int64_t>(c) * taps) * a.ld;
+    for (int64_t it = threadIdx.x; it < items; it += PACK_THREADS) {
+        const int32_t kk = static_cast<int32_t>(it / a.units_per_row);
+        const int32_t col0 = static_cast<int32_t>(it - static_cast<int64_t>(kk) * a.units_per_row) * BYTES;
+        const int32_t kh = kk / a.kw;
+        const int32_t kw = kk - kh * a.kw;
+        int32_t oy = col0 / a.ow;
+        int32_t ox = col0 - oy * a.ow;
+        uint32_t word[BYTES / 4];
+#pragma unroll
+        for (int q = 0; q < BYTES / 4; q++) word[q] = 0;
+#pragma unroll
+        for (int e = 0; e < BYTES; e++) {
+            uint32_t v = pad;
+            if (col0 + e < ncols) {
+                const int32_t iy = oy * a.sh + kh * a.dh - a.ph;
+                const int32_t ix = ox * a.sw + kw * a.dw - a.pw;
+                if (static_cast<uint32_t>(iy) < static_cast<uint32_t>(a.h) &&
+                    static_cast<uint32_t>(ix) < static_cast<uint32_t>(a.w))
+                    v = plane_s[iy * a.w + ix];
+            }
+            word[e >> 2] |= v << (8 * (e & 3));
+            if (++ox == a.ow) {
+                ox = 0;
+                oy++;
+            }
+        }
+        uint8_t* dst = rows0 + static_cast<int64_t>(kk) * a.ld + col0;
+        if constexpr (BYTES == 16)
+            *reinterpret_cast<uint4*>(dst) = make_uint4(word[0], word[1], word[2], word[3]);
+        else
+            *reinterpret_cast<uint32_t*>(dst) = word[0];
+    }
+}
+
+static cudaError_t launch_conv_pack(const PackArgs& a, int64_t planes, cudaStream_t s) {
+    const bool wide = a.ld % 16 == 0 && (reinterpret_cast<uintptr_t>(a.cols) & 15) == 0;
+    const int32_t hw = a.h * a.w;
+    if (hw <= PLANE_SMEM_MAX && planes <= 0x7FFFFFFF) {
+        const unsigned grid = static_cast<unsigned>(planes);
+        const size_t smem = static_cast<size_t>((hw + 15) & ~15);
+        if (wide)
+            conv_pack_plane_kernel<16><<<grid, PACK_THREADS, smem, s>>>(a);
+        else
+            conv_pack_plane_kernel<4><<<grid, PACK_THREADS, smem, s>>>(a);
+        return cudaGetLastError();
+    }
+    const unsigned blocks = static_cast<unsigned>((a.units + PACK_THREADS - 1) / PACK_THREADS);
+    if (wide)
+        conv_pack_kernel<16><<<blocks, PACK_THREADS, 0, s>>>(a);
+    else
+        conv_pack_kernel<4><<<blocks, PACK_THREADS, 0, s>>>(a);
     return cudaGetLastError();
 }
 
@@ -425,7 +498,8 @@ OG_API og_status og_conv_integer_encode(og_conv_integer* cv, og_encoder* enc, co
             a.dw = p.dilation_width;
             a.ph = p.pad_top;
             a.pw = p.pad_left;
-            enc->ops.push_back([=](cudaStream_t s) { return og::launch_conv_pack(a, s); });
+            const int64_t planes = images * p.groups * cin_g;
+            enc->ops.push_back([=](cudaStream_t s) { return og::launch_conv_pack(a, planes, s); });
             enc->dispatches += 1;
 
             if (p.groups == 1) {

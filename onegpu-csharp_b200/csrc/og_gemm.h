@@ -25,7 +25,19 @@ struct GemmLaunch {
     int num_sms;
     int* error_flag;
     int tile;  // tensor-core tile rows: 0 chooses by size, 128 one CTA per tile, 256 a CTA pair (cta_group::2)
+    int stream_k = 0;  // 2: split the (tile, K block) work evenly across the workers (stream-K); otherwise whole tiles
+    // Stream-K hand-over buffers of the tensor-core product (one device buffer of sk_bytes_needed(num_sms) bytes,
+    // split by sk_bind); null leaves every worker whole tiles.
+    int32_t* sk_part = nullptr;
+    unsigned int* sk_flag = nullptr;
+    int64_t sk_bytes = 0;
 };
+
+// Bytes of the stream-K hand-over buffer for a device with num_sms SMs, and the split of one such buffer.
+int64_t sk_bytes_needed(int num_sms);
+void sk_bind(GemmLaunch& L, void* buffer, int64_t bytes);
+// True when the tensor-core product of L would split tiles between workers (stream-K) given the buffers.
+bool sk_wanted(const GemmLaunch& L);
 
 // A launch whose host-side preparation (tensor maps, parameters) is already done: calling it only launches.
 using LaunchFn = std::function<cudaError_t(cudaStream_t)>;

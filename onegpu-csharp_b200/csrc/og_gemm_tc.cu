@@ -45,8 +45,8 @@ struct Cfg {
     static constexpr int B_BOX = 128 * BK;            // one 128-column box of an MN-major B
     static constexpr int STAGES = CG == 1 ? 4 : 6;
     static constexpr int TERMS_BYTES = 5 * 4 * BN;     // per-column epilogue terms
-    static constexpr int BOX_BYTES = 32 * 128;          // one 32-row x 32-word store box
-    static constexpr int STAGING_BYTES = 4 * BOX_BYTES; // one box per epilogue warp
+    static constexpr int BOX_BYTES = 32 * 64;               // one 32-row x 16-word store box (64-byte rows)
+    static constexpr int STAGING_BYTES = 4 * 2 * BOX_BYTES; // two boxes per epilogue warp
     static constexpr int SMEM_BYTES =
         STAGES * (A_BYTES + B_BYTES) + STAGING_BYTES + 1024 /* alignment */ + 256 /* barriers */ + TERMS_BYTES;
 };
@@ -62,7 +62,92 @@ struct TcParams {
     Epilogue epi;
     int* error_flag;
     int tma_store;  // int32 / float results leave through shared memory and TMA stores (C rows 16-byte aligned)
+    // Stream-K: the workers split the total_tiles * k_blocks (tile, K block) units into equal contiguous ranges. A
+    // tile cut by a range boundary is finished by the worker holding its K-block-0 segment (the end of its range),
+    // after the next worker has handed over the sums of the later segment (the start of its range) through
+    // sk_part[next worker] and set sk_flag[next worker] to this launch's generation. The generation lives after the
+    // flags (with a ticket counter): every CTA reads it when it starts and the last CTA to finish advances it, so no
+    // flag needs clearing between launches, replays of a captured graph included.
+    int stream_k;
+    int64_t units;
+    int32_t* sk_part;       // [slots][CG][8 chunks][8 quads][128 rows][4] int32
+    unsigned int* sk_flag;  // [slots] flags, then the generation and the ticket
+    int sk_slots;
 };
+
+// One piece of a worker's work: K blocks [kb0, kb1) of a tile.
+struct WorkItem {
+    int tile, kb0, kb1;
+};
+
+struct WorkCursor {
+    int64_t u, u1;  // stream-K: the worker's remaining units
+    int tile;       // otherwise: the next tile
+};
+
+__device__ __forceinline__ void work_begin(const TcParams& p, int worker, int workers, WorkCursor& c) {
+    c.u = p.units * worker / workers;
+    c.u1 = p.units * (worker + 1) / workers;
+    c.tile = worker;
+}
+
+__device__ __forceinline__ bool work_next(const TcParams& p, int workers, WorkCursor& c, WorkItem& w) {
+    if (p.stream_k) {
+        if (c.u >= c.u1) return false;
+        w.tile = static_cast<int>(c.u / p.k_blocks);
+        w.kb0 = static_cast<int>(c.u - static_cast<int64_t>(w.tile) * p.k_blocks);
+        const int64_t end = static_cast<int64_t>(w.kb0) + (c.u1 - c.u);
+        w.kb1 = end < p.k_blocks ? static_cast<int>(end) : p.k_blocks;
+        c.u += w.kb1 - w.kb0;
+        return true;
+    }
+    if (c.tile >= p.total_tiles) return false;
+    w.tile = c.tile;
+    w.kb0 = 0;
+    w.kb1 = p.k_blocks;
+    c.tile += workers;
+    return true;
+}
+
+constexpr int SK_SLOT_INTS = 8 * 8 * 128 * 4;  // one CTA's 128 x 256 int32 sums
+constexpr uint32_t SK_SLOT_BYTES = SK_SLOT_INTS * 4;
+
+// The raw sums of the later segment of a split tile, written where the finishing worker reads them: quad v of chunk c
+// of row `row` at ((c * 8 + v) * 128 + row) * 4, so that every warp-wide 16-byte store covers 512 contiguous bytes.
+__device__ __forceinline__ void sk_put(int32_t* slot, int c, int row, const uint32_t (&r)[32]) {
+#pragma unroll
+    for (int v = 0; v < 8; v++)
+        __stcg(reinterpret_cast<int4*>(slot + ((c * 8 + v) * 128 + row) * 4),
+               make_int4(int(r[4 * v]), int(r[4 * v + 1]), int(r[4 * v + 2]), int(r[4 * v + 3])));
+}
+
+// Waits (bounded, like every wait here) until another CTA of the grid has set *flag to `want`; false when the wait
+// gave up or another role of this CTA raised the abort flag.
+__device__ __forceinline__ bool flag_wait(const unsigned int* flag, unsigned int want, volatile int* abort) {
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        unsigned int v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+        if (v == want) return true;
+        if (*abort) return false;
+        if (global_timer_ns() - t0 > OG_WAIT_LIMIT_NS) {
+            *abort = 1;
+            return false;
+        }
+    }
+}
+
+// Adds the handed-over sums (already copied into this CTA's shared memory, same layout) to chunk c of a row.
+__device__ __forceinline__ void sk_add(const int32_t* slot_smem, int c, int row, uint32_t (&r)[32]) {
+#pragma unroll
+    for (int v = 0; v < 8; v++) {
+        const int4 x = *reinterpret_cast<const int4*>(slot_smem + ((c * 8 + v) * 128 + row) * 4);
+        r[4 * v] += uint32_t(x.x);
+        r[4 * v + 1] += uint32_t(x.y);
+        r[4 * v + 2] += uint32_t(x.z);
+        r[4 * v + 3] += uint32_t(x.w);
+    }
+}
 
 template <int BM>
 __device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& b, int& tm, int& tn) {
@@ -137,20 +222,61 @@ __device__ __forceinline__ uint32_t finish_word(const ColTerms& t, const Epilogu
     }
 }
 
-// Finishes 32 consecutive int32 / float results of one row (tile columns j0..) and writes them as row `lane` of a
-// 32 x 32-word box in 128-byte-swizzled shared memory: 16-byte chunk j of the row lands at chunk j ^ (lane % 8), so the
-// eight lanes of each store phase hit eight different bank groups.
+// Finishes 16 consecutive int32 / float results of one row (tile columns j0..) and writes them as row `lane` of a
+// 32 x 16-word box in 64-byte-swizzled shared memory: 16-byte chunk j of the row lands at chunk j ^ ((lane / 2) % 4),
+// so the eight lanes of each store phase hit eight different 16-byte bank groups. The column terms are read four
+// columns per 16-byte shared load.
 template <int OUT>
-__device__ __forceinline__ void stage_chunk(const ColTerms& t, const Epilogue& e, bool terms, bool za_per_row,
-                                            uint32_t za, uint32_t rt, int j0, const uint32_t (&r)[32], uint8_t* box,
-                                            int lane) {
-    uint32_t w[32];
+__device__ __forceinline__ void stage_half(const ColTerms& t, const Epilogue& e, bool terms, bool za_per_row,
+                                           uint32_t za, uint32_t rt, int j0, const uint32_t* r, uint8_t* box,
+                                           int lane) {
+    uint32_t w[16];
+    if (OUT == OUT_I32 && !terms) {
 #pragma unroll
-    for (int q = 0; q < 32; q++) w[q] = finish_word<OUT>(t, e, terms, za_per_row, za, rt, j0 + q, r[q]);
-    const uint32_t row = smem_u32(box) + lane * 128;
+        for (int q = 0; q < 16; q++) w[q] = r[q];
+    } else {
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const uint32_t addr = row + ((j ^ (lane & 7)) << 4);
+        for (int v = 0; v < 4; v++) {
+            const int4 zb = *reinterpret_cast<const int4*>(&t.zb[j0 + 4 * v]);
+            const int4 cc = *reinterpret_cast<const int4*>(&t.c[j0 + 4 * v]);
+            const uint32_t zbv[4] = {uint32_t(zb.x), uint32_t(zb.y), uint32_t(zb.z), uint32_t(zb.w)};
+            const uint32_t ccv[4] = {uint32_t(cc.x), uint32_t(cc.y), uint32_t(cc.z), uint32_t(cc.w)};
+            uint32_t s4[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) s4[u] = r[4 * v + u] + zbv[u] * rt + ccv[u];
+            if (za_per_row) {
+                const int4 cs = *reinterpret_cast<const int4*>(&t.csb[j0 + 4 * v]);
+                s4[0] -= za * uint32_t(cs.x);
+                s4[1] -= za * uint32_t(cs.y);
+                s4[2] -= za * uint32_t(cs.z);
+                s4[3] -= za * uint32_t(cs.w);
+            }
+            if constexpr (OUT == OUT_F32) {
+                const float4 sc = *reinterpret_cast<const float4*>(&t.scale[j0 + 4 * v]);
+                const float scv[4] = {sc.x, sc.y, sc.z, sc.w};
+                float f[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) f[u] = __fmul_rn(__int2float_rn(static_cast<int32_t>(s4[u])), scv[u]);
+                if (e.float_bias != nullptr) {
+                    const float4 fb = *reinterpret_cast<const float4*>(&t.fbias[j0 + 4 * v]);
+                    f[0] = __fadd_rn(f[0], fb.x);
+                    f[1] = __fadd_rn(f[1], fb.y);
+                    f[2] = __fadd_rn(f[2], fb.z);
+                    f[3] = __fadd_rn(f[3], fb.w);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; u++) w[4 * v + u] = __float_as_uint(f[u]);
+            } else {
+#pragma unroll
+                for (int u = 0; u < 4; u++) w[4 * v + u] = s4[u];
+            }
+        }
+    }
+    const uint32_t row = smem_u32(box) + lane * 64;
+    const uint32_t sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t addr = row + ((j ^ sw) << 4);
         asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(w[4 * j]), "r"(w[4 * j + 1]),
                      "r"(w[4 * j + 2]), "r"(w[4 * j + 3])
                      : "memory");
@@ -215,7 +341,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sA = smem;
     uint8_t* sB = smem + C::STAGES * C::A_BYTES;
-    uint8_t* staging = sB + C::STAGES * C::B_BYTES;  // 1024-byte aligned store boxes of the epilogue warps
+    uint8_t* staging = sB + C::STAGES * C::B_BYTES;  // 1024-byte aligned store boxes of the epilogue warps (2 each)
     uint64_t* bars = reinterpret_cast<uint64_t*>(staging + C::STAGING_BYTES);
     uint64_t* full = bars;
     uint64_t* empty = bars + C::STAGES;
@@ -223,6 +349,9 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
     uint64_t* tempty = bars + 2 * C::STAGES + tc::NUM_ACC;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * C::STAGES + 2 * tc::NUM_ACC);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    volatile int* epi_go = reinterpret_cast<volatile int*>(tmem_holder + 2);  // [2]: per tile parity
+    volatile unsigned int* sk_gen = reinterpret_cast<volatile unsigned int*>(tmem_holder + 4);
+    uint64_t* sk_bar = bars + 24;  // byte 192 of the barrier block: the hand-over copy
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -240,7 +369,10 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             mbar_init(&tfull[a], 1);
             mbar_init(&tempty[a], 4 * CG);  // one arrival per epilogue warp of every CTA of the pair
         }
+        mbar_init(sk_bar, 1);
         *abort_flag = 0;
+        // This launch's stream-K generation: flags set to it belong to this launch.
+        *sk_gen = p.stream_k ? __ldcg(p.sk_flag + p.sk_slots) + 1u : 0u;
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -268,9 +400,12 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
     if (warp == 0) {
         // TMA producer: the whole warp walks the ring, lane 0 issues.
         uint32_t it = 0;
-        for (int tile = worker; tile < p.total_tiles; tile += workers) {
+        WorkCursor cur;
+        work_begin(p, worker, workers, cur);
+        WorkItem wi;
+        while (work_next(p, workers, cur, wi)) {
             int b, tm, tn;
-            tile_coords<C::BM>(p, tile, b, tm, tn);
+            tile_coords<C::BM>(p, wi.tile, b, tm, tn);
             const int ba = p.a_batched ? b : 0;
             const int bb = p.b_batched ? b : 0;
             const int row0 = tm * C::BM + static_cast<int>(rank) * 128;
@@ -280,7 +415,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             const bool second_half = CG == 1 && B_MN && (col0 + 128 < p.n);
             const uint32_t bytes = CG == 2 ? 2u * (C::A_BYTES + C::B_BYTES)
                                            : C::A_BYTES + (B_MN ? (second_half ? 2 : 1) * C::B_BOX : C::B_BYTES);
-            for (int kb = 0; kb < p.k_blocks; kb++, it++) {
+            for (int kb = wi.kb0; kb < wi.kb1; kb++, it++) {
                 const int s = it % C::STAGES;
                 const uint32_t ph = (it / C::STAGES) & 1;
                 if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) goto done;
@@ -313,14 +448,16 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         // MMA issuer (the leader CTA of a pair issues for both): four K = 32 MMAs per stage.
         if (leader) {
             uint32_t it = 0;
-            int lt = 0;
-            for (int tile = worker; tile < p.total_tiles; tile += workers, lt++) {
+            WorkCursor cur;
+            work_begin(p, worker, workers, cur);
+            WorkItem wi;
+            for (int lt = 0; work_next(p, workers, cur, wi); lt++) {
                 const int acc = lt & 1;
                 const uint32_t aph = (lt >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) goto done;
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + acc * tc::BN;
-                for (int kb = 0; kb < p.k_blocks; kb++, it++) {
+                for (int kb = wi.kb0; kb < wi.kb1; kb++, it++) {
                     const int s = it % C::STAGES;
                     const uint32_t ph = (it / C::STAGES) & 1;
                     if (!mbar_wait(&full[s], ph, abort_flag)) goto done;
@@ -333,7 +470,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                             const uint64_t adesc = smem_desc_sw128(a_addr + kk * 32, 16, 1024);
                             const uint64_t bdesc = B_MN ? smem_desc_sw128(b_addr + kk * 32 * 128, C::B_BOX, 1024)
                                                         : smem_desc_sw128(b_addr + kk * 32, 16, 1024);
-                            const uint32_t accum = (kb | kk) != 0 ? 1u : 0u;
+                            const uint32_t accum = (kb != wi.kb0 || kk != 0) ? 1u : 0u;
                             if constexpr (CG == 2)
                                 mma_i8_pair(d_tmem, adesc, bdesc, idesc, accum);
                             else
@@ -364,16 +501,67 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         // Column terms are needed unless the result is the raw int32 sum.
         const bool terms = OUT != OUT_I32 || e.za != nullptr || e.zb != nullptr || e.int_bias != nullptr;
         const bool za_per_row = e.za != nullptr && e.za_vector;
-        int lt = 0;
-        for (int tile = worker; tile < p.total_tiles; tile += workers, lt++) {
+        WorkCursor cur;
+        work_begin(p, worker, workers, cur);
+        WorkItem wi;
+        for (int lt = 0; work_next(p, workers, cur, wi); lt++) {
             int b, tm, tn;
-            tile_coords<C::BM>(p, tile, b, tm, tn);
+            tile_coords<C::BM>(p, wi.tile, b, tm, tn);
             const int acc = lt & 1;
             const uint32_t aph = (lt >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], aph, abort_flag)) goto done;
+            // The K-block-0 segment of a split tile (the end of this worker's range) also waits for the next
+            // worker's sums of the later segment. One thread does every wait and publishes the outcome, so the four
+            // warps always leave or continue together (the named barriers below cannot time out).
+            const bool sk_wait = wi.kb0 == 0 && wi.kb1 < p.k_blocks;
+            const int sk_slot = (worker + 1) * CG + static_cast<int>(rank);
+            if (threadIdx.x == 64) {
+                bool ok = mbar_wait(&tfull[acc], aph, abort_flag);
+                if (ok && sk_wait) {
+                    // This is the worker's last item: its MMAs are complete, so the operand ring is idle and takes
+                    // the handed-over sums in one bulk copy.
+                    ok = flag_wait(p.sk_flag + sk_slot, *sk_gen, abort_flag);
+                    if (ok) {
+                        mbar_arrive_expect_tx(sk_bar, SK_SLOT_BYTES);
+                        bulk_load(sA, p.sk_part + static_cast<int64_t>(sk_slot) * SK_SLOT_INTS, SK_SLOT_BYTES, sk_bar);
+                        ok = mbar_wait(sk_bar, 0, abort_flag);
+                    }
+                }
+                epi_go[lt & 1] = ok ? 1 : 0;
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (!epi_go[lt & 1]) goto done;
             tc_fence_after();
-            if (terms) {
-                asm volatile("bar.sync 1, 128;" ::: "memory");  // the previous tile's terms are no longer read
+            const int row_in_cta = q * 32 + lane;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * tc::BN;
+            if (wi.kb0 > 0) {
+                // The later segment of a split tile (the start of this worker's range): hand its raw sums to the
+                // worker that holds K block 0 (the previous one), then flag them.
+                int32_t* slot = p.sk_part + static_cast<int64_t>(worker * CG + static_cast<int>(rank)) * SK_SLOT_INTS;
+#pragma unroll 1
+                for (int c = 0; c < tc::BN / 32; c++) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(t_row + c * 32, r);
+                    tmem_ld_wait();
+                    sk_put(slot, c, row_in_cta, r);
+                }
+                __threadfence();
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (threadIdx.x == 64) {
+                    unsigned int* flag = p.sk_flag + worker * CG + static_cast<int>(rank);
+                    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(*sk_gen) : "memory");
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    if constexpr (CG == 2)
+                        mbar_arrive_cluster(tempty_leader + acc * sizeof(uint64_t));
+                    else
+                        mbar_arrive(&tempty[acc]);
+                }
+                continue;
+            }
+            const int32_t* sk_in = sk_wait ? reinterpret_cast<const int32_t*>(sA) : nullptr;
+            if (terms) {  // every warp has left the previous tile (the barrier above), so its terms are free
                 fill_col_terms(terms_smem, e, b, tn * tc::BN, threadIdx.x - 64, 128);
                 asm volatile("bar.sync 1, 128;" ::: "memory");
             }
@@ -385,11 +573,10 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                 const uint32_t rsa = e.row_sum_a ? row_sum_of(e, b, m) : 0u;
                 rt = static_cast<uint32_t>(p.k) * za - rsa;
             }
-            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * tc::BN;
             if (tma_store) {
-                // Each 32 x 32 chunk goes through this warp's box and leaves as one TMA store of full 128-byte row
-                // segments; rows past M and columns past N are clipped by the tensor map.
-                uint8_t* box = staging + q * C::BOX_BYTES;
+                // Each 32 x 32 chunk leaves as two TMA stores of 32 x 16 words (64-byte row segments) through this
+                // warp's two boxes in turn, so staging one half never waits for the store just issued; rows past M
+                // and columns past N are clipped by the tensor map.
                 const int box_row = tm * C::BM + static_cast<int>(rank) * 128 + q * 32;
 #pragma unroll 1
                 for (int c = 0; c < tc::BN / 32; c++) {
@@ -398,14 +585,22 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_row + c * 32, r);
                     tmem_ld_wait();
-                    if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the box
-                    __syncwarp();
-                    stage_chunk<OUT>(terms_smem, e, terms, za_per_row, za, rt, c * 32, r, box, lane);
-                    fence_proxy_async_smem();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tma_store_3d(&tmap_c, box, n0, box_row, b);
-                        bulk_commit_group();
+                    if (sk_in != nullptr) sk_add(sk_in, c, row_in_cta, r);
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        if (n0 + 16 * h >= p.n) break;
+                        // Alternate boxes: the box about to be written was last stored two boxes ago.
+                        uint8_t* box = staging + (q * 2 + h) * C::BOX_BYTES;
+                        if (lane == 0) bulk_wait_group_read<1>();
+                        __syncwarp();
+                        stage_half<OUT>(terms_smem, e, terms, za_per_row, za, rt, c * 32 + 16 * h, r + 16 * h, box,
+                                        lane);
+                        fence_proxy_async_smem();
+                        __syncwarp();
+                        if (lane == 0) {
+                            tma_store_3d(&tmap_c, box, n0 + 16 * h, box_row, b);
+                            bulk_commit_group();
+                        }
                     }
                 }
             } else {
@@ -416,6 +611,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_row + c * 32, r);
                     tmem_ld_wait();
+                    if (sk_in != nullptr) sk_add(sk_in, c, row_in_cta, r);
                     if (row_ok) store_chunk<OUT>(terms_smem, e, terms, za_per_row, za, rt, b, m, n0, c * 32, r);
                 }
             }
@@ -442,6 +638,15 @@ done:
             tmem_dealloc(tmem_base, tc::TMEM_COLS);
     }
     if (threadIdx.x == 0 && *abort_flag) atomicExch(p.error_flag, 1);
+    if (p.stream_k && threadIdx.x == 0) {
+        // The last CTA to finish advances the generation (every CTA read it when it started) and resets the ticket.
+        unsigned int* gen = p.sk_flag + p.sk_slots;
+        __threadfence();
+        if (atomicAdd(gen + 1, 1u) == gridDim.x - 1) {
+            atomicExch(gen + 1, 0u);
+            atomicAdd(gen, 1u);
+        }
+    }
 }
 
 template <bool B_MN, int OUT>
@@ -487,7 +692,7 @@ static bool make_map(CUtensorMap* map, const void* base, uint64_t x, uint64_t y,
     return r == CUDA_SUCCESS;
 }
 
-// The output C as a 3-D tensor of 4-byte words (columns innermost) stored in 32 x 32-word boxes from 128-byte-swizzled
+// The output C as a 3-D tensor of 4-byte words (columns innermost) stored in 32-row x 16-word boxes from 64-byte-swizzled
 // shared memory.
 static bool make_store_map(CUtensorMap* map, void* base, uint64_t n, uint64_t m, uint64_t batch, uint64_t row_bytes,
                            uint64_t batch_bytes) {
@@ -495,10 +700,10 @@ static bool make_store_map(CUtensorMap* map, void* base, uint64_t n, uint64_t m,
     if (fn == nullptr) return false;
     cuuint64_t dims[3] = {n, m, batch};
     cuuint64_t strides[2] = {row_bytes, batch_bytes};
-    cuuint32_t box[3] = {32, 32, 1};
+    cuuint32_t box[3] = {16, 32, 1};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
 }
 
@@ -557,6 +762,44 @@ static LaunchFn bind_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensor
     };
 }
 
+// Stream-K runs only when asked for (mode 2) and when every worker gets at least one tile's worth of K blocks, so
+// that a tile is split between two workers at most. It is not chosen by size: measured on B200 the int8 product's
+// K-block rate is capped by operand delivery to the SMs rather than by how many SM pairs are busy, so the partial last
+// wave of the data-parallel schedule costs less than the hand-over does (4096^3: 53.2 vs 57.6 us; 8192 x 1024 x 8192:
+// 52.0 vs 60.9 us).
+static bool sk_worthwhile(int64_t tiles, int64_t workers, int mode) {
+    if (mode != 2 || tiles < workers) return false;
+    return tiles % workers != 0;
+}
+
+bool sk_wanted(const GemmLaunch& L) {
+    const int cg = tc_cta_group(L);
+    const int64_t bm = 128 * cg;
+    const int64_t tiles = ((L.m + bm - 1) / bm) * ((L.n + tc::BN - 1) / tc::BN) * int64_t(L.batch);
+    return sk_worthwhile(tiles, L.num_sms / cg, L.stream_k);
+}
+
+// Hand-over slots: one per CTA of the grid plus one pair (slot (worker + 1) * CG + rank is the largest read).
+static int64_t sk_slots(int num_sms) { return int64_t(num_sms) + 2; }
+
+int64_t sk_bytes_needed(int num_sms) {
+    return sk_slots(num_sms) * (SK_SLOT_INTS * int64_t(sizeof(int32_t)) + int64_t(sizeof(unsigned int))) +
+           2 * int64_t(sizeof(unsigned int));  // the generation and the ticket
+}
+
+void sk_bind(GemmLaunch& L, void* buffer, int64_t bytes) {
+    if (buffer == nullptr || bytes < sk_bytes_needed(L.num_sms)) {
+        L.sk_part = nullptr;
+        L.sk_flag = nullptr;
+        L.sk_bytes = 0;
+        return;
+    }
+    L.sk_part = static_cast<int32_t*>(buffer);
+    L.sk_flag = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(buffer) +
+                                                sk_slots(L.num_sms) * SK_SLOT_INTS * int64_t(sizeof(int32_t)));
+    L.sk_bytes = bytes;
+}
+
 template <int CG>
 static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
     using C = tc::Cfg<CG>;
@@ -602,6 +845,13 @@ static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
                                  L.batch > 1 ? uint64_t(L.epi.batch_stride_c) * 4 : round16(uint64_t(L.epi.ldc) * 4 * L.m));
     const int64_t workers = L.num_sms / CG;
     const int grid = static_cast<int>((total < workers ? total : workers) * CG);
+    // Stream-K when it pays (sk_worthwhile) and the caller gave the hand-over buffers.
+    p.units = total * p.k_blocks;
+    p.sk_part = L.sk_part;
+    p.sk_flag = L.sk_flag;
+    p.sk_slots = static_cast<int>(sk_slots(L.num_sms));
+    p.stream_k = L.sk_part != nullptr && sk_bytes_needed(L.num_sms) <= L.sk_bytes &&
+                 sk_worthwhile(total, workers, L.stream_k);
     const bool bmn = !L.trans_b;
     switch (L.epi.out_kind) {
         case OUT_I32: return bmn ? bind_tc_t<CG, true, OUT_I32>(L, p, ma, mb, mc, grid)

@@ -9,9 +9,10 @@
 //     NaN gives the output type's lowest value, then the result is clamped to uint8 / int8.
 //
 // The tensor is seen as [outer, axisLen, inner]; element j uses parameter (j / inner) % axisLen. Both kernels are
-// HBM-bound streams: each thread owns one 16-byte piece of the output (aligned to the output's 16-byte boundaries,
-// so every store of a whole piece is one vector store and no two threads share a byte), reads the inputs it needs
-// and finishes them.
+// HBM-bound streams: consecutive threads take consecutive aligned vectors of input and output (so every warp-wide
+// load and store covers contiguous memory), four vectors in flight per thread, the parameter index walked without a
+// division per element; the few elements before the first aligned vector and after the last go one by one. No two
+// threads write the same byte.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -30,12 +31,29 @@ struct QuantArgs {
     uint32_t axis_len;
     uint32_t inner;
     void* out;            // first output element
-    int64_t pieces;       // 16-byte pieces of the output touched
-    int lead;             // output elements before the first 16-byte boundary at or below out
+    int64_t head;         // elements handled one by one before the first whole vector
+    int64_t vectors;      // whole vectors of E elements after the head
+    int64_t threads;      // threads the launch needs
 };
 
-__device__ __forceinline__ uint32_t param_index(const QuantArgs& a, int64_t j) {
-    return a.per_axis ? (static_cast<uint32_t>(j) / a.inner) % a.axis_len : 0u;  // counts stay below 2^31
+// The parameter (scale / zero point) index of element j and its position inside the current run of `inner` elements;
+// param_next steps both to element j + 1 without a division.
+struct ParamCursor {
+    uint32_t pi, r;
+};
+
+__device__ __forceinline__ ParamCursor param_at(const QuantArgs& a, int64_t j) {
+    if (!a.per_axis) return {0u, 0u};
+    const uint32_t q = static_cast<uint32_t>(j) / a.inner;  // counts stay below 2^31
+    return {q % a.axis_len, static_cast<uint32_t>(j) - q * a.inner};
+}
+
+__device__ __forceinline__ void param_next(const QuantArgs& a, ParamCursor& c) {
+    if (!a.per_axis) return;
+    if (++c.r == a.inner) {
+        c.r = 0;
+        if (++c.pi == a.axis_len) c.pi = 0;
+    }
 }
 
 template <int KIND>  // 0 uint8, 1 int8, 2 int32
@@ -46,46 +64,10 @@ __device__ __forceinline__ int32_t load_q(const void* p, int64_t i) {
 }
 
 template <int KIND>
-__device__ __forceinline__ float dequantize_one(const QuantArgs& a, int64_t j) {
-    const uint32_t pi = param_index(a, j);
-    const int32_t zp = a.zp != nullptr ? load_q<KIND>(a.zp, pi) : 0;
-    const int32_t q = load_q<KIND>(a.x, j);
+__device__ __forceinline__ float dequantize_one(const QuantArgs& a, int32_t q, const ParamCursor& c) {
+    const int32_t zp = a.zp != nullptr ? load_q<KIND>(a.zp, c.pi) : 0;
     const int32_t d = static_cast<int32_t>(static_cast<uint32_t>(q) - static_cast<uint32_t>(zp));
-    return __fmul_rn(__int2float_rn(d), __ldg(a.scale + pi));
-}
-
-template <int KIND, bool HALF>
-__global__ void __launch_bounds__(QTHREADS) dequantize_kernel(const QuantArgs a) {
-    constexpr int V = HALF ? 8 : 4;  // output elements per 16-byte piece
-    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (t >= a.pieces) return;
-    const int64_t first = t * V - a.lead;
-    if (first >= 0 && first + V <= a.count) {
-        uint32_t w[4];
-        if constexpr (HALF) {
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const __half lo = __float2half_rn(dequantize_one<KIND>(a, first + 2 * q));
-                const __half hi = __float2half_rn(dequantize_one<KIND>(a, first + 2 * q + 1));
-                w[q] = static_cast<uint32_t>(__half_as_ushort(lo)) | (static_cast<uint32_t>(__half_as_ushort(hi)) << 16);
-            }
-            __stcs(reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + first), make_uint4(w[0], w[1], w[2], w[3]));
-        } else {
-#pragma unroll
-            for (int q = 0; q < 4; q++) w[q] = __float_as_uint(dequantize_one<KIND>(a, first + q));
-            __stcs(reinterpret_cast<uint4*>(static_cast<float*>(a.out) + first), make_uint4(w[0], w[1], w[2], w[3]));
-        }
-    } else {
-        for (int q = 0; q < V; q++) {
-            const int64_t j = first + q;
-            if (j < 0 || j >= a.count) continue;
-            const float v = dequantize_one<KIND>(a, j);
-            if constexpr (HALF)
-                static_cast<__half*>(a.out)[j] = __float2half_rn(v);
-            else
-                static_cast<float*>(a.out)[j] = v;
-        }
-    }
+    return __fmul_rn(__int2float_rn(d), __ldg(a.scale + c.pi));
 }
 
 template <bool HALF>
@@ -94,57 +76,201 @@ __device__ __forceinline__ float load_x(const void* p, int64_t i) {
     else return __ldg(static_cast<const float*>(p) + i);
 }
 
-template <bool SIGNED, bool HALF>
-__device__ __forceinline__ uint32_t quantize_one(const QuantArgs& a, int64_t j) {
-    const uint32_t pi = param_index(a, j);
+template <bool SIGNED>
+__device__ __forceinline__ uint32_t quantize_one(const QuantArgs& a, float xv, const ParamCursor& c) {
     int32_t zp = 0;
     if (a.zp != nullptr) {
-        const uint8_t z = __ldg(static_cast<const uint8_t*>(a.zp) + pi);
+        const uint8_t z = __ldg(static_cast<const uint8_t*>(a.zp) + c.pi);
         zp = SIGNED ? static_cast<int32_t>(static_cast<int8_t>(z)) : static_cast<int32_t>(z);
     }
     const float lo = SIGNED ? -128.0f : 0.0f;
     const float hi = SIGNED ? 127.0f : 255.0f;
-    float v = __fadd_rn(rintf(__fdiv_rn(load_x<HALF>(a.x, j), __ldg(a.scale + pi))), static_cast<float>(zp));
+    float v = __fadd_rn(rintf(__fdiv_rn(xv, __ldg(a.scale + c.pi))), static_cast<float>(zp));
     if (isnan(v)) v = lo;
     v = v < lo ? lo : (v > hi ? hi : v);
     return static_cast<uint32_t>(static_cast<int32_t>(v)) & 0xFFu;
 }
 
-template <bool SIGNED, bool HALF>
-__global__ void __launch_bounds__(QTHREADS) quantize_kernel(const QuantArgs a) {
-    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (t >= a.pieces) return;
-    const int64_t first = t * 16 - a.lead;
-    uint8_t* y = static_cast<uint8_t*>(a.out);
-    if (first >= 0 && first + 16 <= a.count) {
-        uint32_t w[4];
+// Vector shapes: E elements per vector, an input vector and an output vector per thread and step.
+//   DequantizeLinear: bytes -> float E = 4 (4 B -> 16 B), bytes -> half E = 8 (8 B -> 16 B),
+//                     int32 -> float E = 4 (16 B -> 16 B), int32 -> half E = 4 (16 B -> 8 B);
+//   QuantizeLinear:   float -> bytes E = 4 (16 B -> 4 B), half -> bytes E = 8 (16 B -> 8 B).
+// Consecutive threads take consecutive vectors, so every warp-wide load and store covers contiguous memory. The
+// elements before the output's first 16-byte boundary (`head`) and after the last whole vector go element by element.
+template <int KIND, bool HALF>
+struct DqShape {
+    static constexpr int E = (KIND != 2 && HALF) ? 8 : 4;
+};
+
+constexpr int UNROLL = 4;  // vectors in flight per thread
+
+template <int KIND, bool HALF>
+__device__ __forceinline__ void dq_load(const QuantArgs& a, int64_t first, int32_t (&q)[DqShape<KIND, HALF>::E]) {
+    constexpr int E = DqShape<KIND, HALF>::E;
+    if constexpr (KIND == 2) {
+        const int4 w = __ldcs(reinterpret_cast<const int4*>(static_cast<const int32_t*>(a.x) + first));
+        q[0] = w.x;
+        q[1] = w.y;
+        q[2] = w.z;
+        q[3] = w.w;
+    } else if constexpr (E == 8) {
+        const uint2 w = __ldcs(reinterpret_cast<const uint2*>(static_cast<const uint8_t*>(a.x) + first));
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            w[q] = quantize_one<SIGNED, HALF>(a, first + 4 * q) | (quantize_one<SIGNED, HALF>(a, first + 4 * q + 1) << 8) |
-                   (quantize_one<SIGNED, HALF>(a, first + 4 * q + 2) << 16) |
-                   (quantize_one<SIGNED, HALF>(a, first + 4 * q + 3) << 24);
+        for (int e = 0; e < 8; e++) {
+            const uint32_t b = ((e < 4 ? w.x : w.y) >> (8 * (e & 3))) & 0xFFu;
+            q[e] = KIND == 1 ? static_cast<int32_t>(static_cast<int8_t>(b)) : static_cast<int32_t>(b);
         }
-        __stcs(reinterpret_cast<uint4*>(y + first), make_uint4(w[0], w[1], w[2], w[3]));
     } else {
-        for (int q = 0; q < 16; q++) {
-            const int64_t j = first + q;
-            if (j >= 0 && j < a.count) y[j] = static_cast<uint8_t>(quantize_one<SIGNED, HALF>(a, j));
+        const uint32_t w = __ldcs(reinterpret_cast<const unsigned int*>(static_cast<const uint8_t*>(a.x) + first));
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const uint32_t b = (w >> (8 * e)) & 0xFFu;
+            q[e] = KIND == 1 ? static_cast<int32_t>(static_cast<int8_t>(b)) : static_cast<int32_t>(b);
         }
     }
 }
 
-// The 16-byte pieces covering `count` elements of `esize` bytes at `out`, and the elements before the first boundary.
-static void pieces_of(QuantArgs& a, int esize) {
+template <int KIND, bool HALF>
+__device__ __forceinline__ void dq_store(const QuantArgs& a, int64_t first, const float (&v)[DqShape<KIND, HALF>::E]) {
+    constexpr int E = DqShape<KIND, HALF>::E;
+    if constexpr (!HALF) {
+        __stcs(reinterpret_cast<float4*>(static_cast<float*>(a.out) + first), make_float4(v[0], v[1], v[2], v[3]));
+    } else {
+        uint32_t w[E / 2];
+#pragma unroll
+        for (int e = 0; e < E / 2; e++)
+            w[e] = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(v[2 * e]))) |
+                   (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(v[2 * e + 1]))) << 16);
+        if constexpr (E == 8)
+            __stcs(reinterpret_cast<uint4*>(static_cast<__half*>(a.out) + first), make_uint4(w[0], w[1], w[2], w[3]));
+        else
+            __stcs(reinterpret_cast<uint2*>(static_cast<__half*>(a.out) + first), make_uint2(w[0], w[1]));
+    }
+}
+
+template <int KIND, bool HALF>
+__device__ __forceinline__ void dq_scalar(const QuantArgs& a, int64_t j) {
+    const float v = dequantize_one<KIND>(a, load_q<KIND>(a.x, j), param_at(a, j));
+    if constexpr (HALF)
+        static_cast<__half*>(a.out)[j] = __float2half_rn(v);
+    else
+        static_cast<float*>(a.out)[j] = v;
+}
+
+template <int KIND, bool HALF>
+__global__ void __launch_bounds__(QTHREADS) dequantize_kernel(const QuantArgs a) {
+    constexpr int E = DqShape<KIND, HALF>::E;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    const int64_t tail0 = a.head + a.vectors * E;
+    if (tid < a.head) dq_scalar<KIND, HALF>(a, tid);
+    if (tid < a.count - tail0) dq_scalar<KIND, HALF>(a, tail0 + tid);
+    for (int64_t v0 = tid; v0 < a.vectors; v0 += nthreads * UNROLL) {
+        int32_t q[UNROLL][E];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++)
+            if (v0 + u * nthreads < a.vectors) dq_load<KIND, HALF>(a, a.head + (v0 + u * nthreads) * E, q[u]);
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            const int64_t vi = v0 + u * nthreads;
+            if (vi >= a.vectors) break;
+            const int64_t first = a.head + vi * E;
+            ParamCursor c = param_at(a, first);
+            float v[E];
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                v[e] = dequantize_one<KIND>(a, q[u][e], c);
+                param_next(a, c);
+            }
+            dq_store<KIND, HALF>(a, first, v);
+        }
+    }
+}
+
+template <bool HALF>
+__device__ __forceinline__ void q_load(const QuantArgs& a, int64_t first, float (&x)[HALF ? 8 : 4]) {
+    if constexpr (HALF) {
+        const uint4 w = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __half*>(a.x) + first));
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            x[2 * e] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[e] & 0xFFFFu)));
+            x[2 * e + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[e] >> 16)));
+        }
+    } else {
+        const float4 w = __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + first));
+        x[0] = w.x;
+        x[1] = w.y;
+        x[2] = w.z;
+        x[3] = w.w;
+    }
+}
+
+template <bool SIGNED, bool HALF>
+__global__ void __launch_bounds__(QTHREADS) quantize_kernel(const QuantArgs a) {
+    constexpr int E = HALF ? 8 : 4;
+    const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    uint8_t* y = static_cast<uint8_t*>(a.out);
+    const int64_t tail0 = a.head + a.vectors * E;
+    if (tid < a.head) y[tid] = static_cast<uint8_t>(quantize_one<SIGNED>(a, load_x<HALF>(a.x, tid), param_at(a, tid)));
+    if (tid < a.count - tail0) {
+        const int64_t j = tail0 + tid;
+        y[j] = static_cast<uint8_t>(quantize_one<SIGNED>(a, load_x<HALF>(a.x, j), param_at(a, j)));
+    }
+    for (int64_t v0 = tid; v0 < a.vectors; v0 += nthreads * UNROLL) {
+        float x[UNROLL][E];
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++)
+            if (v0 + u * nthreads < a.vectors) q_load<HALF>(a, a.head + (v0 + u * nthreads) * E, x[u]);
+#pragma unroll
+        for (int u = 0; u < UNROLL; u++) {
+            const int64_t vi = v0 + u * nthreads;
+            if (vi >= a.vectors) break;
+            const int64_t first = a.head + vi * E;
+            ParamCursor c = param_at(a, first);
+            uint32_t w[E / 4];
+#pragma unroll
+            for (int e = 0; e < E / 4; e++) w[e] = 0;
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                w[e >> 2] |= quantize_one<SIGNED>(a, x[u][e], c) << (8 * (e & 3));
+                param_next(a, c);
+            }
+            if constexpr (E == 8)
+                __stcs(reinterpret_cast<uint2*>(y + first), make_uint2(w[0], w[1]));
+            else
+                __stcs(reinterpret_cast<unsigned int*>(y + first), w[0]);
+        }
+    }
+}
+
+// Splits the elements into a scalar head (up to the output's first boundary of `out_align` bytes), whole vectors of E
+// elements whose input (in_esize bytes per element) and output both start aligned, and a scalar tail; when the input
+// is not aligned where the output is, everything goes element by element.
+static void split_vectors(QuantArgs& a, int e, int in_esize, int out_esize, int in_align, int out_align) {
     const uintptr_t o = reinterpret_cast<uintptr_t>(a.out);
-    const uintptr_t base = o & ~uintptr_t(15);
-    const uintptr_t end = o + static_cast<uintptr_t>(a.count) * esize;
-    a.lead = static_cast<int>((o - base) / esize);
-    a.pieces = static_cast<int64_t>((end - base + 15) / 16);
+    int64_t head = static_cast<int64_t>((out_align - (o % out_align)) % out_align) / out_esize;
+    if (head > a.count) head = a.count;
+    const uintptr_t xin = reinterpret_cast<uintptr_t>(a.x) + static_cast<uintptr_t>(head) * in_esize;
+    a.head = head;
+    a.vectors = (xin % in_align) == 0 ? (a.count - head) / e : 0;
+    if (a.vectors == 0) a.head = 0;
+    const int64_t scalar = a.count - a.vectors * e;  // head + tail elements, one thread each
+    const int64_t want = (a.vectors + UNROLL - 1) / UNROLL;
+    a.threads = want > scalar ? want : scalar;
+}
+
+static unsigned grid_of(const QuantArgs& a) {
+    const int64_t blocks = (a.threads + QTHREADS - 1) / QTHREADS;
+    return static_cast<unsigned>(blocks < 1 ? 1 : blocks);
 }
 
 static cudaError_t launch_dequantize(QuantArgs a, int kind, bool half, cudaStream_t s) {
-    pieces_of(a, half ? 2 : 4);
-    const unsigned blocks = static_cast<unsigned>((a.pieces + QTHREADS - 1) / QTHREADS);
+    const int in_es = kind == 2 ? 4 : 1, out_es = half ? 2 : 4;
+    const int e = (kind != 2 && half) ? 8 : 4;
+    split_vectors(a, e, in_es, out_es, e * in_es, e * out_es);
+    const unsigned blocks = grid_of(a);
     switch (kind * 2 + (half ? 1 : 0)) {
         case 0: dequantize_kernel<0, false><<<blocks, QTHREADS, 0, s>>>(a); break;
         case 1: dequantize_kernel<0, true><<<blocks, QTHREADS, 0, s>>>(a); break;
@@ -157,8 +283,10 @@ static cudaError_t launch_dequantize(QuantArgs a, int kind, bool half, cudaStrea
 }
 
 static cudaError_t launch_quantize(QuantArgs a, bool is_signed, bool half, cudaStream_t s) {
-    pieces_of(a, 1);
-    const unsigned blocks = static_cast<unsigned>((a.pieces + QTHREADS - 1) / QTHREADS);
+    const int in_es = half ? 2 : 4;
+    const int e = half ? 8 : 4;
+    split_vectors(a, e, in_es, 1, e * in_es, e);
+    const unsigned blocks = grid_of(a);
     switch ((is_signed ? 2 : 0) + (half ? 1 : 0)) {
         case 0: quantize_kernel<false, false><<<blocks, QTHREADS, 0, s>>>(a); break;
         case 1: quantize_kernel<false, true><<<blocks, QTHREADS, 0, s>>>(a); break;

@@ -74,7 +74,8 @@ class og_int8_gemm_problem(ctypes.Structure):
 
 
 class og_int8_gemm_options(ctypes.Structure):
-    _fields_ = [("allow_packed_dot", ctypes.c_int32), ("kernel", ctypes.c_int32), ("tile", ctypes.c_int32)]
+    _fields_ = [("allow_packed_dot", ctypes.c_int32), ("kernel", ctypes.c_int32), ("tile", ctypes.c_int32),
+                ("stream_k", ctypes.c_int32)]
 
 
 _P = ctypes.c_void_p
@@ -466,6 +467,7 @@ class Int8GemmOptions:
     allow_packed_dot: bool = True
     kernel: int = KERNEL_AUTO
     tile: int = 0
+    stream_k: int = 0  # test hook: 2 splits the (tile, K block) work evenly across the SM pairs (stream-K)
 
 
 def _buf(b: Optional[GpuBuffer]):
@@ -485,7 +487,7 @@ class Int8Gemm:
         opt = None
         if options is not None:
             opt = ctypes.byref(og_int8_gemm_options(int(bool(options.allow_packed_dot)), int(options.kernel),
-                                                    int(options.tile)))
+                                                    int(options.tile), int(options.stream_k)))
         _check(_lib.og_int8_gemm_create(device.handle, opt, ctypes.byref(h)))
         self.handle = h.value
 
@@ -793,7 +795,7 @@ class ConvIntegerKernels:
         opt = None
         if options is not None:
             opt = ctypes.byref(og_int8_gemm_options(int(bool(options.allow_packed_dot)), int(options.kernel),
-                                                    int(options.tile)))
+                                                    int(options.tile), int(options.stream_k)))
         _check(_lib.og_conv_integer_create(device.handle, opt, ctypes.byref(h)))
         self.handle = h.value
 

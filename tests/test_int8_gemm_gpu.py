@@ -354,6 +354,52 @@ def full_size_check(device, gemm, m, n, k, batch, a_signed, zp, trans_b=False, s
     return kern
 
 
+@pytest.mark.parametrize("cfg,m,n,k", [("tensor-core-2sm", 1280, 4096, 512), ("tensor-core-1sm", 1280, 4096, 512),
+                                       ("tensor-core-2sm", 1536, 3328, 1152), ("tensor-core-2sm", 1100, 4100, 520)])
+def test_stream_k_split_tiles_are_bit_exact(device, cfg, m, n, k):
+    """With the stream-K option and a partial last wave of tiles, the (tile, K block) units are split evenly across
+    the SMs and a tile cut between two of them is finished by the one holding K block 0 after the other has handed
+    over its sums. int32 with both zero-point layouts, the float and requantized forms, and three products
+    recorded back to back in one encoder (the hand-over flags are reset between launches)."""
+    opts = CONFIGS[cfg]
+    gemm = og.Int8Gemm(device, og.Int8GemmOptions(kernel=opts.kernel, tile=opts.tile, stream_k=2))
+    with gemm:
+        kernels = set()
+        for i, (za_mode, zb_mode, a_s, b_s) in enumerate(((1, 2, False, True), (2, 1, True, False), (0, 0, True, True))):
+            c = align_case(Case("stream-k", problem(m, n, k), a_signed=a_s, b_signed=b_s, za_mode=za_mode,
+                                zb_mode=zb_mode))
+            bad, kernel = run_int32(device, gemm, c, 70 + i)
+            assert bad == 0, (c.p, kernel)
+            kernels.add(kernel)
+        assert kernels == {cfg + "-stream-k"}, kernels
+        assert float_case(device, gemm, m, n, k, True, True, True, 80, aligned=True) == 0
+        assert requant_case(device, gemm, m, n, k, True, False, 3, True, 81, False, True, aligned=True) == 0
+
+        # Three products in one encoder, run in stream order on one instance (and so one hand-over buffer).
+        shapes = [(m, n, k, 90), (m, n, 2 * k, 91), (m, n, k, 92)]
+        data, bufs = [], []
+        enc = device.begin_commands()
+        for (mm, nn, kk, seed) in shapes:
+            p = align_case(Case("seq", problem(mm, nn, kk), a_signed=False, b_signed=True, za_mode=1, zb_mode=2)).p
+            a = oracle.bytes_(p["m"] * p["lda"] + p["offset_a"] + 4, seed)
+            b = oracle.bytes_(kk * p["ldb"] + p["offset_b"] + 4, seed + 1)
+            za, zb = oracle.bytes_(1, seed + 2), oracle.bytes_(nn, seed + 3)
+            want = oracle.int8_gemm(a, False, b, True, za, False, zb, True, **oracle_shape(p))
+            bs = [typed(device, a, False), typed(device, b, True), device.create_buffer(np.int32, want.size),
+                  typed(device, za, False), typed(device, zb, True)]
+            gemm.encode_int32(enc, og.Int8GemmProblem(**p), bs[0], bs[1], bs[2], og.Int8Operand(bs[3], 0),
+                              og.Int8Operand(bs[4], 0, True))
+            data.append((bs[2], want))
+            bufs += bs
+        device.submit(enc)
+        try:
+            for c_buf, want in data:
+                assert np.array_equal(c_buf.read(), want)
+        finally:
+            for v in bufs:
+                v.dispose()
+
+
 @pytest.mark.parametrize("workload", ["c3", "c2", "c4", "c5", "c3-transposed"])
 def test_config_sizes_checksums_and_sampled_rows(device, workload):
     """BASELINE.json's configs at full size: 8192^3 s8 x s8, 4096^3 u8 x s8 with zero points, the batched QKV

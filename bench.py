@@ -71,9 +71,16 @@ def load_peaks():
     return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
 
 
+PROFILES = {"c3": "int8_gemm_tc2_c3.md", "c2": "dql_int8_gemm_chain_c2.md", "c4": "int8_gemm_tc2_c4.md",
+            "c5": "int8_gemm_rows_c5.md", "dequant": "dequantize_linear_dequant.md"}
+
+
 def profile_traffic(workload: str):
-    """Per-launch DRAM bytes of the top kernel from the committed ncu summary, or None."""
-    path = os.path.join(ROOT, "profiles", f"int8_gemm_tc_{workload}.md")
+    """Per-launch DRAM bytes (read + write) of the workload's dominant kernel from its committed ncu summary, or
+    None when there is no full capture for it."""
+    if workload not in PROFILES:
+        return None
+    path = os.path.join(ROOT, "profiles", PROFILES[workload])
     if not os.path.exists(path):
         return None
     m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(path).read())
@@ -392,7 +399,7 @@ def run_family(args, rank: int, world: int, local_rank: int):
         roof = {"bound": "hbm", "unit": "GB/s", "peak_source": f"{peaks['source']} HBM copy bandwidth"}
     achieved = d["work"] / (statistics.mean(per_step) * 1e-9) / scale_unit
     roof.update({"achieved": round(achieved, 3), "peak": round(peak, 1), "frac": round(achieved / peak, 4),
-                 "traffic": None})
+                 "traffic": profile_traffic(args.workload)})
     cpu = None
     if not args.no_cpu:
         v, cores, sample = cpu_family(args.workload, os.cpu_count() or 1, args.cpu_seconds)

@@ -3,7 +3,8 @@
 //     maximum, warps reduce with shuffles, blocks write one partial each; the last block to finish (ticket counter,
 //     no spinning) combines the partials and derives scale and zero point, which it stores for the caller and for
 //     pass 2.
-//  2. dq_quantize: each thread writes 16 output bytes (one 16-byte store where the chunk is whole) from 16 inputs.
+//  2. QuantizeLinear per tensor to uint8 (og_quant.cu) with the scale and zero point pass 1 stored: the same
+//     arithmetic, y = clamp(round_half_even(x / scale) + zero point, 0, 255), NaN to 0.
 // The arithmetic is onemodel's (DynamicQuantizeKernels.cs:9-16): lo = min(0, min x), hi = max(0, max x),
 // scale = (hi - lo) / 255, zero point = clamp(round_half_even(-(lo / scale)), 0, 255) when scale is finite and not 0,
 // an all-zero range gives scale 1 and zero point 0, y = clamp(round_half_even(x / scale) + zero point, 0, 255) and
@@ -131,56 +132,6 @@ __global__ void __launch_bounds__(DQ_THREADS)
     }
 }
 
-__device__ __forceinline__ uint8_t quantize_one(float v, float scale, float zpf) {
-    const float q = __fadd_rn(rintf(__fdiv_rn(v, scale)), zpf);
-    if (isnan(q)) return 0;
-    return q < 0.0f ? 0 : (q > 255.0f ? 255 : static_cast<uint8_t>(static_cast<int>(q)));
-}
-
-// Thread t owns the 16-byte-aligned chunk t of y's range (the first and last chunks may be partial).
-__global__ void __launch_bounds__(DQ_THREADS)
-    dq_quantize_kernel(const float* __restrict__ x, int64_t count, uint8_t* __restrict__ y,
-                       const DqScratch* __restrict__ s, int64_t chunks) {
-    const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (t >= chunks) return;
-    const float scale = __ldcg(&s->scale);
-    const float zpf = static_cast<float>(__ldcg(&s->zero_point));
-    const uintptr_t ybase = reinterpret_cast<uintptr_t>(y) & ~uintptr_t(15);
-    const int64_t first = static_cast<int64_t>(ybase + 16 * t) - static_cast<int64_t>(reinterpret_cast<uintptr_t>(y));
-    if (first >= 0 && first + 16 <= count) {
-        float v[16];
-        const float* xp = x + first;
-        if ((reinterpret_cast<uintptr_t>(xp) & 15) == 0) {
-            const float4* x4 = reinterpret_cast<const float4*>(xp);
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float4 w = __ldcs(x4 + j);
-                v[4 * j] = w.x;
-                v[4 * j + 1] = w.y;
-                v[4 * j + 2] = w.z;
-                v[4 * j + 3] = w.w;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 16; j++) v[j] = __ldcs(xp + j);
-        }
-        uint32_t w[4];
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            w[j] = static_cast<uint32_t>(quantize_one(v[4 * j], scale, zpf)) |
-                   (static_cast<uint32_t>(quantize_one(v[4 * j + 1], scale, zpf)) << 8) |
-                   (static_cast<uint32_t>(quantize_one(v[4 * j + 2], scale, zpf)) << 16) |
-                   (static_cast<uint32_t>(quantize_one(v[4 * j + 3], scale, zpf)) << 24);
-        }
-        *reinterpret_cast<uint4*>(y + first) = make_uint4(w[0], w[1], w[2], w[3]);
-    } else {
-        for (int j = 0; j < 16; j++) {
-            const int64_t i = first + j;
-            if (i >= 0 && i < count) y[i] = quantize_one(x[i], scale, zpf);
-        }
-    }
-}
-
 cudaError_t launch_dynamic_quantize(const float* x, int64_t count, uint8_t* y, float* scale_out, uint8_t* zp_out,
                                     DqScratch* scratch, int num_sms, cudaStream_t stream) {
     int64_t blocks = (count + DQ_THREADS * 16 - 1) / (DQ_THREADS * 16);
@@ -191,11 +142,8 @@ cudaError_t launch_dynamic_quantize(const float* x, int64_t count, uint8_t* y, f
     dq_range_kernel<<<static_cast<unsigned>(blocks), DQ_THREADS, 0, stream>>>(x, count, scratch, scale_out, zp_out);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
-    const uintptr_t yb = reinterpret_cast<uintptr_t>(y);
-    const int64_t chunks = static_cast<int64_t>(((yb + count - 1) >> 4) - (yb >> 4) + 1);
-    const int64_t qblocks = (chunks + DQ_THREADS - 1) / DQ_THREADS;
-    dq_quantize_kernel<<<static_cast<unsigned>(qblocks), DQ_THREADS, 0, stream>>>(x, count, y, scratch, chunks);
-    return cudaGetLastError();
+    // Pass 2 is QuantizeLinear per tensor with the scale and zero point pass 1 stored for the caller.
+    return launch_quantize_u8_tensor(x, count, y, scale_out, zp_out, stream);
 }
 
 }  // namespace og

@@ -81,6 +81,10 @@ LaunchFn prepare_byte_sums_tc(const uint8_t* mat, int cols, int k, int64_t ld, i
 
 // DynamicQuantizeLinear (og_dq.cu).
 struct DqScratch;
+// QuantizeLinear per tensor to uint8 (og_quant.cu): clamp(round_half_even(x / *scale) + *zero_point, 0, 255), NaN
+// to 0 - the second pass of DynamicQuantizeLinear.
+cudaError_t launch_quantize_u8_tensor(const float* x, int64_t count, uint8_t* y, const float* scale,
+                                      const uint8_t* zero_point, cudaStream_t s);
 size_t dq_scratch_bytes();
 cudaError_t launch_dynamic_quantize(const float* x, int64_t count, uint8_t* y, float* scale_out, uint8_t* zp_out,
                                     DqScratch* scratch, int num_sms, cudaStream_t stream);

@@ -76,19 +76,65 @@ __device__ __forceinline__ float load_x(const void* p, int64_t i) {
     else return __ldg(static_cast<const float*>(p) + i);
 }
 
+// The scale and the zero point of one parameter index.
+struct QParam {
+    uint32_t pi;
+    float s, zf;
+};
+
 template <bool SIGNED>
-__device__ __forceinline__ uint32_t quantize_one(const QuantArgs& a, float xv, const ParamCursor& c) {
+__device__ __forceinline__ void qparam_load(const QuantArgs& a, uint32_t pi, QParam& q) {
+    q.pi = pi;
+    q.s = __ldg(a.scale + pi);
     int32_t zp = 0;
     if (a.zp != nullptr) {
-        const uint8_t z = __ldg(static_cast<const uint8_t*>(a.zp) + c.pi);
+        const uint8_t z = __ldg(static_cast<const uint8_t*>(a.zp) + pi);
         zp = SIGNED ? static_cast<int32_t>(static_cast<int8_t>(z)) : static_cast<int32_t>(z);
     }
+    q.zf = static_cast<float>(zp);
+}
+
+// round_half_even(x / s), the quotient correctly rounded (IEEE division); kept out of line so that callers that
+// reach it rarely do not pay for it inline.
+__device__ __noinline__ float rne_quotient_exact(float x, float s) { return rintf(__fdiv_rn(x, s)); }
+
+__device__ __forceinline__ float rne_quotient(float x, const QParam& p) { return rne_quotient_exact(x, p.s); }
+
+// The same value when the scale is shared by many elements: with r = RN(1 / s) and m = RN(x * r),
+// |m - x/s| <= |x/s| (2^-23 + 2^-48) and the correctly rounded quotient lies within |x/s| 2^-24 of x/s, so both round
+// to the same integer unless a half-integer lies within about |m| 2^-22 of m. m is used when the nearest half-integer
+// is further than |m| 2^-20 + 2^-20 away (and |m| < 2^22, where m - (floor(m) + 0.5) is within 2^-25 of exact);
+// otherwise - near ties, for NaN, infinities and huge values - the quotient itself is rounded. `r_ok` says r is
+// finite and normal.
+__device__ __forceinline__ float rne_quotient_r(float x, float s, float r, bool r_ok) {
+    if (r_ok) {
+        const float m = __fmul_rn(x, r);
+        const float am = fabsf(m);
+        const float d = fabsf(__fsub_rn(m, __fadd_rn(floorf(m), 0.5f)));
+        if (am < 4194304.0f && d > __fmaf_rn(am, 9.5367431640625e-07f, 9.5367431640625e-07f)) return rintf(m);
+    }
+    return rne_quotient_exact(x, s);
+}
+
+template <bool SIGNED>
+__device__ __forceinline__ uint32_t saturate_byte(float v) {
     const float lo = SIGNED ? -128.0f : 0.0f;
     const float hi = SIGNED ? 127.0f : 255.0f;
-    float v = __fadd_rn(rintf(__fdiv_rn(xv, __ldg(a.scale + c.pi))), static_cast<float>(zp));
     if (isnan(v)) v = lo;
     v = v < lo ? lo : (v > hi ? hi : v);
     return static_cast<uint32_t>(static_cast<int32_t>(v)) & 0xFFu;
+}
+
+template <bool SIGNED>
+__device__ __forceinline__ uint32_t quantize_with(float xv, const QParam& p) {
+    return saturate_byte<SIGNED>(__fadd_rn(rne_quotient(xv, p), p.zf));
+}
+
+template <bool SIGNED>
+__device__ __forceinline__ uint32_t quantize_one(const QuantArgs& a, float xv, const ParamCursor& c) {
+    QParam p;
+    qparam_load<SIGNED>(a, c.pi, p);
+    return quantize_with<SIGNED>(xv, p);
 }
 
 // Vector shapes: E elements per vector, an input vector and an output vector per thread and step.
@@ -187,30 +233,41 @@ __global__ void __launch_bounds__(QTHREADS) dequantize_kernel(const QuantArgs a)
     }
 }
 
+// The 16 inputs x[first .. first + 15] of one vector (four float or two half 16-byte loads).
 template <bool HALF>
-__device__ __forceinline__ void q_load(const QuantArgs& a, int64_t first, float (&x)[HALF ? 8 : 4]) {
+__device__ __forceinline__ void q_load16(const QuantArgs& a, int64_t first, float (&x)[16]) {
     if constexpr (HALF) {
-        const uint4 w = __ldcs(reinterpret_cast<const uint4*>(static_cast<const __half*>(a.x) + first));
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const uint4* p = reinterpret_cast<const uint4*>(static_cast<const __half*>(a.x) + first);
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            x[2 * e] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[e] & 0xFFFFu)));
-            x[2 * e + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[e] >> 16)));
+        for (int v = 0; v < 2; v++) {
+            const uint4 w = __ldcs(p + v);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                x[8 * v + 2 * e] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[e] & 0xFFFFu)));
+                x[8 * v + 2 * e + 1] = __half2float(__ushort_as_half(static_cast<unsigned short>(ws[e] >> 16)));
+            }
         }
     } else {
-        const float4 w = __ldcs(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + first));
-        x[0] = w.x;
-        x[1] = w.y;
-        x[2] = w.z;
-        x[3] = w.w;
+        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + first);
+#pragma unroll
+        for (int v = 0; v < 4; v++) {
+            const float4 w = __ldcs(p + v);
+            x[4 * v] = w.x;
+            x[4 * v + 1] = w.y;
+            x[4 * v + 2] = w.z;
+            x[4 * v + 3] = w.w;
+        }
     }
 }
 
+// Thread t owns output bytes [head + 16 t, +16): one 16-byte store, consecutive threads consecutive stores. When the
+// 16 elements share one scale (per tensor, or a run of `inner` elements that covers them), the quotient is formed by
+// the multiply-first rounding; otherwise each element divides by its own scale.
 template <bool SIGNED, bool HALF>
 __global__ void __launch_bounds__(QTHREADS) quantize_kernel(const QuantArgs a) {
-    constexpr int E = HALF ? 8 : 4;
+    constexpr int E = 16;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
     uint8_t* y = static_cast<uint8_t*>(a.out);
     const int64_t tail0 = a.head + a.vectors * E;
     if (tid < a.head) y[tid] = static_cast<uint8_t>(quantize_one<SIGNED>(a, load_x<HALF>(a.x, tid), param_at(a, tid)));
@@ -218,31 +275,31 @@ __global__ void __launch_bounds__(QTHREADS) quantize_kernel(const QuantArgs a) {
         const int64_t j = tail0 + tid;
         y[j] = static_cast<uint8_t>(quantize_one<SIGNED>(a, load_x<HALF>(a.x, j), param_at(a, j)));
     }
-    for (int64_t v0 = tid; v0 < a.vectors; v0 += nthreads * UNROLL) {
-        float x[UNROLL][E];
+    if (tid >= a.vectors) return;
+    const int64_t first = a.head + tid * E;
+    float x[16];
+    q_load16<HALF>(a, first, x);
+    ParamCursor c = param_at(a, first);
+    uint32_t w[4] = {0, 0, 0, 0};
+    if (!a.per_axis || c.r + E <= a.inner) {
+        QParam p;
+        qparam_load<SIGNED>(a, c.pi, p);
+        const float r = __frcp_rn(p.s);
+        const bool r_ok = fabsf(r) >= 1.17549435e-38f && fabsf(r) <= 3.40282347e+38f;  // normal and finite
 #pragma unroll
-        for (int u = 0; u < UNROLL; u++)
-            if (v0 + u * nthreads < a.vectors) q_load<HALF>(a, a.head + (v0 + u * nthreads) * E, x[u]);
+        for (int e = 0; e < E; e++)
+            w[e >> 2] |= saturate_byte<SIGNED>(__fadd_rn(rne_quotient_r(x[e], p.s, r, r_ok), p.zf)) << (8 * (e & 3));
+    } else {
+        QParam p;
+        qparam_load<SIGNED>(a, c.pi, p);
 #pragma unroll
-        for (int u = 0; u < UNROLL; u++) {
-            const int64_t vi = v0 + u * nthreads;
-            if (vi >= a.vectors) break;
-            const int64_t first = a.head + vi * E;
-            ParamCursor c = param_at(a, first);
-            uint32_t w[E / 4];
-#pragma unroll
-            for (int e = 0; e < E / 4; e++) w[e] = 0;
-#pragma unroll
-            for (int e = 0; e < E; e++) {
-                w[e >> 2] |= quantize_one<SIGNED>(a, x[u][e], c) << (8 * (e & 3));
-                param_next(a, c);
-            }
-            if constexpr (E == 8)
-                __stcs(reinterpret_cast<uint2*>(y + first), make_uint2(w[0], w[1]));
-            else
-                __stcs(reinterpret_cast<unsigned int*>(y + first), w[0]);
+        for (int e = 0; e < E; e++) {
+            if (c.pi != p.pi) qparam_load<SIGNED>(a, c.pi, p);
+            w[e >> 2] |= quantize_with<SIGNED>(x[e], p) << (8 * (e & 3));
+            param_next(a, c);
         }
     }
+    __stcs(reinterpret_cast<uint4*>(y + first), make_uint4(w[0], w[1], w[2], w[3]));
 }
 
 // Splits the elements into a scalar head (up to the output's first boundary of `out_align` bytes), whole vectors of E
@@ -282,10 +339,28 @@ static cudaError_t launch_dequantize(QuantArgs a, int kind, bool half, cudaStrea
     return cudaGetLastError();
 }
 
+static cudaError_t launch_quantize(QuantArgs a, bool is_signed, bool half, cudaStream_t s);
+
+// DynamicQuantizeLinear's second pass is QuantizeLinear per tensor to uint8 with the scale and zero point the first
+// pass stored on the device: clamp(round_half_even(x / scale) + zp, 0, 255), NaN to 0.
+cudaError_t launch_quantize_u8_tensor(const float* x, int64_t count, uint8_t* y, const float* scale,
+                                      const uint8_t* zero_point, cudaStream_t s) {
+    QuantArgs a{};
+    a.x = x;
+    a.count = count;
+    a.scale = scale;
+    a.zp = zero_point;
+    a.per_axis = 0;
+    a.axis_len = 1;
+    a.inner = 1;
+    a.out = y;
+    return launch_quantize(a, false, false, s);
+}
+
 static cudaError_t launch_quantize(QuantArgs a, bool is_signed, bool half, cudaStream_t s) {
-    const int in_es = half ? 2 : 4;
-    const int e = half ? 8 : 4;
-    split_vectors(a, e, in_es, 1, e * in_es, e);
+    split_vectors(a, 16, half ? 2 : 4, 1, 16, 16);
+    const int64_t scalar = a.count - a.vectors * 16;
+    a.threads = a.vectors > scalar ? a.vectors : scalar;  // one vector per thread
     const unsigned blocks = grid_of(a);
     switch ((is_signed ? 2 : 0) + (half ? 1 : 0)) {
         case 0: quantize_kernel<false, false><<<blocks, QTHREADS, 0, s>>>(a); break;

@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <climits>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <functional>

@@ -19,7 +19,9 @@
 #include <algorithm>
 #include <cstring>
 
+#include "og_gemm.h"
 #include "og_host.h"
+#include "og_ptx.cuh"
 
 namespace og {
 
@@ -41,6 +43,8 @@ struct PackArgs {
 // point where that position lies in the padding or the column lies past OH * OW (ConvIntegerPack.hlsl:55-89).
 template <int BYTES>
 __global__ void __launch_bounds__(PACK_THREADS) conv_pack_kernel(const PackArgs a) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (t >= a.units) return;
     const int64_t r = t / a.units_per_row;
@@ -91,6 +95,8 @@ constexpr int PLANE_SMEM_MAX = 48 * 1024;  // planes up to this size are staged 
 // columns per thread and store, every byte gathered from shared memory.
 template <int BYTES>
 __global__ void __launch_bounds__(PACK_THREADS) conv_pack_plane_kernel(const PackArgs a) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ uint8_t plane_s[];
     const int64_t plane = blockIdx.x;  // (image * groups + g) * cin_g + c
     const int32_t c = static_cast<int32_t>(plane % a.cin_g);
@@ -153,18 +159,12 @@ static cudaError_t launch_conv_pack(const PackArgs& a, int64_t planes, cudaStrea
     if (hw <= PLANE_SMEM_MAX && planes <= 0x7FFFFFFF) {
         const unsigned grid = static_cast<unsigned>(planes);
         const size_t smem = static_cast<size_t>((hw + 15) & ~15);
-        if (wide)
-            conv_pack_plane_kernel<16><<<grid, PACK_THREADS, smem, s>>>(a);
-        else
-            conv_pack_plane_kernel<4><<<grid, PACK_THREADS, smem, s>>>(a);
-        return cudaGetLastError();
+        return wide ? launch_pdl(conv_pack_plane_kernel<16>, dim3(grid), dim3(PACK_THREADS), smem, s, a)
+                    : launch_pdl(conv_pack_plane_kernel<4>, dim3(grid), dim3(PACK_THREADS), smem, s, a);
     }
     const unsigned blocks = static_cast<unsigned>((a.units + PACK_THREADS - 1) / PACK_THREADS);
-    if (wide)
-        conv_pack_kernel<16><<<blocks, PACK_THREADS, 0, s>>>(a);
-    else
-        conv_pack_kernel<4><<<blocks, PACK_THREADS, 0, s>>>(a);
-    return cudaGetLastError();
+    return wide ? launch_pdl(conv_pack_kernel<16>, dim3(blocks), dim3(PACK_THREADS), 0, s, a)
+                : launch_pdl(conv_pack_kernel<4>, dim3(blocks), dim3(PACK_THREADS), 0, s, a);
 }
 
 }  // namespace og

@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include "og_gemm.h"
+#include "og_ptx.cuh"
 
 namespace og {
 
@@ -58,6 +59,8 @@ __device__ __forceinline__ void block_min_max(float& mn, float& mx, float* smin,
 __global__ void __launch_bounds__(DQ_THREADS)
     dq_range_kernel(const float* __restrict__ x, int64_t count, DqScratch* __restrict__ s, float* __restrict__ scale_out,
                     uint8_t* __restrict__ zp_out) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float smin[32], smax[32];
     __shared__ bool last;
     float mn = INFINITY, mx = -INFINITY;
@@ -139,8 +142,8 @@ cudaError_t launch_dynamic_quantize(const float* x, int64_t count, uint8_t* y, f
                                                                           : DQ_MAX_BLOCKS;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    dq_range_kernel<<<static_cast<unsigned>(blocks), DQ_THREADS, 0, stream>>>(x, count, scratch, scale_out, zp_out);
-    cudaError_t err = cudaGetLastError();
+    cudaError_t err = launch_pdl(dq_range_kernel, dim3(static_cast<unsigned>(blocks)), dim3(DQ_THREADS), 0, stream, x,
+                                 count, scratch, scale_out, zp_out);
     if (err != cudaSuccess) return err;
     // Pass 2 is QuantizeLinear per tensor with the scale and zero point pass 1 stored for the caller.
     return launch_quantize_u8_tensor(x, count, y, scale_out, zp_out, stream);

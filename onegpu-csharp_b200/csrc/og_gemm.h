@@ -42,6 +42,31 @@ bool sk_wanted(const GemmLaunch& L);
 // A launch whose host-side preparation (tensor maps, parameters) is already done: calling it only launches.
 using LaunchFn = std::function<cudaError_t(cudaStream_t)>;
 
+// Whether launches may overlap the preceding grid (environment ONEGPU_PDL=0 turns it off; read once).
+bool pdl_enabled();
+
+// Launches a kernel that may overlap the tail of the preceding grid in the stream (programmatic dependent launch);
+// the kernel must call pdl_wait() before it touches global memory or allocates TMEM.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+    if (!pdl_enabled()) {
+        kernel<<<grid, block, smem, stream>>>(args...);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // tcgen05 product (og_gemm_tc.cu). Eligible when K >= 1 and both operands' rows and batches start on 16-byte
 // boundaries (the TMA requirement). prepare_* builds the tensor maps at record time (null + *err on failure).
 bool tc_eligible(const GemmLaunch& L);

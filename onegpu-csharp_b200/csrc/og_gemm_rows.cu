@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
     const int kb_count = min(p.k_blocks, p.k_blocks_total - kb_begin);
     const bool sums_only = p.sums_out != nullptr;
     const bool need_col_sums = sums_only || p.epi.za != nullptr;  // za * colsum(B)
+    pdl_trigger();
 
     // The block of ones (any swizzle of all-ones bytes is all ones).
     for (int i = threadIdx.x; i < rows::ONES_BYTES / 16; i += blockDim.x)
@@ -104,6 +105,7 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
         prefetch_tmap(&tmap_a);
         prefetch_tmap(&tmap_b);
     }
+    pdl_wait();  // the preceding grid is done: its outputs are readable and its TMEM is free
     if (warp == 1) {
         tmem_alloc(tmem_holder, rows::TMEM_COLS);
         tmem_relinquish();
@@ -279,8 +281,7 @@ static LaunchFn bind_rows_t(const RowsParams& p, const CUtensorMap& ma, const CU
             if (e != cudaSuccess) return e;
             configured |= bit;
         }
-        kern<<<grid, rows::THREADS, rows::SMEM_BYTES, stream>>>(ma, mb, p, idesc);
-        return cudaGetLastError();
+        return launch_pdl(kern, grid, dim3(rows::THREADS), rows::SMEM_BYTES, stream, ma, mb, p, idesc);
     };
 }
 

@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 #include "og_gemm.h"
@@ -360,6 +361,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
     const int worker = CG == 2 ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
     const int workers = CG == 2 ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
+    pdl_trigger();
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; s++) {
             mbar_init(&full[s], 1);
@@ -371,8 +373,6 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         }
         mbar_init(sk_bar, 1);
         *abort_flag = 0;
-        // This launch's stream-K generation: flags set to it belong to this launch.
-        *sk_gen = p.stream_k ? __ldcg(p.sk_flag + p.sk_slots) + 1u : 0u;
         fence_mbar_init();
     }
     if (warp == 0 && lane == 0) {
@@ -382,6 +382,9 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
     constexpr bool WORDS = OUT == OUT_I32 || OUT == OUT_F32;
     const bool tma_store = WORDS && p.tma_store;
     if (tma_store && warp == 2 && lane == 0) prefetch_tmap(&tmap_c);
+    pdl_wait();  // the preceding grid is done: its outputs are readable and its TMEM is free
+    // This launch's stream-K generation: flags set to it belong to this launch.
+    if (threadIdx.x == 0) *sk_gen = p.stream_k ? __ldcg(p.sk_flag + p.sk_slots) + 1u : 0u;
     if (warp == 1) {
         if constexpr (CG == 2) {
             tmem_alloc_pair(tmem_holder, tc::TMEM_COLS);
@@ -665,6 +668,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::THREADS, 1)
 
 // ---- host side ---------------------------------------------------------------------------------------------------
 
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("ONEGPU_PDL");
+        return v == nullptr || std::strcmp(v, "0") != 0;
+    }();
+    return on;
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     if (fn == nullptr) {
@@ -751,14 +762,13 @@ static LaunchFn bind_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensor
             auto kern = int8_gemm_tc2_kernel<B_MN, OUT>;
             cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
             if (e != cudaSuccess) return e;
-            kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, mc, p, idesc);
+            return launch_pdl(kern, dim3(grid), dim3(tc::THREADS), C::SMEM_BYTES, stream, ma, mb, mc, p, idesc);
         } else {
             auto kern = int8_gemm_tc_kernel<B_MN, OUT>;
             cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
             if (e != cudaSuccess) return e;
-            kern<<<grid, tc::THREADS, C::SMEM_BYTES, stream>>>(ma, mb, mc, p, idesc);
+            return launch_pdl(kern, dim3(grid), dim3(tc::THREADS), C::SMEM_BYTES, stream, ma, mb, mc, p, idesc);
         }
-        return cudaGetLastError();
     };
 }
 

@@ -79,6 +79,14 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const void* tmap, ui
         : "memory");
 }
 
+// Programmatic dependent launch. Kernels launched with launch_pdl may start while the preceding grid in the stream
+// is finishing: pdl_wait() returns once that grid has completed and its writes are visible, so every such kernel calls
+// it before touching global memory or allocating TMEM (a predecessor still running on the SM may need its TMEM).
+// pdl_trigger() lets the next grid be scheduled as soon as every CTA of this one has started. Both are no-ops for
+// a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Bulk copy (no tensor map, no multicast) of `bytes` (a multiple of 16, both addresses 16-byte aligned) from global
 // memory into this CTA's shared memory, completing on the mbarrier.
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {

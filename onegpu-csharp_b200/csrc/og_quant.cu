@@ -16,7 +16,9 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "og_gemm.h"
 #include "og_host.h"
+#include "og_ptx.cuh"
 
 namespace og {
 
@@ -205,6 +207,8 @@ __device__ __forceinline__ void dq_scalar(const QuantArgs& a, int64_t j) {
 
 template <int KIND, bool HALF>
 __global__ void __launch_bounds__(QTHREADS) dequantize_kernel(const QuantArgs a) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int E = DqShape<KIND, HALF>::E;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -266,6 +270,8 @@ __device__ __forceinline__ void q_load16(const QuantArgs& a, int64_t first, floa
 // the multiply-first rounding; otherwise each element divides by its own scale.
 template <bool SIGNED, bool HALF>
 __global__ void __launch_bounds__(QTHREADS) quantize_kernel(const QuantArgs a) {
+    pdl_trigger();
+    pdl_wait();
     constexpr int E = 16;
     const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     uint8_t* y = static_cast<uint8_t*>(a.out);
@@ -329,14 +335,13 @@ static cudaError_t launch_dequantize(QuantArgs a, int kind, bool half, cudaStrea
     split_vectors(a, e, in_es, out_es, e * in_es, e * out_es);
     const unsigned blocks = grid_of(a);
     switch (kind * 2 + (half ? 1 : 0)) {
-        case 0: dequantize_kernel<0, false><<<blocks, QTHREADS, 0, s>>>(a); break;
-        case 1: dequantize_kernel<0, true><<<blocks, QTHREADS, 0, s>>>(a); break;
-        case 2: dequantize_kernel<1, false><<<blocks, QTHREADS, 0, s>>>(a); break;
-        case 3: dequantize_kernel<1, true><<<blocks, QTHREADS, 0, s>>>(a); break;
-        case 4: dequantize_kernel<2, false><<<blocks, QTHREADS, 0, s>>>(a); break;
-        default: dequantize_kernel<2, true><<<blocks, QTHREADS, 0, s>>>(a); break;
+        case 0: return launch_pdl(dequantize_kernel<0, false>, dim3(blocks), dim3(QTHREADS), 0, s, a);
+        case 1: return launch_pdl(dequantize_kernel<0, true>, dim3(blocks), dim3(QTHREADS), 0, s, a);
+        case 2: return launch_pdl(dequantize_kernel<1, false>, dim3(blocks), dim3(QTHREADS), 0, s, a);
+        case 3: return launch_pdl(dequantize_kernel<1, true>, dim3(blocks), dim3(QTHREADS), 0, s, a);
+        case 4: return launch_pdl(dequantize_kernel<2, false>, dim3(blocks), dim3(QTHREADS), 0, s, a);
+        default: return launch_pdl(dequantize_kernel<2, true>, dim3(blocks), dim3(QTHREADS), 0, s, a);
     }
-    return cudaGetLastError();
 }
 
 static cudaError_t launch_quantize(QuantArgs a, bool is_signed, bool half, cudaStream_t s);
@@ -363,12 +368,11 @@ static cudaError_t launch_quantize(QuantArgs a, bool is_signed, bool half, cudaS
     a.threads = a.vectors > scalar ? a.vectors : scalar;  // one vector per thread
     const unsigned blocks = grid_of(a);
     switch ((is_signed ? 2 : 0) + (half ? 1 : 0)) {
-        case 0: quantize_kernel<false, false><<<blocks, QTHREADS, 0, s>>>(a); break;
-        case 1: quantize_kernel<false, true><<<blocks, QTHREADS, 0, s>>>(a); break;
-        case 2: quantize_kernel<true, false><<<blocks, QTHREADS, 0, s>>>(a); break;
-        default: quantize_kernel<true, true><<<blocks, QTHREADS, 0, s>>>(a); break;
+        case 0: return launch_pdl(quantize_kernel<false, false>, dim3(blocks), dim3(QTHREADS), 0, s, a);
+        case 1: return launch_pdl(quantize_kernel<false, true>, dim3(blocks), dim3(QTHREADS), 0, s, a);
+        case 2: return launch_pdl(quantize_kernel<true, false>, dim3(blocks), dim3(QTHREADS), 0, s, a);
+        default: return launch_pdl(quantize_kernel<true, true>, dim3(blocks), dim3(QTHREADS), 0, s, a);
     }
-    return cudaGetLastError();
 }
 
 }  // namespace og

@@ -133,6 +133,21 @@ OG_API og_status og_buffer_free(og_device* device, void* ptr);
 OG_API og_status og_buffer_write(og_device* device, void* dst, const void* host_src, uint64_t bytes);
 /* GpuBuffer<T>.ReadAsync (GpuBufferOfT.cs:63-75) completed synchronously: returns after all prior work and the copy. */
 OG_API og_status og_buffer_read(og_device* device, void* host_dst, const void* src, uint64_t bytes);
+/* Asynchronous transfers on the device's copy engines (no counterpart in the reference's API beyond
+ * GpuBuffer<T>.ReadAsync being asynchronous, GpuBufferOfT.cs:63-75), so that uploads, products and readbacks of
+ * consecutive steps overlap.
+ * og_buffer_write_async: the copy runs on the upload stream as soon as possible, possibly while work submitted
+ * earlier still runs - the caller guarantees that no submitted work still reads or writes `dst`; work submitted
+ * afterwards waits for the copy. `host_src` should be page-locked (og_host_alloc) for the copy to be asynchronous. */
+typedef struct og_readback og_readback;
+OG_API og_status og_buffer_write_async(og_device* device, void* dst, const void* host_src, uint64_t bytes);
+/* og_buffer_read_async: queues, on the readback stream, the copy of `bytes` from `src` to page-locked host memory
+ * after all work submitted so far, without blocking the caller or later submissions; og_readback_wait blocks until
+ * that copy has finished (reporting OG_ERROR_COMMAND_FAILED if a kernel before it gave up a bounded wait) and
+ * releases the ticket. */
+OG_API og_status og_buffer_read_async(og_device* device, void* host_dst, const void* src, uint64_t bytes,
+                                      og_readback** ticket);
+OG_API og_status og_readback_wait(og_readback* ticket);
 /* Fills bytes of a buffer with a value, in stream order. */
 OG_API og_status og_buffer_fill(og_device* device, void* dst, int32_t value, uint64_t bytes);
 /* Page-locked host memory for fast uploads and readbacks. */

@@ -134,6 +134,12 @@ using namespace og_host;
 
 using Op = OgOp;
 
+struct og_readback {
+    og_device* device = nullptr;
+    cudaEvent_t done = nullptr;
+    int* status_host = nullptr;  // the device's failure word as it stood when the copy ran
+};
+
 struct og_timestamps {
     og_device* device = nullptr;
     std::vector<cudaEvent_t> events;
@@ -564,11 +570,15 @@ OG_API og_status og_device_create(int32_t ordinal, og_device** out) {
             check_cuda(cudaGetDeviceProperties(&d->prop, ordinal), "cudaGetDeviceProperties");
             d->sm_count = d->prop.multiProcessorCount;
             check_cuda(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+            check_cuda(cudaStreamCreateWithFlags(&d->upload, cudaStreamNonBlocking), "cudaStreamCreate");
+            check_cuda(cudaStreamCreateWithFlags(&d->readback, cudaStreamNonBlocking), "cudaStreamCreate");
             check_cuda(cudaMalloc(&d->status, sizeof(int)), "cudaMalloc");
             check_cuda(cudaMemset(d->status, 0, sizeof(int)), "cudaMemset");
             check_cuda(cudaMallocHost(&d->status_host, sizeof(int)), "cudaMallocHost");
         } catch (...) {
             if (d->stream) cudaStreamDestroy(d->stream);
+            if (d->upload) cudaStreamDestroy(d->upload);
+            if (d->readback) cudaStreamDestroy(d->readback);
             if (d->status) cudaFree(d->status);
             delete d;
             throw;
@@ -582,7 +592,11 @@ OG_API og_status og_device_destroy(og_device* d) {
         if (d == nullptr) return;
         use(d);
         cudaStreamSynchronize(d->stream);
+        cudaStreamSynchronize(d->upload);
+        cudaStreamSynchronize(d->readback);
         if (d->own_stream) cudaStreamDestroy(d->stream);
+        cudaStreamDestroy(d->upload);
+        cudaStreamDestroy(d->readback);
         cudaFree(d->status);
         cudaFreeHost(d->status_host);
         delete d;
@@ -609,6 +623,8 @@ OG_API og_status og_device_wait_idle(og_device* d) {
     return guard([&] {
         if (d == nullptr) null_arg("GpuDevice", "device");
         use(d);
+        check_cuda(cudaStreamSynchronize(d->upload), "WaitIdle");
+        check_cuda(cudaStreamSynchronize(d->readback), "WaitIdle");
         check_device_status(d);
     });
 }
@@ -694,6 +710,74 @@ OG_API og_status og_buffer_read(og_device* d, void* dst, const void* src, uint64
         use(d);
         if (bytes != 0) check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, d->stream), "ReadAsync");
         check_device_status(d);
+    });
+}
+
+OG_API og_status og_buffer_write_async(og_device* d, void* dst, const void* src, uint64_t bytes) {
+    return guard([&] {
+        if (d == nullptr) null_arg("GpuDevice", "device");
+        if (bytes == 0) return;
+        if (dst == nullptr || src == nullptr) null_arg("GpuDevice", "buffer");
+        use(d);
+        cudaEvent_t done = nullptr;
+        check_cuda(cudaEventCreateWithFlags(&done, cudaEventDisableTiming), "WriteBuffer");
+        cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, d->upload);
+        if (e == cudaSuccess) e = cudaEventRecord(done, d->upload);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(d->stream, done, 0);  // later submissions wait for the upload
+        cudaEventDestroy(done);
+        check_cuda(e, "WriteBuffer");
+    });
+}
+
+OG_API og_status og_buffer_read_async(og_device* d, void* dst, const void* src, uint64_t bytes, og_readback** out) {
+    return guard([&] {
+        if (d == nullptr) null_arg("GpuDevice", "device");
+        if (out == nullptr) null_arg("GpuDevice", "readback");
+        if (dst == nullptr || src == nullptr) null_arg("GpuDevice", "buffer");
+        use(d);
+        auto* r = new og_readback();
+        r->device = d;
+        try {
+            cudaEvent_t submitted = nullptr;
+            check_cuda(cudaMallocHost(&r->status_host, sizeof(int)), "ReadAsync");
+            check_cuda(cudaEventCreateWithFlags(&submitted, cudaEventDisableTiming), "ReadAsync");
+            cudaError_t e = cudaEventRecord(submitted, d->stream);  // everything submitted so far
+            if (e == cudaSuccess) e = cudaStreamWaitEvent(d->readback, submitted, 0);
+            cudaEventDestroy(submitted);
+            check_cuda(e, "ReadAsync");
+            check_cuda(cudaMemcpyAsync(r->status_host, d->status, sizeof(int), cudaMemcpyDeviceToHost, d->readback),
+                       "ReadAsync");
+            if (bytes != 0)
+                check_cuda(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, d->readback), "ReadAsync");
+            check_cuda(cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming), "ReadAsync");
+            check_cuda(cudaEventRecord(r->done, d->readback), "ReadAsync");
+        } catch (...) {
+            if (r->done) cudaEventDestroy(r->done);
+            if (r->status_host) cudaFreeHost(r->status_host);
+            delete r;
+            throw;
+        }
+        *out = r;
+    });
+}
+
+OG_API og_status og_readback_wait(og_readback* r) {
+    return guard([&] {
+        if (r == nullptr) null_arg("GpuDevice", "readback");
+        struct Release {
+            og_readback* r;
+            ~Release() {
+                cudaEventDestroy(r->done);
+                cudaFreeHost(r->status_host);
+                delete r;
+            }
+        } release{r};
+        use(r->device);
+        check_cuda(cudaEventSynchronize(r->done), "ReadAsync");
+        if (*r->status_host != 0)
+            throw OgError{OG_ERROR_COMMAND_FAILED, "GpuDevice", "",
+                          "a kernel gave up waiting on its own pipeline (watchdog) and skipped its work", "Watchdog",
+                          "", ""};
     });
 }
 

@@ -21,6 +21,8 @@ struct og_device {
     cudaDeviceProp prop = {};
     int* status = nullptr;       // device word a kernel sets when a bounded wait gave up
     int* status_host = nullptr;  // pinned mirror for readbacks
+    cudaStream_t upload = nullptr;    // copy-engine stream of og_buffer_write_async
+    cudaStream_t readback = nullptr;  // copy-engine stream of og_buffer_read_async
 };
 
 // One recorded piece of work: launches on the stream it is given.

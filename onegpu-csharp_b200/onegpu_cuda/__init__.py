@@ -137,6 +137,9 @@ EXPORTS = {
                                    ctypes.c_int32, _BUF, ctypes.c_int32],
     "og_dynamic_quantize_check": [_BUF, ctypes.c_int32, ctypes.c_int32, _BUF, ctypes.c_int32, _BUF, ctypes.c_int32,
                                   _BUF, ctypes.c_int32],
+    "og_buffer_write_async": [_P, _P, _P, ctypes.c_uint64],
+    "og_buffer_read_async": [_P, _P, _P, ctypes.c_uint64, _PP],
+    "og_readback_wait": [_P],
     "og_dequantize_create": [_P, _PP],
     "og_dequantize_destroy": [_P],
     "og_dequantize_encode": [_P, _P] + _QUANT_ARGS,
@@ -340,6 +343,40 @@ class GpuTimestampSet:
             self.handle = None
 
 
+class PinnedHost:
+    """Page-locked host memory (og_host_alloc) for asynchronous uploads and readbacks; `view` gives numpy arrays."""
+
+    def __init__(self, nbytes: int):
+        p = ctypes.c_void_p()
+        _check(_lib.og_host_alloc(nbytes, ctypes.byref(p)))
+        self.ptr = p.value
+        self.nbytes = nbytes
+
+    def view(self, dtype, count: int, offset: int = 0) -> np.ndarray:
+        dt = np.dtype(dtype)
+        if offset + count * dt.itemsize > self.nbytes:
+            raise ValueError("view past the end of the pinned buffer")
+        raw = (ctypes.c_uint8 * (count * dt.itemsize)).from_address(self.ptr + offset)
+        return np.frombuffer(raw, dtype=dt, count=count)
+
+    def dispose(self) -> None:
+        if self.ptr:
+            _check(_lib.og_host_free(ctypes.c_void_p(self.ptr)))
+            self.ptr = None
+
+
+class GpuReadback:
+    """A readback queued by GpuDevice.read_async; wait() blocks until the bytes are in host memory."""
+
+    def __init__(self, handle):
+        self.handle = handle
+
+    def wait(self) -> None:
+        if self.handle:
+            h, self.handle = self.handle, None
+            _check(_lib.og_readback_wait(h))
+
+
 class GpuDevice:
     """The CUDA backend's device (compute subset of GpuDevice, src/RecursiveAI.OneGpu/GpuDevice.cs:27-228)."""
 
@@ -382,6 +419,18 @@ class GpuDevice:
     def wait_idle(self) -> None:
         _check(_lib.og_device_wait_idle(self.handle))
         self._keep.clear()
+
+    def write_async(self, dst_ptr: int, host_ptr: int, nbytes: int) -> None:
+        """og_buffer_write_async: upload on the copy engine, overlapping earlier work that does not use `dst`;
+        later submissions wait for it. `host_ptr` should be page-locked (og_host_alloc)."""
+        _check(_lib.og_buffer_write_async(self.handle, ctypes.c_void_p(dst_ptr), ctypes.c_void_p(host_ptr), nbytes))
+
+    def read_async(self, host_ptr: int, src_ptr: int, nbytes: int) -> "GpuReadback":
+        """og_buffer_read_async: readback after the work submitted so far, without blocking; wait() on the result."""
+        h = ctypes.c_void_p()
+        _check(_lib.og_buffer_read_async(self.handle, ctypes.c_void_p(host_ptr), ctypes.c_void_p(src_ptr), nbytes,
+                                         ctypes.byref(h)))
+        return GpuReadback(h.value)
 
     def watchdog_selftest(self, limit_us: int) -> None:
         """Queues a kernel whose bounded wait runs out after ``limit_us``; the next wait_idle raises

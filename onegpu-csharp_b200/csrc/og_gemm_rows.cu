@@ -34,6 +34,8 @@ constexpr int TMEM_COLS = 32;             // columns 0..15 dot products, 16..31 
 constexpr int SMEM_BYTES = STAGES * (B_BYTES + A_BYTES) + ONES_BYTES + 1024 + 256;
 }  // namespace rows
 
+constexpr int SUMS_SMEM_BYTES = rows::STAGES * rows::B_BYTES + rows::ONES_BYTES + 1024 + 256;
+
 struct RowsParams {
     int m, n, k;
     int k_blocks;
@@ -243,6 +245,139 @@ done:
     if (threadIdx.x == 0 && *abort_flag) atomicExch(p.error_flag, 1);
 }
 
+// ---- byte sums of two matrices in one launch ------------------------------------------------------------------------
+//
+// The zero-point correction needs the byte sums over K of A's rows and of B's columns. Each is a stream of the
+// operand through the tensor cores against a block of ones: D[c, j] = sum_k T[c, k] * 1 with 128 rows or columns c
+// of the operand as the MMA's M side and N = 16. One launch covers both operands: the first job's CTAs come first in
+// the grid, then the second's; the layout (K-major rows, or MN-major columns) and the tensor map are the job's.
+
+struct SumsJob {
+    int32_t* out;  // [splits][batches][cols]
+    int cols, tiles, batches, splits;
+    int k_blocks_total, k_blocks;  // K blocks of the whole operand, and of one split
+    int kmajor;                    // cols x K with K contiguous (1), or K x cols with columns contiguous (0)
+    int batched;
+    uint32_t idesc;
+    int ctas;  // tiles * batches * splits
+};
+
+struct SumsParams {
+    SumsJob job[2];
+    int* error_flag;
+};
+
+__global__ void __launch_bounds__(rows::THREADS, 2)
+    int8_byte_sums_kernel(const __grid_constant__ CUtensorMap tmap0, const __grid_constant__ CUtensorMap tmap1,
+                          const __grid_constant__ SumsParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sB = smem;                                   // [STAGES][128 rows or columns x 128 k]
+    uint8_t* sOnes = sB + rows::STAGES * rows::B_BYTES;   // [16 rows x 128 k] of ones
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + rows::ONES_BYTES);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + rows::STAGES;
+    uint64_t* tfull = bars + 2 * rows::STAGES;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * rows::STAGES + 1);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int j = static_cast<int>(blockIdx.x) < p.job[0].ctas ? 0 : 1;
+    const SumsJob& job = p.job[j];
+    const CUtensorMap* tmap = j == 0 ? &tmap0 : &tmap1;
+    const int local = static_cast<int>(blockIdx.x) - (j == 0 ? 0 : p.job[0].ctas);
+    const int tile = local % job.tiles;
+    const int rest = local / job.tiles;
+    const int b = rest % job.batches;
+    const int split = rest / job.batches;
+    const int kb_begin = split * job.k_blocks;
+    const int kb_count = min(job.k_blocks, job.k_blocks_total - kb_begin);
+    pdl_trigger();
+
+    for (int i = threadIdx.x; i < rows::ONES_BYTES / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(sOnes)[i] = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> visible to the tensor cores
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < rows::STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(tfull, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) prefetch_tmap(tmap);
+    pdl_wait();  // the preceding grid is done: the operands are written and its TMEM is free
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, rows::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+    const int bz = job.batched ? b : 0;
+
+    if (warp == 0) {
+        for (int kb = 0; kb < kb_count; kb++) {
+            const int s = kb % rows::STAGES;
+            const uint32_t ph = (kb / rows::STAGES) & 1;
+            const int kc = (kb_begin + kb) * rows::BK;
+            if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) goto done;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[s], rows::B_BYTES);
+                if (job.kmajor)
+                    tma_load_3d(sB + s * rows::B_BYTES, tmap, &full[s], kc, tile * rows::BN, bz);
+                else
+                    tma_load_3d(sB + s * rows::B_BYTES, tmap, &full[s], tile * rows::BN, kc, bz);
+            }
+            __syncwarp();
+        }
+    } else if (warp == 1) {
+        for (int kb = 0; kb < kb_count; kb++) {
+            const int s = kb % rows::STAGES;
+            const uint32_t ph = (kb / rows::STAGES) & 1;
+            if (!mbar_wait(&full[s], ph, abort_flag)) goto done;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t t_addr = smem_u32(sB + s * rows::B_BYTES);
+                const uint32_t o_addr = smem_u32(sOnes);
+#pragma unroll
+                for (int kk = 0; kk < rows::BK / 32; kk++) {
+                    const uint64_t tdesc = job.kmajor ? smem_desc_sw128(t_addr + kk * 32, 16, 1024)
+                                                      : smem_desc_sw128(t_addr + kk * 32 * 128, rows::B_BYTES, 1024);
+                    mma_i8(tmem_base, tdesc, smem_desc_sw128(o_addr + kk * 32, 16, 1024), job.idesc,
+                           (kb | kk) != 0 ? 1u : 0u);
+                }
+                mma_commit(&empty[s]);
+            }
+            __syncwarp();
+        }
+        if (lane == 0) mma_commit(tfull);
+        __syncwarp();
+    } else {
+        const int q = warp & 3;
+        if (!mbar_wait(tfull, 0, abort_flag)) goto done;
+        tc_fence_after();
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16), r);
+        tmem_ld_wait();
+        const int c = tile * rows::BN + q * 32 + lane;
+        if (c < job.cols)
+            job.out[(static_cast<int64_t>(split) * job.batches + b) * job.cols + c] = static_cast<int32_t>(r[0]);
+        tc_fence_before();
+    }
+
+done:
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, rows::TMEM_COLS);
+    }
+    if (threadIdx.x == 0 && *abort_flag) atomicExch(p.error_flag, 1);
+}
+
 // ---- host side ---------------------------------------------------------------------------------------------------
 
 bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint64_t stride_y,
@@ -359,6 +494,80 @@ LaunchFn prepare_byte_sums_tc(const uint8_t* mat, int cols, int k, int64_t ld, i
     const dim3 grid((cols + rows::BN - 1) / rows::BN, batches, splits);
     return k_major ? bind_rows_t<true, OUT_I32>(p, mb, mb, grid, idesc)
                    : bind_rows_t<false, OUT_I32>(p, mb, mb, grid, idesc);
+}
+
+// One sums job: `mat` is cols x K with K contiguous (k_major) or K x cols with columns contiguous.
+static bool sums_job(SumsJob& j, CUtensorMap& map, const uint8_t* mat, int cols, int k, int64_t ld, int64_t bstride,
+                     int batches, bool k_major, bool is_signed, int32_t* out, int splits) {
+    const uint64_t rows_stored = k_major ? cols : k;
+    const uint64_t sb = batches > 1 ? uint64_t(bstride) : (uint64_t(ld) * rows_stored + 15) & ~uint64_t(15);
+    const bool ok = k_major ? make_tensor_map_u8(&map, mat, k, cols, batches, ld, sb, rows::BK, rows::BN)
+                            : make_tensor_map_u8(&map, mat, cols, k, batches, ld, sb, rows::BN, rows::BK);
+    if (!ok) return false;
+    j.out = out;
+    j.cols = cols;
+    j.tiles = (cols + rows::BN - 1) / rows::BN;
+    j.batches = batches;
+    j.splits = splits;
+    j.k_blocks_total = (k + rows::BK - 1) / rows::BK;
+    j.k_blocks = (j.k_blocks_total + splits - 1) / splits;  // every split gets at least one K block (sums_splits)
+    j.kmajor = k_major ? 1 : 0;
+    j.batched = batches > 1;
+    j.idesc = idesc_i8(is_signed, false, !k_major, false, rows::BN, rows::MAXM);
+    j.ctas = j.tiles * batches * splits;
+    return true;
+}
+
+// The byte sums of A's rows (row_sums, when non-null) and of B's columns (col_sums) in one launch, each as `splits`
+// partial sums over K ([splits][batches][rows or columns]).
+LaunchFn prepare_byte_sums_pair_tc(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, int splits,
+                                   cudaError_t* err) {
+    *err = cudaErrorInvalidValue;
+    const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
+    const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
+    SumsParams p = {};
+    CUtensorMap maps[2];
+    int jobs = 0;
+    if (row_sums != nullptr) {
+        if (!sums_job(p.job[jobs], maps[jobs], L.a, L.m, L.k, L.lda, L.stride_a, ba, true, L.a_signed, row_sums, splits))
+            return nullptr;
+        jobs++;
+    }
+    if (col_sums != nullptr) {
+        if (!sums_job(p.job[jobs], maps[jobs], L.b, L.n, L.k, L.ldb, L.stride_b, bb, L.trans_b != 0, L.b_signed,
+                      col_sums, splits))
+            return nullptr;
+        jobs++;
+    }
+    if (jobs == 0) {
+        *err = cudaSuccess;
+        return [](cudaStream_t) { return cudaSuccess; };
+    }
+    if (jobs == 1) {
+        p.job[1] = p.job[0];
+        p.job[1].ctas = 0;
+        maps[1] = maps[0];
+    }
+    p.error_flag = L.error_flag;
+    const int64_t ctas = int64_t(p.job[0].ctas) + p.job[1].ctas;
+    if (ctas > 0x7FFFFFFF) return nullptr;
+    *err = cudaSuccess;
+    const CUtensorMap m0 = maps[0], m1 = maps[1];
+    const dim3 grid(static_cast<unsigned>(ctas));
+    return [=](cudaStream_t stream) -> cudaError_t {
+        static uint64_t configured = 0;
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        const uint64_t bit = uint64_t(1) << (dev & 63);
+        if (!(configured & bit)) {
+            e = cudaFuncSetAttribute(int8_byte_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     SUMS_SMEM_BYTES);
+            if (e != cudaSuccess) return e;
+            configured |= bit;
+        }
+        return launch_pdl(int8_byte_sums_kernel, grid, dim3(rows::THREADS), SUMS_SMEM_BYTES, stream, m0, m1, p);
+    };
 }
 
 cudaError_t launch_gemm_rows(const GemmLaunch& L, cudaStream_t stream) {

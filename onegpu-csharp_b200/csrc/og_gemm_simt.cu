@@ -277,24 +277,9 @@ LaunchFn prepare_byte_sums(const GemmLaunch& L, int32_t* row_sums, int32_t* col_
         }
         return [L, row_sums, col_sums](cudaStream_t s) { return launch_byte_sums_simt(L, row_sums, col_sums, s); };
     }
-    LaunchFn rows_fn, cols_fn;
-    if (row_sums != nullptr) {
-        rows_fn = prepare_byte_sums_tc(L.a, L.m, L.k, L.lda, L.stride_a, ba, true, L.a_signed, row_sums, splits,
-                                       L.error_flag, err);
-        if (!rows_fn) return nullptr;
-    }
-    if (col_sums != nullptr) {
-        cols_fn = prepare_byte_sums_tc(L.b, L.n, L.k, L.ldb, L.stride_b, bb, L.trans_b != 0, L.b_signed, col_sums,
-                                       splits, L.error_flag, err);
-        if (!cols_fn) return nullptr;
-    }
-    return [rows_fn, cols_fn](cudaStream_t s) -> cudaError_t {
-        if (rows_fn) {
-            const cudaError_t e = rows_fn(s);
-            if (e != cudaSuccess) return e;
-        }
-        return cols_fn ? cols_fn(s) : cudaSuccess;
-    };
+    (void)ba;
+    (void)bb;
+    return prepare_byte_sums_pair_tc(L, row_sums, col_sums, splits, err);  // both operands in one launch
 }
 
 cudaError_t launch_byte_sums(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, cudaStream_t stream) {

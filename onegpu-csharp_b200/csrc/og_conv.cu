@@ -36,7 +36,22 @@ struct PackArgs {
     int32_t rows;       // K
     int32_t groups, cin, cin_g, h, w, oh, ow, kh, kw, sh, sw, dh, dw, ph, pw;
     int32_t ld;         // bytes per matrix row
+    uint32_t ow_magic;  // n / ow = (umulhi(ow_magic, n) + n) >> ow_shift for 0 <= n < 2^31
+    int32_t ow_shift;
 };
+
+// n / d for 0 <= n < 2^31 by multiplication (Granlund and Montgomery, "Division by Invariant Integers using
+// Multiplication", 1994): magic and shift from magic_for(d).
+__device__ __forceinline__ int32_t div_magic(int32_t n, uint32_t magic, int32_t shift) {
+    return static_cast<int32_t>((__umulhi(magic, static_cast<uint32_t>(n)) + static_cast<uint32_t>(n)) >> shift);
+}
+
+static void magic_for(uint32_t d, uint32_t* magic, int32_t* shift) {
+    int32_t l = 0;
+    while ((uint64_t(1) << l) < d) l++;  // ceil(log2 d)
+    *magic = static_cast<uint32_t>(((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1);
+    *shift = l;
+}
 
 // Unit t covers BYTES consecutive columns of one matrix row: row (c * KH + kh) * KW + kw of matrix (image, group)
 // holds x[image, g * CinG + c, oh * SH - PH + kh * DH, ow * SW - PW + kw * DW] at column oh * OW + ow, or the zero
@@ -117,39 +132,46 @@ __global__ void __launch_bounds__(PACK_THREADS) conv_pack_plane_kernel(const Pac
     const uint32_t pad = a.zp != nullptr ? __ldg(a.zp) : 0u;
     const int32_t taps = a.kh * a.kw;
     const int32_t ncols = a.oh * a.ow;
-    const int64_t items = static_cast<int64_t>(taps) * a.units_per_row;
+    // A plane's items (taps x units of one matrix row) fit 32-bit arithmetic, which is far cheaper than 64-bit here.
+    const int32_t upr = a.units_per_row;
     uint8_t* rows0 = a.cols + (ig * a.rows + static_cast<int64_t>(c) * taps) * a.ld;
-    for (int64_t it = threadIdx.x; it < items; it += PACK_THREADS) {
-        const int32_t kk = static_cast<int32_t>(it / a.units_per_row);
-        const int32_t col0 = static_cast<int32_t>(it - static_cast<int64_t>(kk) * a.units_per_row) * BYTES;
+    // Taps in the outer loop (uniform, no division per item); the output position of a unit's first column by one
+    // multiply-high (div_magic). Output (oy, ox) reads input row oy * SH + dy, column ox * SW + dx.
+    for (int32_t kk = 0; kk < taps; kk++) {
         const int32_t kh = kk / a.kw;
         const int32_t kw = kk - kh * a.kw;
-        int32_t oy = col0 / a.ow;
-        int32_t ox = col0 - oy * a.ow;
-        uint32_t word[BYTES / 4];
+        const int32_t dy = kh * a.dh - a.ph;
+        const int32_t dx = kw * a.dw - a.pw;
+        uint8_t* row_dst = rows0 + static_cast<int64_t>(kk) * a.ld;
+        for (int32_t u = threadIdx.x; u < upr; u += PACK_THREADS) {
+            const int32_t col0 = u * BYTES;
+            int32_t oy = div_magic(col0, a.ow_magic, a.ow_shift);
+            int32_t ox = col0 - oy * a.ow;
+            int32_t iy = oy * a.sh + dy;
+            int32_t ix = ox * a.sw + dx;
+            uint32_t word[BYTES / 4];
 #pragma unroll
-        for (int q = 0; q < BYTES / 4; q++) word[q] = 0;
+            for (int q = 0; q < BYTES / 4; q++) word[q] = 0;
 #pragma unroll
-        for (int e = 0; e < BYTES; e++) {
-            uint32_t v = pad;
-            if (col0 + e < ncols) {
-                const int32_t iy = oy * a.sh + kh * a.dh - a.ph;
-                const int32_t ix = ox * a.sw + kw * a.dw - a.pw;
-                if (static_cast<uint32_t>(iy) < static_cast<uint32_t>(a.h) &&
+            for (int e = 0; e < BYTES; e++) {
+                uint32_t v = pad;
+                if (col0 + e < ncols && static_cast<uint32_t>(iy) < static_cast<uint32_t>(a.h) &&
                     static_cast<uint32_t>(ix) < static_cast<uint32_t>(a.w))
                     v = plane_s[iy * a.w + ix];
+                word[e >> 2] |= v << (8 * (e & 3));
+                ix += a.sw;
+                if (++ox == a.ow) {
+                    ox = 0;
+                    ix = dx;
+                    iy += a.sh;
+                }
             }
-            word[e >> 2] |= v << (8 * (e & 3));
-            if (++ox == a.ow) {
-                ox = 0;
-                oy++;
-            }
+            uint8_t* dst = row_dst + col0;
+            if constexpr (BYTES == 16)
+                *reinterpret_cast<uint4*>(dst) = make_uint4(word[0], word[1], word[2], word[3]);
+            else
+                *reinterpret_cast<uint32_t*>(dst) = word[0];
         }
-        uint8_t* dst = rows0 + static_cast<int64_t>(kk) * a.ld + col0;
-        if constexpr (BYTES == 16)
-            *reinterpret_cast<uint4*>(dst) = make_uint4(word[0], word[1], word[2], word[3]);
-        else
-            *reinterpret_cast<uint32_t*>(dst) = word[0];
     }
 }
 
@@ -159,8 +181,12 @@ static cudaError_t launch_conv_pack(const PackArgs& a, int64_t planes, cudaStrea
     if (hw <= PLANE_SMEM_MAX && planes <= 0x7FFFFFFF) {
         const unsigned grid = static_cast<unsigned>(planes);
         const size_t smem = static_cast<size_t>((hw + 15) & ~15);
-        return wide ? launch_pdl(conv_pack_plane_kernel<16>, dim3(grid), dim3(PACK_THREADS), smem, s, a)
-                    : launch_pdl(conv_pack_plane_kernel<4>, dim3(grid), dim3(PACK_THREADS), smem, s, a);
+        // Four columns per thread: adjacent lanes gather from shared memory 4 * stride bytes apart (at most 2-way
+        // bank conflicts at stride 2, none at stride 1), and each warp stores 128 contiguous bytes.
+        PackArgs b = a;
+        b.units_per_row = a.ld / 4;
+        b.units = a.units * (a.ld / 4) / a.units_per_row;
+        return launch_pdl(conv_pack_plane_kernel<4>, dim3(grid), dim3(PACK_THREADS), smem, s, b);
     }
     const unsigned blocks = static_cast<unsigned>((a.units + PACK_THREADS - 1) / PACK_THREADS);
     return wide ? launch_pdl(conv_pack_kernel<16>, dim3(blocks), dim3(PACK_THREADS), 0, s, a)
@@ -498,6 +524,7 @@ OG_API og_status og_conv_integer_encode(og_conv_integer* cv, og_encoder* enc, co
             a.dw = p.dilation_width;
             a.ph = p.pad_top;
             a.pw = p.pad_left;
+            og::magic_for(static_cast<uint32_t>(c.g.ow), &a.ow_magic, &a.ow_shift);
             const int64_t planes = images * p.groups * cin_g;
             enc->ops.push_back([=](cudaStream_t s) { return og::launch_conv_pack(a, planes, s); });
             enc->dispatches += 1;

@@ -72,7 +72,8 @@ def load_peaks():
 
 
 PROFILES = {"c3": "int8_gemm_tc2_c3.md", "c2": "dql_int8_gemm_chain_c2.md", "c4": "int8_gemm_tc2_c4.md",
-            "c5": "int8_gemm_rows_c5.md", "dequant": "dequantize_linear_dequant.md"}
+            "c5": "int8_gemm_rows_c5.md", "dequant": "dequantize_linear_dequant.md",
+            "quant": "quantize_linear_quant.md", "conv": "conv_integer_conv.md"}
 
 
 def profile_traffic(workload: str):

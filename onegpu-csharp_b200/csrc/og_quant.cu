@@ -19,6 +19,7 @@
 #include "og_gemm.h"
 #include "og_host.h"
 #include "og_ptx.cuh"
+#include "og_qmath.cuh"
 
 namespace og {
 
@@ -96,36 +97,7 @@ __device__ __forceinline__ void qparam_load(const QuantArgs& a, uint32_t pi, QPa
     q.zf = static_cast<float>(zp);
 }
 
-// round_half_even(x / s), the quotient correctly rounded (IEEE division); kept out of line so that callers that
-// reach it rarely do not pay for it inline.
-__device__ __noinline__ float rne_quotient_exact(float x, float s) { return rintf(__fdiv_rn(x, s)); }
-
 __device__ __forceinline__ float rne_quotient(float x, const QParam& p) { return rne_quotient_exact(x, p.s); }
-
-// The same value when the scale is shared by many elements: with r = RN(1 / s) and m = RN(x * r),
-// |m - x/s| <= |x/s| (2^-23 + 2^-48) and the correctly rounded quotient lies within |x/s| 2^-24 of x/s, so both round
-// to the same integer unless a half-integer lies within about |m| 2^-22 of m. m is used when the nearest half-integer
-// is further than |m| 2^-20 + 2^-20 away (and |m| < 2^22, where m - (floor(m) + 0.5) is within 2^-25 of exact);
-// otherwise - near ties, for NaN, infinities and huge values - the quotient itself is rounded. `r_ok` says r is
-// finite and normal.
-__device__ __forceinline__ float rne_quotient_r(float x, float s, float r, bool r_ok) {
-    if (r_ok) {
-        const float m = __fmul_rn(x, r);
-        const float am = fabsf(m);
-        const float d = fabsf(__fsub_rn(m, __fadd_rn(floorf(m), 0.5f)));
-        if (am < 4194304.0f && d > __fmaf_rn(am, 9.5367431640625e-07f, 9.5367431640625e-07f)) return rintf(m);
-    }
-    return rne_quotient_exact(x, s);
-}
-
-template <bool SIGNED>
-__device__ __forceinline__ uint32_t saturate_byte(float v) {
-    const float lo = SIGNED ? -128.0f : 0.0f;
-    const float hi = SIGNED ? 127.0f : 255.0f;
-    if (isnan(v)) v = lo;
-    v = v < lo ? lo : (v > hi ? hi : v);
-    return static_cast<uint32_t>(static_cast<int32_t>(v)) & 0xFFu;
-}
 
 template <bool SIGNED>
 __device__ __forceinline__ uint32_t quantize_with(float xv, const QParam& p) {

@@ -142,3 +142,46 @@ def test_large_tensors_per_axis(device):
             b.dispose()
     finally:
         k.dispose()
+
+
+def _near_ties(scale: np.float32, n: int, rng) -> np.ndarray:
+    """Values within a few ulps of (k + 1/2) * scale, where the quotient's rounding is decided by its last bits."""
+    k = rng.integers(-300, 300, size=n).astype(np.float64)
+    base = ((k + 0.5) * np.float64(scale)).astype(np.float32)
+    return (base.view(np.int32) + rng.integers(-4, 5, size=n).astype(np.int32)).view(np.float32)
+
+
+@pytest.mark.gpu
+def test_quantize_near_ties(device):
+    """The uniform-scale quotient (multiply by the rounded reciprocal, divide where that could round differently) on
+    inputs crowded around half-integer quotients, plus NaN, infinities, zeros, subnormals and huge values, per tensor
+    and per axis (long runs of one scale), against the oracle's division."""
+    k = og.DequantizeKernels(device)
+    rng = np.random.default_rng(11)
+    specials = np.array([np.nan, np.inf, -np.inf, 0.0, -0.0, 1e-42, -1e-42, 3e38, -3e38, 1e-30, 7e6, -7e6],
+                        np.float32)
+    try:
+        for scale in (np.float32(0.1), np.float32(0.0234), np.float32(3.0), np.float32(1e-3), np.float32(7.5e-6),
+                      np.float32(1e30), np.float32(1e-38)):
+            count = 1 << 16
+            x = np.concatenate([_near_ties(scale, count - specials.size, rng), specials])
+            for signed in (False, True):
+                for per_axis in (False, True):
+                    shape, axis = ([4, 4, count // 16], 1) if per_axis else ([count], 0)
+                    axis_len = 4 if per_axis else 1
+                    scales = np.full(axis_len, scale, np.float32)
+                    zp = rng.integers(-20, 20, size=axis_len + 3, dtype=np.int16).astype(np.int8)
+                    zp = zp if signed else zp.view(np.uint8)
+                    out_t = np.int8 if signed else np.uint8
+                    bx, bs = device.create_buffer(np.float32, x), device.create_buffer(np.float32, scales)
+                    bz, by = device.create_buffer(out_t, zp.view(out_t)), device.create_buffer(out_t, count)
+                    enc = device.begin_commands()
+                    k.encode_quantize(enc, bx, 0, shape, axis, per_axis, bs, 0, bz, 0, by, 0)
+                    device.submit(enc)
+                    got = by.read().view(np.uint8)
+                    want = oracle.quantize(x, shape, axis, per_axis, scales, zp[:axis_len], signed)
+                    for b in (bx, bs, bz, by):
+                        b.dispose()
+                    assert np.array_equal(got, want), f"scale {scale} signed {signed} per_axis {per_axis}"
+    finally:
+        k.dispose()

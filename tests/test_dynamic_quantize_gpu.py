@@ -138,3 +138,32 @@ def test_dynamic_quantize_feeds_the_product_without_leaving_the_device(device):
         assert bs.read()[0].view(np.uint32) == np.float32(wscale).view(np.uint32)
         for v in (bx, by, bs, bz, bw, bscale, bc):
             v.dispose()
+
+
+def test_dynamic_quantize_near_ties(device):
+    """Inputs crowded within a few ulps of half-integer quotients x / scale, the scale fixed by the range's ends,
+    for ranges that give zero points at 0, in the middle and at 255; sizes that take the vector and scalar paths."""
+    rng = np.random.default_rng(3)
+    with og.DynamicQuantizeKernels(device) as dq:
+        for lo, hi in ((-1.0, 3.0), (-2.5, 0.75), (0.0, 1.7), (-0.3, 0.0), (-1000.0, 10.0)):
+            _, scale, _ = oracle.dynamic_quantize(np.array([lo, hi], np.float32))
+            scale = np.float32(scale)
+            for count, off in ((1 << 20, 0), (100003, 1)):
+                k = rng.integers(int(np.ceil(lo / scale)), int(np.floor(hi / scale)), size=count).astype(np.float64)
+                x = ((k + 0.5) * np.float64(scale)).astype(np.float32)
+                x = (x.view(np.int32) + rng.integers(-4, 5, size=count).astype(np.int32)).view(np.float32)
+                x = np.clip(x, np.float32(lo), np.float32(hi)).astype(np.float32)
+                x[:2] = (lo, hi)
+                wy, ws, wz = oracle.dynamic_quantize(x)
+                assert np.float32(ws) == scale
+                bx = device.create_buffer(np.float32, np.concatenate([np.zeros(off, np.float32), x]))
+                by = device.create_buffer(np.uint8, count + off + 3)
+                bs, bz = device.create_buffer(np.float32, 1), device.create_buffer(np.uint8, 4)
+                enc = device.begin_commands()
+                dq.encode(enc, bx, off, count, by, off, bs, 0, bz, 0)
+                device.submit(enc)
+                got = by.read()[off:off + count]
+                bad = int(np.count_nonzero(got != wy))
+                for v in (bx, by, bs, bz):
+                    v.dispose()
+                assert bad == 0, f"range [{lo}, {hi}] count {count}: {bad} bytes differ"

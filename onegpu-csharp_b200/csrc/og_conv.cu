@@ -38,6 +38,8 @@ struct PackArgs {
     int32_t ld;         // bytes per matrix row
     uint32_t ow_magic;  // n / ow = (umulhi(ow_magic, n) + n) >> ow_shift for 0 <= n < 2^31
     int32_t ow_shift;
+    uint32_t cin_g_magic, groups_magic;  // the same for n / cin_g and n / groups (the plane kernel's block index)
+    int32_t cin_g_shift, groups_shift;
 };
 
 // n / d for 0 <= n < 2^31 by multiplication (Granlund and Montgomery, "Division by Invariant Integers using
@@ -103,90 +105,323 @@ __global__ void __launch_bounds__(PACK_THREADS) conv_pack_kernel(const PackArgs 
         *reinterpret_cast<uint32_t*>(dst) = word[0];
 }
 
-constexpr int PLANE_SMEM_MAX = 48 * 1024;  // planes up to this size are staged in shared memory
+constexpr int64_t PLANE_SMEM_MAX = 160 * 1024;  // the plane kernel runs when its shared memory fits this
 
-// One CTA per input plane (image, group, channel c): the plane is read once, with coalesced loads, into shared
-// memory; then the CTA writes the KH * KW rows of the column matrix that plane feeds (rows c * KH * KW ..), BYTES
-// columns per thread and store, every byte gathered from shared memory.
-template <int BYTES>
-__global__ void __launch_bounds__(PACK_THREADS) conv_pack_plane_kernel(const PackArgs a) {
+// Plane kernel: groups of TPP threads (a CTA holds PACK_THREADS / TPP of them, each with its own shared memory)
+// walk input planes (image, group, channel c) in grid-stride order. A group stages its plane in shared memory (4-byte
+// cp.async when every plane starts on a 4-byte boundary), re-lays it as phase rows (below), starts staging its next
+// plane and meanwhile writes the KH * KW rows of the column matrix that the current plane feeds (rows c * KH * KW ..). Small planes get small groups, so the per-plane
+// bookkeeping is not repeated by threads that have little else to do. A group first re-lays its plane as phase rows:
+// for input row iy and phase r < SW, E[iy][r][j] = x[iy][j * SW + r - PW], the zero point where that column lies in
+// the padding. Tap (kh, kw) of output (oy, ox) then reads E[oy * SH + kh * DH - PH][t % SW][ox + t / SW] with
+// t = kw * DW: one output row is a contiguous slice of one phase row, copied 16 bytes per thread with two aligned
+// 16-byte shared loads and funnel shifts, consecutive threads writing consecutive 16 bytes of the matrix row. Chunks
+// that cross an output row, reach past OH * OW or lie in vertical padding go byte by byte.
+struct PlaneLayout {
+    int32_t hw;       // bytes of one input plane
+    int32_t raw_pad;  // bytes of the staging buffer (hw rounded up to 16, plus 16)
+    int32_t e_len;    // L: bytes of one phase row (a multiple of 16, covering every slice plus 32 bytes)
+    int32_t group_bytes;  // shared memory of one group: the staging buffer and H * SW phase rows
+    uint32_t sw_magic;    // t / SW by div_magic
+    int32_t sw_shift;
+    bool async;       // every plane starts 4-byte aligned and spans whole words
+};
+
+template <int TPP>
+__device__ __forceinline__ void group_sync(int32_t group) {
+    if constexpr (TPP == 32)
+        __syncwarp();
+    else
+        asm volatile("bar.sync %0, %1;" ::"r"(group + 1), "r"(TPP) : "memory");
+}
+
+template <int TPP>
+__device__ __forceinline__ void stage_plane(const PackArgs& a, const PlaneLayout& pl, int32_t plane, int32_t lane,
+                                            uint8_t* dst) {
+    const int32_t ig = div_magic(plane, a.cin_g_magic, a.cin_g_shift);
+    const int32_t c = plane - ig * a.cin_g;
+    const int32_t img = div_magic(ig, a.groups_magic, a.groups_shift);
+    const int32_t g = ig - img * a.groups;
+    const uint8_t* src = a.x + (static_cast<int64_t>(img) * a.cin + g * a.cin_g + c) * static_cast<int64_t>(pl.hw);
+    if (pl.async) {
+        const int32_t words = pl.hw >> 2;
+        for (int32_t i = lane; i < words; i += TPP) cp_async4(dst + 4 * i, src + 4 * i);
+    } else {
+        for (int32_t i = lane; i < pl.hw; i += TPP) dst[i] = __ldg(src + i);
+    }
+}
+
+// The 16 bytes of E starting at byte s (any alignment; E + s + 31 rounded down to 16 lies inside E).
+__device__ __forceinline__ uint4 slice16(const uint8_t* __restrict__ e, int32_t s) {
+    const uint4 v0 = *reinterpret_cast<const uint4*>(e + (s & ~15));
+    const uint4 v1 = *reinterpret_cast<const uint4*>(e + (s & ~15) + 16);
+    const uint32_t sh = 8 * (s & 3);
+    uint32_t w0, w1, w2, w3, w4;
+    switch ((s >> 2) & 3) {
+        case 0: w0 = v0.x; w1 = v0.y; w2 = v0.z; w3 = v0.w; w4 = v1.x; break;
+        case 1: w0 = v0.y; w1 = v0.z; w2 = v0.w; w3 = v1.x; w4 = v1.y; break;
+        case 2: w0 = v0.z; w1 = v0.w; w2 = v1.x; w3 = v1.y; w4 = v1.z; break;
+        default: w0 = v0.w; w1 = v1.x; w2 = v1.y; w3 = v1.z; w4 = v1.w; break;
+    }
+    return make_uint4(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh), __funnelshift_r(w2, w3, sh),
+                      __funnelshift_r(w3, w4, sh));
+}
+
+// Four bytes of phase row r at j: x[iy][s + q * SW] for q < 4 with s = j * SW + r - PW, from the staged row `rrow`
+// (padded by 16 readable bytes past the plane); word loads and byte permutes when all four lie inside the row.
+template <int SW>
+__device__ __forceinline__ uint32_t phase_word(const uint8_t* __restrict__ raw, int32_t row0, int32_t s, int32_t w,
+                                               int32_t sw, uint32_t pad) {
+    if (s >= 0 && s + 3 * sw < w) {
+        const int32_t b = row0 + s;
+        if constexpr (SW == 1) {
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(raw + (b & ~3));
+            return __funnelshift_r(wp[0], wp[1], 8 * (b & 3));
+        } else if constexpr (SW == 2) {
+            const uint32_t* wp = reinterpret_cast<const uint32_t*>(raw + (b & ~3));
+            const uint32_t w0 = wp[0], w1 = wp[1], w2 = wp[2];
+            return __byte_perm(__funnelshift_r(w0, w1, 8 * (b & 3)), __funnelshift_r(w1, w2, 8 * (b & 3)), 0x6420);
+        } else {
+            return __byte_perm(__byte_perm(raw[b], raw[b + sw], 0x0040), __byte_perm(raw[b + 2 * sw], raw[b + 3 * sw], 0x0040),
+                               0x5410);
+        }
+    }
+    uint32_t v[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int32_t cq = s + q * sw;
+        v[q] = static_cast<uint32_t>(cq) < static_cast<uint32_t>(w) ? raw[row0 + cq] : pad;
+    }
+    return __byte_perm(__byte_perm(v[0], v[1], 0x0040), __byte_perm(v[2], v[3], 0x0040), 0x5410);
+}
+
+template <int TPP, int SW>
+__global__ void __launch_bounds__(PACK_THREADS) conv_pack_plane_kernel(const PackArgs a, int32_t planes,
+                                                                       PlaneLayout pl) {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ uint8_t plane_s[];
-    const int64_t plane = blockIdx.x;  // (image * groups + g) * cin_g + c
-    const int32_t c = static_cast<int32_t>(plane % a.cin_g);
-    const int64_t ig = plane / a.cin_g;
-    const int64_t img = ig / a.groups;
-    const int32_t g = static_cast<int32_t>(ig - img * a.groups);
-    const int32_t hw = a.h * a.w;
-    const uint8_t* src = a.x + (img * a.cin + g * a.cin_g + c) * static_cast<int64_t>(hw);
-    if ((reinterpret_cast<uintptr_t>(src) & 3) == 0) {
-        const int32_t words = hw >> 2;
-        for (int32_t i = threadIdx.x; i < words; i += PACK_THREADS)
-            reinterpret_cast<uint32_t*>(plane_s)[i] = __ldg(reinterpret_cast<const uint32_t*>(src) + i);
-        for (int32_t i = (words << 2) + threadIdx.x; i < hw; i += PACK_THREADS) plane_s[i] = __ldg(src + i);
-    } else {
-        for (int32_t i = threadIdx.x; i < hw; i += PACK_THREADS) plane_s[i] = __ldg(src + i);
-    }
-    __syncthreads();
+    extern __shared__ __align__(16) uint8_t smem[];
+    constexpr int32_t GROUPS = PACK_THREADS / TPP;
+    const int32_t group = static_cast<int32_t>(threadIdx.x) / TPP;
+    const int32_t lane = static_cast<int32_t>(threadIdx.x) % TPP;
+    uint8_t* const raw = smem + group * pl.group_bytes;  // the staged plane
+    uint8_t* const e = raw + pl.raw_pad;                  // its phase rows, H * SW of them
     const uint32_t pad = a.zp != nullptr ? __ldg(a.zp) : 0u;
-    const int32_t taps = a.kh * a.kw;
     const int32_t ncols = a.oh * a.ow;
-    // A plane's items (taps x units of one matrix row) fit 32-bit arithmetic, which is far cheaper than 64-bit here.
-    const int32_t upr = a.units_per_row;
-    uint8_t* rows0 = a.cols + (ig * a.rows + static_cast<int64_t>(c) * taps) * a.ld;
-    // Taps in the outer loop (uniform, no division per item); the output position of a unit's first column by one
-    // multiply-high (div_magic). Output (oy, ox) reads input row oy * SH + dy, column ox * SW + dx.
-    for (int32_t kk = 0; kk < taps; kk++) {
-        const int32_t kh = kk / a.kw;
-        const int32_t kw = kk - kh * a.kw;
-        const int32_t dy = kh * a.dh - a.ph;
-        const int32_t dx = kw * a.dw - a.pw;
-        uint8_t* row_dst = rows0 + static_cast<int64_t>(kk) * a.ld;
-        for (int32_t u = threadIdx.x; u < upr; u += PACK_THREADS) {
-            const int32_t col0 = u * BYTES;
-            int32_t oy = div_magic(col0, a.ow_magic, a.ow_shift);
-            int32_t ox = col0 - oy * a.ow;
-            int32_t iy = oy * a.sh + dy;
-            int32_t ix = ox * a.sw + dx;
-            uint32_t word[BYTES / 4];
+    const int32_t taps = a.kh * a.kw;
+    const int32_t chunks = a.ld >> 4;
+    const int32_t stride = static_cast<int32_t>(gridDim.x) * GROUPS;
+    const int32_t sw = SW != 0 ? SW : a.sw;
+    int32_t p = static_cast<int32_t>(blockIdx.x) * GROUPS + group;
+    if (p < planes) stage_plane<TPP>(a, pl, p, lane, raw);
+    for (; p < planes; p += stride) {
+        cp_async_wait_all();
+        group_sync<TPP>(group);  // plane p is staged, and the group is done reading E
+        // E, four bytes per thread and step.
+        for (int32_t iy = 0; iy < a.h; iy++) {
+            for (int32_t r = 0; r < sw; r++) {
+                uint32_t* erow = reinterpret_cast<uint32_t*>(e + (iy * sw + r) * pl.e_len);
+                for (int32_t j = 4 * lane; j < pl.e_len; j += 4 * TPP)
+                    erow[j >> 2] = phase_word<SW>(raw, iy * a.w, j * sw + r - a.pw, a.w, sw, pad);
+            }
+        }
+        group_sync<TPP>(group);  // E is complete and the staged plane is free: bring in the next one meanwhile
+        const int32_t next = p + stride;
+        if (next < planes) stage_plane<TPP>(a, pl, next, lane, raw);
+        const int32_t ig = div_magic(p, a.cin_g_magic, a.cin_g_shift);
+        const int32_t c = p - ig * a.cin_g;
+        uint8_t* row_dst = a.cols + (static_cast<int64_t>(ig) * a.rows + static_cast<int64_t>(c) * taps) * a.ld;
+        for (int32_t kh = 0; kh < a.kh; kh++) {
+            const int32_t dy = kh * a.dh - a.ph;
+            for (int32_t kw = 0; kw < a.kw; kw++, row_dst += a.ld) {
+                const int32_t t = kw * a.dw;
+                const int32_t q = div_magic(t, pl.sw_magic, pl.sw_shift);
+                const int32_t rr = t - q * sw;
+                for (int32_t u = lane; u < chunks; u += TPP) {
+                    const int32_t col0 = u * 16;
+                    const int32_t oy = div_magic(col0, a.ow_magic, a.ow_shift);
+                    int32_t ox = col0 - oy * a.ow;
+                    int32_t iy = oy * a.sh + dy;
+                    uint4 out;
+                    if (col0 + 16 <= ncols && ox + 16 <= a.ow && static_cast<uint32_t>(iy) < static_cast<uint32_t>(a.h)) {
+                        out = slice16(e, (iy * sw + rr) * pl.e_len + ox + q);
+                    } else {
+                        uint32_t w[4] = {0, 0, 0, 0};
 #pragma unroll
-            for (int q = 0; q < BYTES / 4; q++) word[q] = 0;
-#pragma unroll
-            for (int e = 0; e < BYTES; e++) {
-                uint32_t v = pad;
-                if (col0 + e < ncols && static_cast<uint32_t>(iy) < static_cast<uint32_t>(a.h) &&
-                    static_cast<uint32_t>(ix) < static_cast<uint32_t>(a.w))
-                    v = plane_s[iy * a.w + ix];
-                word[e >> 2] |= v << (8 * (e & 3));
-                ix += a.sw;
-                if (++ox == a.ow) {
-                    ox = 0;
-                    ix = dx;
-                    iy += a.sh;
+                        for (int k = 0; k < 16; k++) {
+                            uint32_t v = pad;
+                            if (col0 + k < ncols && static_cast<uint32_t>(iy) < static_cast<uint32_t>(a.h))
+                                v = e[(iy * sw + rr) * pl.e_len + ox + q];
+                            w[k >> 2] |= v << (8 * (k & 3));
+                            if (++ox == a.ow) {
+                                ox = 0;
+                                iy += a.sh;
+                            }
+                        }
+                        out = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    *reinterpret_cast<uint4*>(row_dst + col0) = out;
                 }
             }
-            uint8_t* dst = row_dst + col0;
-            if constexpr (BYTES == 16)
-                *reinterpret_cast<uint4*>(dst) = make_uint4(word[0], word[1], word[2], word[3]);
-            else
-                *reinterpret_cast<uint32_t*>(dst) = word[0];
         }
     }
 }
 
-static cudaError_t launch_conv_pack(const PackArgs& a, int64_t planes, cudaStream_t s) {
+// One-dimensional convolutions (H = KH = 1) with width stride SW of 1 or 2 and taps spanning at most 8 input columns
+// ((KW - 1) * DW <= 8): one warp per input row, each lane writing output words (four columns) of the row's KW matrix
+// rows. For a word at ox0, every tap reads inside the input window [SW * ox0 - PW, SW * ox0 + 3 * SW + (KW - 1) * DW
+// - PW]; the lane loads that window once as NW aligned words and forms each tap's word with funnel shifts (and, at
+// stride 2, a byte permute picking every other byte). Words whose window leaves the row, or that reach past OW, go
+// byte by byte with the padding rules. Four words per lane are in flight at once.
+template <int SW>
+struct RowWindow {
+    static constexpr int NW = SW == 1 ? 4 : 5;  // words: an offset below 4 plus at most 8 + 3 * SW + 1 bytes
+};
+
+template <int SW, int I>
+__device__ __forceinline__ uint32_t tap_word_at(const uint32_t (&w)[RowWindow<SW>::NW], uint32_t sh) {
+    if constexpr (SW == 1) {
+        return __funnelshift_r(w[I], w[I + 1], sh);
+    } else {
+        return __byte_perm(__funnelshift_r(w[I], w[I + 1], sh), __funnelshift_r(w[I + 1], w[I + 2], sh), 0x6420);
+    }
+}
+
+// The tap word whose first byte is byte S of the window (S <= 11).
+template <int SW>
+__device__ __forceinline__ uint32_t tap_word(const uint32_t (&w)[RowWindow<SW>::NW], int32_t s) {
+    const uint32_t sh = 8u * static_cast<uint32_t>(s & 3);
+    switch (s >> 2) {
+        case 0: return tap_word_at<SW, 0>(w, sh);
+        case 1: return tap_word_at<SW, 1>(w, sh);
+        default: return tap_word_at<SW, 2>(w, sh);
+    }
+}
+
+template <int SW>
+__global__ void __launch_bounds__(PACK_THREADS) conv_pack_row_kernel(const PackArgs a, int32_t planes) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int NW = RowWindow<SW>::NW;
+    constexpr int U = 4;  // output words per lane in flight
+    const int32_t lane = static_cast<int32_t>(threadIdx.x) & 31;
+    const int32_t warps = static_cast<int32_t>(gridDim.x) * (PACK_THREADS / 32);
+    const uint32_t pad = a.zp != nullptr ? __ldg(a.zp) : 0u;
+    const int32_t words = a.ld >> 2;
+    for (int32_t plane = static_cast<int32_t>((blockIdx.x * PACK_THREADS + threadIdx.x) >> 5); plane < planes;
+         plane += warps) {
+        const int32_t ig = div_magic(plane, a.cin_g_magic, a.cin_g_shift);
+        const int32_t c = plane - ig * a.cin_g;
+        const int32_t img = div_magic(ig, a.groups_magic, a.groups_shift);
+        const int32_t g = ig - img * a.groups;
+        const uint8_t* row = a.x + (static_cast<int64_t>(img) * a.cin + g * a.cin_g + c) * static_cast<int64_t>(a.w);
+        uint8_t* dst0 = a.cols + (static_cast<int64_t>(ig) * a.rows + static_cast<int64_t>(c) * a.kw) * a.ld;
+        // Byte offset of the window's first byte within its aligned word (the same for every word of the row).
+        const int32_t o = static_cast<int32_t>((reinterpret_cast<uintptr_t>(row) - static_cast<uintptr_t>(a.pw)) & 3);
+        for (int32_t t0 = lane; t0 < words; t0 += 32 * U) {
+            uint32_t win[U][NW];
+            bool fast[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int32_t ox0 = 4 * (t0 + 32 * u);
+                const int32_t lo = SW * ox0 - a.pw - o;  // first byte of the window's first word
+                fast[u] = t0 + 32 * u < words && ox0 + 4 <= a.ow && lo >= 0 && lo + 4 * NW <= a.w;
+                if (fast[u]) {
+                    const uint32_t* wp = reinterpret_cast<const uint32_t*>(row + lo);
+#pragma unroll
+                    for (int k = 0; k < NW; k++) win[u][k] = __ldg(wp + k);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int32_t t = t0 + 32 * u;
+                if (t >= words) break;
+                const int32_t ox0 = 4 * t;
+                uint8_t* dst = dst0 + ox0;
+                for (int32_t kw = 0; kw < a.kw; kw++, dst += a.ld) {
+                    uint32_t word;
+                    if (fast[u]) {
+                        word = tap_word<SW>(win[u], kw * a.dw + o);
+                    } else {
+                        word = 0;
+                        const int32_t d = kw * a.dw - a.pw;
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int32_t ix = SW * (ox0 + e) + d;
+                            uint32_t v = pad;
+                            if (ox0 + e < a.ow && static_cast<uint32_t>(ix) < static_cast<uint32_t>(a.w)) v = __ldg(row + ix);
+                            word |= v << (8 * e);
+                        }
+                    }
+                    *reinterpret_cast<uint32_t*>(dst) = word;
+                }
+            }
+        }
+    }
+}
+
+static cudaError_t launch_conv_pack(const PackArgs& a, int64_t planes, int num_sms, cudaStream_t s) {
     const bool wide = a.ld % 16 == 0 && (reinterpret_cast<uintptr_t>(a.cols) & 15) == 0;
-    const int32_t hw = a.h * a.w;
-    if (hw <= PLANE_SMEM_MAX && planes <= 0x7FFFFFFF) {
-        const unsigned grid = static_cast<unsigned>(planes);
-        const size_t smem = static_cast<size_t>((hw + 15) & ~15);
-        // Four columns per thread: adjacent lanes gather from shared memory 4 * stride bytes apart (at most 2-way
-        // bank conflicts at stride 2, none at stride 1), and each warp stores 128 contiguous bytes.
-        PackArgs b = a;
-        b.units_per_row = a.ld / 4;
-        b.units = a.units * (a.ld / 4) / a.units_per_row;
-        return launch_pdl(conv_pack_plane_kernel<4>, dim3(grid), dim3(PACK_THREADS), smem, s, b);
+    const int64_t hw = static_cast<int64_t>(a.h) * a.w;
+    // Phase rows: the longest slice is OW + (KW - 1) * DW / SW bytes; 32 more for the aligned 16-byte loads.
+    const int64_t e_len = ((static_cast<int64_t>(a.ow) + (static_cast<int64_t>(a.kw) - 1) * a.dw / a.sw + 15) & ~15) + 32;
+    const int64_t raw_pad = ((hw + 15) & ~15) + 16;  // 16 readable bytes past the plane for the word gathers
+    const int64_t smem = raw_pad + static_cast<int64_t>(a.h) * a.sw * e_len;
+    if (a.h == 1 && a.kh == 1 && a.oh == 1 && (a.sw == 1 || a.sw == 2) &&
+        (static_cast<int64_t>(a.kw) - 1) * a.dw <= 8 && a.pw <= 8 && planes <= 0x7FFF0000) {
+        const int64_t blocks = (planes + PACK_THREADS / 32 - 1) / (PACK_THREADS / 32);
+        const int64_t cap = 8 * static_cast<int64_t>(num_sms);
+        const unsigned grid = static_cast<unsigned>(blocks < cap ? blocks : cap);
+        const int32_t np = static_cast<int32_t>(planes);
+        return a.sw == 1 ? launch_pdl(conv_pack_row_kernel<1>, dim3(grid), dim3(PACK_THREADS), 0, s, a, np)
+                         : launch_pdl(conv_pack_row_kernel<2>, dim3(grid), dim3(PACK_THREADS), 0, s, a, np);
+    }
+    if (wide && smem <= PLANE_SMEM_MAX && planes <= 0x7FFF0000) {  // grid-stride plane indices stay below 2^31
+        // Threads per plane: about one per 96 bytes of plane, a power of two from 32 to 256.
+        int tpp = 32;
+        while (tpp < PACK_THREADS && static_cast<int64_t>(tpp) * 96 < hw) tpp *= 2;
+        const int groups = PACK_THREADS / tpp;
+        PlaneLayout pl;
+        pl.hw = static_cast<int32_t>(hw);
+        pl.raw_pad = static_cast<int32_t>(raw_pad);
+        pl.e_len = static_cast<int32_t>(e_len);
+        pl.group_bytes = static_cast<int32_t>(smem);
+        magic_for(static_cast<uint32_t>(a.sw), &pl.sw_magic, &pl.sw_shift);
+        pl.async = ((reinterpret_cast<uintptr_t>(a.x) | static_cast<uintptr_t>(hw)) & 3) == 0;
+        // The grid covers the planes once, or fills the SMs with as many CTAs as the shared memory allows.
+        const int64_t cta_smem = smem * groups;
+        if (cta_smem > 200 * 1024) tpp = PACK_THREADS;  // (only reached for planes above 24 KB: one group)
+        const int64_t cta_bytes = tpp == PACK_THREADS ? smem : cta_smem;
+        int per_sm = static_cast<int>((200 * 1024) / cta_bytes);
+        per_sm = per_sm < 1 ? 1 : (per_sm > 8 ? 8 : per_sm);
+        const int g_per_cta = PACK_THREADS / tpp;
+        const int64_t need = (planes + g_per_cta - 1) / g_per_cta;
+        const int64_t resident = static_cast<int64_t>(per_sm) * num_sms;
+        const unsigned grid = static_cast<unsigned>(need < resident ? need : resident);
+        const size_t bytes = static_cast<size_t>(cta_bytes);
+        auto go = [&](auto kernel) -> cudaError_t {
+            if (bytes > 48 * 1024) {
+                const cudaError_t e =
+                    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+                if (e != cudaSuccess) return e;
+            }
+            return launch_pdl(kernel, dim3(grid), dim3(PACK_THREADS), bytes, s, a, static_cast<int32_t>(planes), pl);
+        };
+        const int swc = a.sw == 1 ? 1 : (a.sw == 2 ? 2 : 0);
+        switch (tpp * 4 + swc) {
+            case 32 * 4 + 1: return go(conv_pack_plane_kernel<32, 1>);
+            case 32 * 4 + 2: return go(conv_pack_plane_kernel<32, 2>);
+            case 32 * 4: return go(conv_pack_plane_kernel<32, 0>);
+            case 64 * 4 + 1: return go(conv_pack_plane_kernel<64, 1>);
+            case 64 * 4 + 2: return go(conv_pack_plane_kernel<64, 2>);
+            case 64 * 4: return go(conv_pack_plane_kernel<64, 0>);
+            case 128 * 4 + 1: return go(conv_pack_plane_kernel<128, 1>);
+            case 128 * 4 + 2: return go(conv_pack_plane_kernel<128, 2>);
+            case 128 * 4: return go(conv_pack_plane_kernel<128, 0>);
+            case 256 * 4 + 1: return go(conv_pack_plane_kernel<256, 1>);
+            case 256 * 4 + 2: return go(conv_pack_plane_kernel<256, 2>);
+            default: return go(conv_pack_plane_kernel<256, 0>);
+        }
     }
     const unsigned blocks = static_cast<unsigned>((a.units + PACK_THREADS - 1) / PACK_THREADS);
     return wide ? launch_pdl(conv_pack_kernel<16>, dim3(blocks), dim3(PACK_THREADS), 0, s, a)
@@ -525,8 +760,11 @@ OG_API og_status og_conv_integer_encode(og_conv_integer* cv, og_encoder* enc, co
             a.ph = p.pad_top;
             a.pw = p.pad_left;
             og::magic_for(static_cast<uint32_t>(c.g.ow), &a.ow_magic, &a.ow_shift);
+            og::magic_for(static_cast<uint32_t>(cin_g), &a.cin_g_magic, &a.cin_g_shift);
+            og::magic_for(static_cast<uint32_t>(p.groups), &a.groups_magic, &a.groups_shift);
             const int64_t planes = images * p.groups * cin_g;
-            enc->ops.push_back([=](cudaStream_t s) { return og::launch_conv_pack(a, planes, s); });
+            const int sms = cv->device->sm_count;
+            enc->ops.push_back([=](cudaStream_t s) { return og::launch_conv_pack(a, planes, sms, s); });
             enc->dispatches += 1;
 
             if (p.groups == 1) {

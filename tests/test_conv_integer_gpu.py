@@ -135,3 +135,35 @@ def test_warm_calls_allocate_nothing(device):
         for b in (x, w, y):
             b.dispose()
         conv.dispose()
+
+
+def _geometry(batch, cin, h, w, cout, kh, kw, sh=1, sw=1, dh=1, dw=1, pads=(0, 0, 0, 0), groups=1, offset_x=0):
+    return dict(batch=batch, cin=cin, h=h, w=w, cout=cout, kh=kh, kw=kw, stride_h=sh, stride_w=sw, dilation_h=dh,
+                dilation_w=dw, pad_top=pads[0], pad_left=pads[1], pad_bottom=pads[2], pad_right=pads[3],
+                groups=groups, offset_x=offset_x, offset_w=0, offset_y=0)
+
+
+# The im2col pack's paths: one-dimensional rows, word gathers at width strides 1 and 2, byte gathers at other strides, planes staged
+# asynchronously (every plane on a 4-byte boundary) or byte by byte, planes above 24 KB (two buffers beyond 48 KB of
+# shared memory), more planes than resident CTAs (each CTA walks several), windows cut by padding at both ends.
+PACK_GEOMETRIES = [
+    ("1-D stride 1, wide rows", _geometry(2, 6, 1, 4000, 5, 1, 5, pads=(0, 2, 0, 2))),
+    ("2-D stride 2", _geometry(1, 3, 130, 130, 4, 3, 3, sh=2, sw=2, pads=(1, 1, 1, 1))),
+    ("stride 3, dilation 2, odd width", _geometry(2, 3, 5, 1001, 4, 2, 4, sh=1, sw=3, dh=2, dw=2, pads=(1, 3, 0, 1))),
+    ("40000-byte planes", _geometry(1, 2, 200, 200, 4, 3, 3, sh=2, sw=2, pads=(1, 1, 1, 1))),
+    ("many planes per CTA, grouped", _geometry(4, 700, 12, 12, 8, 3, 3, pads=(1, 1, 1, 1), groups=4)),
+    ("unaligned planes", _geometry(2, 5, 7, 50, 6, 3, 3, pads=(1, 1, 1, 1), offset_x=3)),
+    ("depthwise stride 2", _geometry(2, 16, 33, 34, 16, 3, 3, sh=2, sw=2, pads=(1, 1, 1, 1), groups=16)),
+    # one-dimensional rows (the row kernel): misaligned row starts, dilation, short rows, padding on one side
+    ("1-D stride 2, odd length, offset", _geometry(3, 7, 1, 999, 4, 1, 3, sw=2, pads=(0, 1, 0, 2), offset_x=1)),
+    ("1-D dilation 2, right padding only", _geometry(2, 4, 1, 517, 3, 1, 5, dw=2, pads=(0, 0, 0, 3))),
+    ("1-D short rows", _geometry(4, 3, 1, 13, 2, 1, 3, sw=2, pads=(0, 1, 0, 1))),
+    ("1-D stride 2, dilation 4", _geometry(2, 3, 1, 300, 2, 1, 3, sw=2, dw=4, pads=(0, 4, 0, 4))),
+    ("1-D grouped stride 1", _geometry(2, 12, 1, 801, 6, 1, 3, pads=(0, 1, 0, 1), groups=3)),
+]
+
+
+@pytest.mark.gpu
+def test_pack_layouts_are_bit_exact(device):
+    cases = [dict(name=name, p=p, xs=False, ws=True, xz=1, wz=2, fill=-1, scratch=0) for name, p in PACK_GEOMETRIES]
+    _check(device, cases)

@@ -31,7 +31,9 @@ constexpr int BN = 256;
 constexpr int BK = 128;                    // bytes of K per stage = one 128-byte swizzle row
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = NUM_ACC * BN;    // 512: all of TMEM
-constexpr int THREADS = 192;               // producer, MMA, 4 epilogue warps
+constexpr int EPI_WARPS = 8;               // two per TMEM lane quadrant, each taking half of the tile's columns
+constexpr int EPI_THREADS = 32 * EPI_WARPS;
+constexpr int THREADS = 64 + EPI_THREADS;  // producer, MMA, epilogue warps
 constexpr int GROUP_M = 8;                 // output tiles per raster group along M
 
 // CG = 1: one CTA computes a 128 x 256 tile. CG = 2: a CTA pair computes a 256 x 256 tile with tcgen05.mma
@@ -44,10 +46,11 @@ struct Cfg {
     static constexpr int B_COLS = BN / CG;            // columns of B staged by one CTA
     static constexpr int B_BYTES = B_COLS * BK;       // 32 KB or 16 KB per CTA
     static constexpr int B_BOX = 128 * BK;            // one 128-column box of an MN-major B
-    static constexpr int STAGES = CG == 1 ? 4 : 6;
+    static constexpr int STAGES = CG == 1 ? 4 : 5;
     static constexpr int TERMS_BYTES = 5 * 4 * BN;     // per-column epilogue terms
-    static constexpr int BOX_BYTES = 32 * 64;               // one 32-row x 16-word store box (64-byte rows)
-    static constexpr int STAGING_BYTES = 4 * 2 * BOX_BYTES; // two boxes per epilogue warp
+    static constexpr int BOX_BYTES = 32 * 64;          // one 32-row x 16-word store box (64-byte rows)
+    static constexpr int BOXES = CG == 1 ? 1 : 2;      // store boxes per epilogue warp
+    static constexpr int STAGING_BYTES = EPI_WARPS * BOXES * BOX_BYTES;
     static constexpr int SMEM_BYTES =
         STAGES * (A_BYTES + B_BYTES) + STAGING_BYTES + 1024 /* alignment */ + 256 /* barriers */ + TERMS_BYTES;
 };
@@ -369,7 +372,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         }
         for (int a = 0; a < tc::NUM_ACC; a++) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 4 * CG);  // one arrival per epilogue warp of every CTA of the pair
+            mbar_init(&tempty[a], tc::EPI_WARPS * CG);  // one arrival per epilogue warp of every CTA of the pair
         }
         mbar_init(sk_bar, 1);
         *abort_flag = 0;
@@ -496,8 +499,11 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             }
         }
     } else {
-        // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, i.e. rows 32*(w%4) + lane of this CTA's 128 rows.
+        // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, i.e. rows 32*(w%4) + lane of this CTA's 128 rows; warps
+        // 2-5 take the tile's first 128 columns (chunks 0-3 of 32), warps 6-9 the other 128.
         const int q = warp & 3;
+        const int ew = warp - 2;
+        const int c_first = (ew >> 2) * (tc::BN / 64), c_end = c_first + tc::BN / 64;
         const uint32_t tempty_leader = CG == 2 ? mapa_shared(smem_u32(&tempty[0]), 0) : 0;
         const Epilogue& e = p.epi;
         ColTerms& terms_smem = *reinterpret_cast<ColTerms*>(reinterpret_cast<uint8_t*>(bars) + 256);
@@ -531,7 +537,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                 }
                 epi_go[lt & 1] = ok ? 1 : 0;
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync 1, %0;" ::"n"(tc::EPI_THREADS) : "memory");
             if (!epi_go[lt & 1]) goto done;
             tc_fence_after();
             const int row_in_cta = q * 32 + lane;
@@ -541,14 +547,14 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                 // worker that holds K block 0 (the previous one), then flag them.
                 int32_t* slot = p.sk_part + static_cast<int64_t>(worker * CG + static_cast<int>(rank)) * SK_SLOT_INTS;
 #pragma unroll 1
-                for (int c = 0; c < tc::BN / 32; c++) {
+                for (int c = c_first; c < c_end; c++) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(t_row + c * 32, r);
                     tmem_ld_wait();
                     sk_put(slot, c, row_in_cta, r);
                 }
                 __threadfence();
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                asm volatile("bar.sync 1, %0;" ::"n"(tc::EPI_THREADS) : "memory");
                 if (threadIdx.x == 64) {
                     unsigned int* flag = p.sk_flag + worker * CG + static_cast<int>(rank);
                     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(*sk_gen) : "memory");
@@ -565,8 +571,8 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             }
             const int32_t* sk_in = sk_wait ? reinterpret_cast<const int32_t*>(sA) : nullptr;
             if (terms) {  // every warp has left the previous tile (the barrier above), so its terms are free
-                fill_col_terms(terms_smem, e, b, tn * tc::BN, threadIdx.x - 64, 128);
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                fill_col_terms(terms_smem, e, b, tn * tc::BN, threadIdx.x - 64, tc::EPI_THREADS);
+                asm volatile("bar.sync 1, %0;" ::"n"(tc::EPI_THREADS) : "memory");
             }
             const int m = tm * C::BM + static_cast<int>(rank) * 128 + q * 32 + lane;
             const bool row_ok = m < p.m;
@@ -578,11 +584,11 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             }
             if (tma_store) {
                 // Each 32 x 32 chunk leaves as two TMA stores of 32 x 16 words (64-byte row segments) through this
-                // warp's two boxes in turn, so staging one half never waits for the store just issued; rows past M
-                // and columns past N are clipped by the tensor map.
+                // warp's boxes in turn (with two boxes, staging one half never waits for the store just issued);
+                // rows past M and columns past N are clipped by the tensor map.
                 const int box_row = tm * C::BM + static_cast<int>(rank) * 128 + q * 32;
 #pragma unroll 1
-                for (int c = 0; c < tc::BN / 32; c++) {
+                for (int c = c_first; c < c_end; c++) {
                     const int n0 = tn * tc::BN + c * 32;
                     if (n0 >= p.n || box_row >= p.m) break;  // boxes start inside C
                     uint32_t r[32];
@@ -592,9 +598,9 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
 #pragma unroll
                     for (int h = 0; h < 2; h++) {
                         if (n0 + 16 * h >= p.n) break;
-                        // Alternate boxes: the box about to be written was last stored two boxes ago.
-                        uint8_t* box = staging + (q * 2 + h) * C::BOX_BYTES;
-                        if (lane == 0) bulk_wait_group_read<1>();
+                        // Alternate boxes: the box about to be written was last stored BOXES boxes ago.
+                        uint8_t* box = staging + (ew * C::BOXES + h % C::BOXES) * C::BOX_BYTES;
+                        if (lane == 0) bulk_wait_group_read<C::BOXES - 1>();
                         __syncwarp();
                         stage_half<OUT>(terms_smem, e, terms, za_per_row, za, rt, c * 32 + 16 * h, r + 16 * h, box,
                                         lane);
@@ -608,7 +614,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                 }
             } else {
 #pragma unroll 1
-                for (int c = 0; c < tc::BN / 32; c++) {
+                for (int c = c_first; c < c_end; c++) {
                     const int n0 = tn * tc::BN + c * 32;
                     if (n0 >= p.n) break;
                     uint32_t r[32];

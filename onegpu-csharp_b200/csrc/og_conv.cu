@@ -42,19 +42,6 @@ struct PackArgs {
     int32_t cin_g_shift, groups_shift;
 };
 
-// n / d for 0 <= n < 2^31 by multiplication (Granlund and Montgomery, "Division by Invariant Integers using
-// Multiplication", 1994): magic and shift from magic_for(d).
-__device__ __forceinline__ int32_t div_magic(int32_t n, uint32_t magic, int32_t shift) {
-    return static_cast<int32_t>((__umulhi(magic, static_cast<uint32_t>(n)) + static_cast<uint32_t>(n)) >> shift);
-}
-
-static void magic_for(uint32_t d, uint32_t* magic, int32_t* shift) {
-    int32_t l = 0;
-    while ((uint64_t(1) << l) < d) l++;  // ceil(log2 d)
-    *magic = static_cast<uint32_t>(((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1);
-    *shift = l;
-}
-
 // Unit t covers BYTES consecutive columns of one matrix row: row (c * KH + kh) * KW + kw of matrix (image, group)
 // holds x[image, g * CinG + c, oh * SH - PH + kh * DH, ow * SW - PW + kw * DW] at column oh * OW + ow, or the zero
 // point where that position lies in the padding or the column lies past OH * OW (ConvIntegerPack.hlsl:55-89).
@@ -272,7 +259,7 @@ __global__ void __launch_bounds__(PACK_THREADS) conv_pack_plane_kernel(const Pac
 // rows. For a word at ox0, every tap reads inside the input window [SW * ox0 - PW, SW * ox0 + 3 * SW + (KW - 1) * DW
 // - PW]; the lane loads that window once as NW aligned words and forms each tap's word with funnel shifts (and, at
 // stride 2, a byte permute picking every other byte). Words whose window leaves the row, or that reach past OW, go
-// byte by byte with the padding rules. Four words per lane are in flight at once.
+// byte by byte with the padding rules. Two or four words per lane are in flight at once.
 template <int SW>
 struct RowWindow {
     static constexpr int NW = SW == 1 ? 4 : 5;  // words: an offset below 4 plus at most 8 + 3 * SW + 1 bytes
@@ -298,16 +285,81 @@ __device__ __forceinline__ uint32_t tap_word(const uint32_t (&w)[RowWindow<SW>::
     }
 }
 
-template <int SW>
-__global__ void __launch_bounds__(PACK_THREADS) conv_pack_row_kernel(const PackArgs a, int32_t planes) {
+// The KW tap words of one output word from its window, every position and shift a constant: taps of unit
+// dilation, window offset O (KW > 0 only).
+template <int SW, int O, int KW, int K = 0>
+struct RowTaps {
+    __device__ static __forceinline__ void store(const uint32_t (&w)[RowWindow<SW>::NW], uint8_t* dst, int32_t ld) {
+        if constexpr (K < KW) {
+            constexpr int S = K + O;
+            *reinterpret_cast<uint32_t*>(dst) = tap_word_at<SW, (S >> 2)>(w, 8u * (S & 3));
+            RowTaps<SW, O, KW, K + 1>::store(w, dst + ld, ld);
+        }
+    }
+};
+
+// One input row's output words. KW = 0: any tap count and dilation (tap positions found at run time); KW > 0: that
+// many taps of unit dilation with the window offset O fixed.
+template <int SW, int KW, int O>
+__device__ __forceinline__ void row_words(const PackArgs& a, const uint8_t* row, uint8_t* dst0, int32_t o,
+                                          int32_t lane, uint32_t pad) {
+    constexpr int NW = RowWindow<SW>::NW;
+    constexpr int U = KW > 0 ? 2 : 4;  // output words per lane in flight
+    const int32_t words = a.ld >> 2;
+    for (int32_t t0 = lane; t0 < words; t0 += 32 * U) {
+        uint32_t win[U][NW];
+        bool fast[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int32_t ox0 = 4 * (t0 + 32 * u);
+            const int32_t lo = SW * ox0 - a.pw - o;  // first byte of the window's first word
+            fast[u] = t0 + 32 * u < words && ox0 + 4 <= a.ow && lo >= 0 && lo + 4 * NW <= a.w;
+            if (fast[u]) {
+                const uint32_t* wp = reinterpret_cast<const uint32_t*>(row + lo);
+#pragma unroll
+                for (int k = 0; k < NW; k++) win[u][k] = __ldg(wp + k);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int32_t t = t0 + 32 * u;
+            if (t >= words) break;
+            const int32_t ox0 = 4 * t;
+            uint8_t* dst = dst0 + ox0;
+            if constexpr (KW > 0) {
+                if (fast[u]) {
+                    RowTaps<SW, O, KW>::store(win[u], dst, a.ld);
+                    continue;
+                }
+            }
+            for (int32_t kw = 0; kw < a.kw; kw++, dst += a.ld) {
+                uint32_t word;
+                if (KW == 0 && fast[u]) {
+                    word = tap_word<SW>(win[u], kw * a.dw + o);
+                } else {
+                    word = 0;
+                    const int32_t d = kw * a.dw - a.pw;
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int32_t ix = SW * (ox0 + e) + d;
+                        uint32_t v = pad;
+                        if (ox0 + e < a.ow && static_cast<uint32_t>(ix) < static_cast<uint32_t>(a.w)) v = __ldg(row + ix);
+                        word |= v << (8 * e);
+                    }
+                }
+                *reinterpret_cast<uint32_t*>(dst) = word;
+            }
+        }
+    }
+}
+
+template <int SW, int KW>
+__global__ void __launch_bounds__(PACK_THREADS, 4) conv_pack_row_kernel(const PackArgs a, int32_t planes) {
     pdl_trigger();
     pdl_wait();
-    constexpr int NW = RowWindow<SW>::NW;
-    constexpr int U = 4;  // output words per lane in flight
     const int32_t lane = static_cast<int32_t>(threadIdx.x) & 31;
     const int32_t warps = static_cast<int32_t>(gridDim.x) * (PACK_THREADS / 32);
     const uint32_t pad = a.zp != nullptr ? __ldg(a.zp) : 0u;
-    const int32_t words = a.ld >> 2;
     for (int32_t plane = static_cast<int32_t>((blockIdx.x * PACK_THREADS + threadIdx.x) >> 5); plane < planes;
          plane += warps) {
         const int32_t ig = div_magic(plane, a.cin_g_magic, a.cin_g_shift);
@@ -318,43 +370,14 @@ __global__ void __launch_bounds__(PACK_THREADS) conv_pack_row_kernel(const PackA
         uint8_t* dst0 = a.cols + (static_cast<int64_t>(ig) * a.rows + static_cast<int64_t>(c) * a.kw) * a.ld;
         // Byte offset of the window's first byte within its aligned word (the same for every word of the row).
         const int32_t o = static_cast<int32_t>((reinterpret_cast<uintptr_t>(row) - static_cast<uintptr_t>(a.pw)) & 3);
-        for (int32_t t0 = lane; t0 < words; t0 += 32 * U) {
-            uint32_t win[U][NW];
-            bool fast[U];
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int32_t ox0 = 4 * (t0 + 32 * u);
-                const int32_t lo = SW * ox0 - a.pw - o;  // first byte of the window's first word
-                fast[u] = t0 + 32 * u < words && ox0 + 4 <= a.ow && lo >= 0 && lo + 4 * NW <= a.w;
-                if (fast[u]) {
-                    const uint32_t* wp = reinterpret_cast<const uint32_t*>(row + lo);
-#pragma unroll
-                    for (int k = 0; k < NW; k++) win[u][k] = __ldg(wp + k);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const int32_t t = t0 + 32 * u;
-                if (t >= words) break;
-                const int32_t ox0 = 4 * t;
-                uint8_t* dst = dst0 + ox0;
-                for (int32_t kw = 0; kw < a.kw; kw++, dst += a.ld) {
-                    uint32_t word;
-                    if (fast[u]) {
-                        word = tap_word<SW>(win[u], kw * a.dw + o);
-                    } else {
-                        word = 0;
-                        const int32_t d = kw * a.dw - a.pw;
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const int32_t ix = SW * (ox0 + e) + d;
-                            uint32_t v = pad;
-                            if (ox0 + e < a.ow && static_cast<uint32_t>(ix) < static_cast<uint32_t>(a.w)) v = __ldg(row + ix);
-                            word |= v << (8 * e);
-                        }
-                    }
-                    *reinterpret_cast<uint32_t*>(dst) = word;
-                }
+        if constexpr (KW == 0) {
+            row_words<SW, 0, 0>(a, row, dst0, o, lane, pad);
+        } else {
+            switch (o) {
+                case 0: row_words<SW, KW, 0>(a, row, dst0, o, lane, pad); break;
+                case 1: row_words<SW, KW, 1>(a, row, dst0, o, lane, pad); break;
+                case 2: row_words<SW, KW, 2>(a, row, dst0, o, lane, pad); break;
+                default: row_words<SW, KW, 3>(a, row, dst0, o, lane, pad); break;
             }
         }
     }
@@ -373,8 +396,11 @@ static cudaError_t launch_conv_pack(const PackArgs& a, int64_t planes, int num_s
         const int64_t cap = 8 * static_cast<int64_t>(num_sms);
         const unsigned grid = static_cast<unsigned>(blocks < cap ? blocks : cap);
         const int32_t np = static_cast<int32_t>(planes);
-        return a.sw == 1 ? launch_pdl(conv_pack_row_kernel<1>, dim3(grid), dim3(PACK_THREADS), 0, s, a, np)
-                         : launch_pdl(conv_pack_row_kernel<2>, dim3(grid), dim3(PACK_THREADS), 0, s, a, np);
+        if (a.kw == 3 && a.dw == 1)  // the common three-tap kernel: every tap position a constant
+            return a.sw == 1 ? launch_pdl(conv_pack_row_kernel<1, 3>, dim3(grid), dim3(PACK_THREADS), 0, s, a, np)
+                             : launch_pdl(conv_pack_row_kernel<2, 3>, dim3(grid), dim3(PACK_THREADS), 0, s, a, np);
+        return a.sw == 1 ? launch_pdl(conv_pack_row_kernel<1, 0>, dim3(grid), dim3(PACK_THREADS), 0, s, a, np)
+                         : launch_pdl(conv_pack_row_kernel<2, 0>, dim3(grid), dim3(PACK_THREADS), 0, s, a, np);
     }
     if (wide && smem <= PLANE_SMEM_MAX && planes <= 0x7FFF0000) {  // grid-stride plane indices stay below 2^31
         // Threads per plane: about one per 96 bytes of plane, a power of two from 32 to 256.

@@ -65,6 +65,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     }
 }
 
+// n / d for 0 <= n < 2^31 by multiplication (Granlund and Montgomery, "Division by Invariant Integers using
+// Multiplication", 1994): magic and shift from magic_for(d).
+__device__ __forceinline__ int32_t div_magic(int32_t n, uint32_t magic, int32_t shift) {
+    return static_cast<int32_t>((__umulhi(magic, static_cast<uint32_t>(n)) + static_cast<uint32_t>(n)) >> shift);
+}
+
+inline void magic_for(uint32_t d, uint32_t* magic, int32_t* shift) {
+    int32_t l = 0;
+    while ((uint64_t(1) << l) < d) l++;  // ceil(log2 d)
+    *magic = static_cast<uint32_t>(((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1);
+    *shift = l;
+}
+
 // 4-byte asynchronous copy global -> shared (both addresses 4-byte aligned), and waiting for all of this thread's.
 __device__ __forceinline__ void cp_async4(void* smem_dst, const void* src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(src) : "memory");

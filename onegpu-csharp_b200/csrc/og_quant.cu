@@ -37,7 +37,16 @@ struct QuantArgs {
     int64_t head;         // elements handled one by one before the first whole vector
     int64_t vectors;      // whole vectors of E elements after the head
     int64_t threads;      // threads the launch needs
+    uint32_t inner_magic, axis_magic;  // j / inner and q / axis_len by div_magic
+    int32_t inner_shift, axis_shift;
+    int vec_params;       // DequantizeLinear: every vector's E parameters are consecutive and aligned (inner = 1)
 };
+
+// Fills in the division constants of a's inner and axis_len.
+static void set_param_magics(QuantArgs& a) {
+    magic_for(a.inner, &a.inner_magic, &a.inner_shift);
+    magic_for(a.axis_len, &a.axis_magic, &a.axis_shift);
+}
 
 // The parameter (scale / zero point) index of element j and its position inside the current run of `inner` elements;
 // param_next steps both to element j + 1 without a division.
@@ -47,8 +56,10 @@ struct ParamCursor {
 
 __device__ __forceinline__ ParamCursor param_at(const QuantArgs& a, int64_t j) {
     if (!a.per_axis) return {0u, 0u};
-    const uint32_t q = static_cast<uint32_t>(j) / a.inner;  // counts stay below 2^31
-    return {q % a.axis_len, static_cast<uint32_t>(j) - q * a.inner};
+    const int32_t jj = static_cast<int32_t>(j);  // counts stay below 2^31
+    const int32_t q = div_magic(jj, a.inner_magic, a.inner_shift);
+    const int32_t pi = q - div_magic(q, a.axis_magic, a.axis_shift) * static_cast<int32_t>(a.axis_len);
+    return {static_cast<uint32_t>(pi), static_cast<uint32_t>(jj - q * static_cast<int32_t>(a.inner))};
 }
 
 __device__ __forceinline__ void param_next(const QuantArgs& a, ParamCursor& c) {
@@ -64,6 +75,12 @@ __device__ __forceinline__ int32_t load_q(const void* p, int64_t i) {
     if constexpr (KIND == 0) return static_cast<int32_t>(__ldg(static_cast<const uint8_t*>(p) + i));
     else if constexpr (KIND == 1) return static_cast<int32_t>(static_cast<int8_t>(__ldg(static_cast<const uint8_t*>(p) + i)));
     else return __ldg(static_cast<const int32_t*>(p) + i);
+}
+
+// float(d) for |d| < 2^22, exactly as __int2float_rn(d): d added to the bits of 1.5 * 2^23 (whose unit in the last
+// place is 1) gives 1.5 * 2^23 + d, and subtracting 1.5 * 2^23 is exact.
+__device__ __forceinline__ float small_int_to_float(int32_t d) {
+    return __fsub_rn(__int_as_float(d + 0x4B400000), 12582912.0f);
 }
 
 template <int KIND>
@@ -150,6 +167,45 @@ __device__ __forceinline__ void dq_load(const QuantArgs& a, int64_t first, int32
     }
 }
 
+// The scales and zero points of E elements from parameter pi: E consecutive ones (vector loads; pi is a multiple of
+// E and the parameter arrays are aligned) or pi's for all.
+template <int KIND, int E>
+__device__ __forceinline__ void dq_params(const QuantArgs& a, uint32_t pi, bool consecutive, float (&s)[E],
+                                          int32_t (&z)[E]) {
+    if (consecutive) {
+#pragma unroll
+        for (int h = 0; h < E / 4; h++) {
+            const float4 sv = __ldg(reinterpret_cast<const float4*>(a.scale + pi) + h);
+            s[4 * h] = sv.x;
+            s[4 * h + 1] = sv.y;
+            s[4 * h + 2] = sv.z;
+            s[4 * h + 3] = sv.w;
+        }
+        if (a.zp != nullptr) {
+#pragma unroll
+            for (int h = 0; h < E / 4; h++) {
+                const uint32_t w = __ldg(reinterpret_cast<const unsigned int*>(static_cast<const uint8_t*>(a.zp) + pi) + h);
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const uint32_t b = (w >> (8 * e)) & 0xFFu;
+                    z[4 * h + e] = KIND == 1 ? static_cast<int32_t>(static_cast<int8_t>(b)) : static_cast<int32_t>(b);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int e = 0; e < E; e++) z[e] = 0;
+        }
+    } else {
+        const float s0 = __ldg(a.scale + pi);
+        const int32_t z0 = a.zp != nullptr ? load_q<KIND>(a.zp, pi) : 0;
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            s[e] = s0;
+            z[e] = z0;
+        }
+    }
+}
+
 template <int KIND, bool HALF>
 __device__ __forceinline__ void dq_store(const QuantArgs& a, int64_t first, const float (&v)[DqShape<KIND, HALF>::E]) {
     constexpr int E = DqShape<KIND, HALF>::E;
@@ -199,10 +255,20 @@ __global__ void __launch_bounds__(QTHREADS) dequantize_kernel(const QuantArgs a)
             const int64_t first = a.head + vi * E;
             ParamCursor c = param_at(a, first);
             float v[E];
+            if (KIND != 2 && (a.vec_params || !a.per_axis || c.r + E <= a.inner)) {
+                // Byte inputs with the vector's parameters in one or E consecutive places: loaded once, d = q - zp
+                // is at most 255 in size (converted exactly without the conversion unit).
+                float s[E];
+                int32_t z[E];
+                dq_params<KIND, E>(a, c.pi, a.vec_params != 0, s, z);
 #pragma unroll
-            for (int e = 0; e < E; e++) {
-                v[e] = dequantize_one<KIND>(a, q[u][e], c);
-                param_next(a, c);
+                for (int e = 0; e < E; e++) v[e] = __fmul_rn(small_int_to_float(q[u][e] - z[e]), s[e]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < E; e++) {
+                    v[e] = dequantize_one<KIND>(a, q[u][e], c);
+                    param_next(a, c);
+                }
             }
             dq_store<KIND, HALF>(a, first, v);
         }
@@ -305,6 +371,12 @@ static cudaError_t launch_dequantize(QuantArgs a, int kind, bool half, cudaStrea
     const int in_es = kind == 2 ? 4 : 1, out_es = half ? 2 : 4;
     const int e = (kind != 2 && half) ? 8 : 4;
     split_vectors(a, e, in_es, out_es, e * in_es, e * out_es);
+    set_param_magics(a);
+    // Parameters along the contiguous axis: vector v's E parameters start at (head + v E) % axis_len, a multiple of E
+    // when head and axis_len are, and load as whole vectors when the arrays are aligned for them.
+    a.vec_params = kind != 2 && a.per_axis && a.inner == 1 && a.axis_len % e == 0 && a.head % e == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.scale) & 15) == 0 &&
+                   (a.zp == nullptr || (reinterpret_cast<uintptr_t>(a.zp) & 3) == 0);
     const unsigned blocks = grid_of(a);
     switch (kind * 2 + (half ? 1 : 0)) {
         case 0: return launch_pdl(dequantize_kernel<0, false>, dim3(blocks), dim3(QTHREADS), 0, s, a);
@@ -336,6 +408,7 @@ cudaError_t launch_quantize_u8_tensor(const float* x, int64_t count, uint8_t* y,
 
 static cudaError_t launch_quantize(QuantArgs a, bool is_signed, bool half, cudaStream_t s) {
     split_vectors(a, 16, half ? 2 : 4, 1, 16, 16);
+    set_param_magics(a);
     const int64_t scalar = a.count - a.vectors * 16;
     a.threads = a.vectors > scalar ? a.vectors : scalar;  // one vector per thread
     const unsigned blocks = grid_of(a);

@@ -185,3 +185,39 @@ def test_quantize_near_ties(device):
                     assert np.array_equal(got, want), f"scale {scale} signed {signed} per_axis {per_axis}"
     finally:
         k.dispose()
+
+
+@pytest.mark.gpu
+def test_dequantize_parameters_along_the_contiguous_axis(device):
+    """Per-axis parameters on the last axis with aligned buffers, where each vector's scales and zero points are
+    consecutive and load as whole vectors; sizes with and without whole vectors, both byte kinds, both outputs."""
+    k = og.DequantizeKernels(device)
+    rng = np.random.default_rng(21)
+    try:
+        for shape in ([3, 64], [5, 1000], [2, 3, 1024], [7, 8], [4, 12]):
+            axis = len(shape) - 1
+            count, axis_len, _ = axis_params(shape, axis, True)
+            for kind in ("u8", "s8"):
+                for half in (False, True):
+                    for with_zero in (True, False):
+                        for off_x, off_o in ((0, 0), (4, 8), (3, 0)):
+                            x = quantized(kind, count + off_x + 4, int(rng.integers(1 << 30)))
+                            scale = rng.uniform(0.001, 2.0, size=axis_len).astype(np.float32)
+                            zeros = quantized(kind, axis_len + 4, int(rng.integers(1 << 30)))
+                            out_len = count + off_o + 8
+                            bx, bs = device.create_buffer(NP[kind], x), device.create_buffer(np.float32, scale)
+                            bz = device.create_buffer(NP[kind], zeros)
+                            bo = device.create_buffer(np.float16 if half else np.float32, out_len)
+                            enc = device.begin_commands()
+                            k.encode(enc, bx, off_x, shape, axis, True, bs, 0, bz if with_zero else None, 0, bo, off_o)
+                            device.submit(enc)
+                            got = bo.read()[off_o:off_o + count]
+                            for b in (bx, bs, bz, bo):
+                                b.dispose()
+                            want = oracle.dequantize(x[off_x:], shape, axis, True, scale,
+                                                     zeros[:axis_len] if with_zero else None, half)
+                            bits = np.uint16 if half else np.uint32
+                            assert np.array_equal(got.view(bits), want.view(bits)), \
+                                f"{shape} {kind} half={half} zero={with_zero} offsets {off_x}, {off_o}"
+    finally:
+        k.dispose()

@@ -157,6 +157,11 @@ struct og_int8_gemm {
     int64_t scratch_elements = 0;
     void* sk_buf = nullptr;      // stream-K hand-over buffer of the tensor-core product, allocated on first need
     int64_t sk_bytes = 0;
+    // Partials and tickets of the evenly split few-rows product (the latest pair; older ones live until destroy)
+    std::vector<void*> rows_bufs;
+    int32_t* rows_part = nullptr;
+    unsigned int* rows_ticket = nullptr;
+    int64_t rows_part_ints = 0, rows_ticket_count = 0;
 };
 
 struct og_dynamic_quantize {
@@ -458,6 +463,28 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
         return;
     }
     if (g->tile == 0 && og::rows_eligible(L)) {
+        const int workers = og::rows_workers(L);
+        if (workers > 0) {
+            // Partials and tickets of the even split, owned by the instance (tickets start at zero and every launch
+            // leaves them there); recorded launches of one instance run in stream order, so they share them.
+            const int64_t part = og::rows_part_ints(L, workers), tickets = og::rows_tickets(L);
+            if (g->rows_part_ints < part || g->rows_ticket_count < tickets) {
+                void* pp = nullptr;
+                void* tp = nullptr;
+                check_cuda(cudaMalloc(&pp, static_cast<size_t>(part) * sizeof(int32_t)), "Int8Gemm split partials");
+                g->rows_bufs.push_back(pp);
+                check_cuda(cudaMalloc(&tp, static_cast<size_t>(tickets) * sizeof(unsigned int)), "Int8Gemm tickets");
+                g->rows_bufs.push_back(tp);
+                check_cuda(cudaMemset(tp, 0, static_cast<size_t>(tickets) * sizeof(unsigned int)), "Int8Gemm tickets");
+                g->rows_part = static_cast<int32_t*>(pp);
+                g->rows_ticket = static_cast<unsigned int*>(tp);
+                g->rows_part_ints = part;
+                g->rows_ticket_count = tickets;
+            }
+            L.rows_part = g->rows_part;
+            L.rows_ticket = g->rows_ticket;
+            L.rows_workers = workers;
+        }
         cudaError_t err;
         og::LaunchFn fn = og::prepare_gemm_rows(L, &err);  // tensor maps built now, at record time
         check_cuda(err, "Int8Gemm tensor maps");
@@ -938,6 +965,7 @@ OG_API og_status og_int8_gemm_destroy(og_int8_gemm* g) {
         use(g->device);
         cudaStreamSynchronize(g->device->stream);
         for (void* p : g->scratch) cudaFree(p);
+        for (void* p : g->rows_bufs) cudaFree(p);
         if (g->sk_buf != nullptr) cudaFree(g->sk_buf);
         delete g;
     });

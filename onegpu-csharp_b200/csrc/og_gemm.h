@@ -31,6 +31,12 @@ struct GemmLaunch {
     int32_t* sk_part = nullptr;
     unsigned int* sk_flag = nullptr;
     int64_t sk_bytes = 0;
+    // The few-rows kernel with its (column tile, K block) units split evenly across rows_workers persistent CTAs:
+    // partial segments meet through rows_part (rows_part_ints) and one ticket per (batch, column tile) in rows_ticket
+    // (rows_tickets, zero between launches). Null: one CTA per column tile.
+    int32_t* rows_part = nullptr;
+    unsigned int* rows_ticket = nullptr;
+    int rows_workers = 0;
 };
 
 // Bytes of the stream-K hand-over buffer for a device with num_sms SMs, and the split of one such buffer.
@@ -78,6 +84,11 @@ cudaError_t launch_gemm_tc(const GemmLaunch& L, cudaStream_t stream);
 // sums of B from the same MMA, so it needs no byte-sum pass and no scratch.
 bool rows_eligible(const GemmLaunch& L);
 LaunchFn prepare_gemm_rows(const GemmLaunch& L, cudaError_t* err);
+// Persistent workers that spread the few-rows product evenly over the SMs (0: one CTA per column tile serves), and
+// the int32 partials and tickets such a launch of L needs.
+int rows_workers(const GemmLaunch& L);
+int64_t rows_part_ints(const GemmLaunch& L, int workers);
+int64_t rows_tickets(const GemmLaunch& L);
 cudaError_t launch_gemm_rows(const GemmLaunch& L, cudaStream_t stream);
 
 // A 3-D byte tensor map (x innermost) with 128-byte swizzled box_x x box_y boxes (og_gemm_tc.cu).

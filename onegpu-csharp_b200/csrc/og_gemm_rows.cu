@@ -7,10 +7,12 @@
 // B (235 MB at the decode config) is made for them.
 //
 // One CTA per 128 columns (and batch), the whole of K per CTA, 6 stages of 16 KB of B + 2 KB of A; two CTAs fit on
-// an SM, so every tile of the decode config (224) is resident at once and each pulls its share of HBM bandwidth
-// until all finish together. Warp 0 loads (TMA, no multicast), warp 1 issues the MMAs into a 32-column TMEM
-// accumulator, warps 2-5 compute the row sums of A while B streams (the zero point of B needs them), then drain TMEM:
-// lane = column, 16 results per lane, stores coalesced along N.
+// an SM, so every tile of the decode config (224) is resident at once, all CTAs walking K together (so the rows of B
+// they read at any moment are the same few DRAM pages). There 76 SMs hold two tiles and 72 one, which sets the time.
+// Warp 0 loads (TMA, no multicast), warp 1 issues the MMAs into a 32-column TMEM accumulator, warps 2-5 compute the
+// row sums of A while B streams (the zero point of B needs them), then drain TMEM: lane = column, 16 results per
+// lane, stores coalesced along N. Products with too few column tiles to occupy the SMs split K evenly instead
+// (int8_gemm_rows_stream_kernel below).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -49,7 +51,15 @@ struct RowsParams {
     int64_t sums_stride;
     int64_t sums_split_stride;  // between the partial sums of consecutive K splits (blockIdx.z)
     int k_blocks_total;         // K blocks of the whole product; p.k_blocks is the share of one split
+    // Stream mode (int8_gemm_rows_stream_kernel): the (column tile, K block) units of all batches, split evenly.
+    int64_t units;
+    int tiles;                  // column tiles of one batch
+    int32_t* split_part;        // [workers][2][PART_INTS]: a worker's first and last segments, when partial
+    unsigned int* split_ticket; // [batch * tiles]: K blocks of the tile finished so far (back to 0 when complete)
 };
+
+// One partial record: the 16 x 128 dot products, the 128 column sums of B, the 16 row sums of A of a K range.
+constexpr int PART_INTS = 17 * rows::BN + rows::MAXM;
 
 template <int OUT>
 __device__ __forceinline__ void store_one(const Epilogue& e, int b, int m, int n, uint32_t s) {
@@ -245,6 +255,265 @@ done:
     if (threadIdx.x == 0 && *abort_flag) atomicExch(p.error_flag, 1);
 }
 
+// ---- few rows, K split evenly across the SMs ------------------------------------------------------------------------
+//
+// When there are too few column tiles to occupy the SMs (N of a few thousand), persistent workers (two per SM) take
+// equal contiguous ranges of the (column tile, K block) units, stream-K style.
+// A worker's range covers whole tiles and at most two partial ones (its first and last segments). A whole tile is
+// finished directly; a partial segment leaves its sums (dot products, column sums of B, row sums of A over its K
+// range) in the worker's record and adds its K blocks to the tile's ticket: the worker completing the tile's K
+// blocks adds the other segments' records and finishes the tile. Nothing waits on another CTA. Two TMEM
+// accumulators let a worker's next segment start while its last one is read out.
+
+// The worker whose range holds unit u (ranges [floor(U i / W), floor(U (i + 1) / W))).
+__device__ __forceinline__ int rows_owner(int64_t u, int64_t units, int workers) {
+    return static_cast<int>(((u + 1) * workers - 1) / units);
+}
+
+template <bool B_KMAJOR, int OUT>
+__global__ void __launch_bounds__(rows::THREADS, 2)
+    int8_gemm_rows_stream_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                                 const RowsParams p, uint32_t idesc) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sB = smem;                                   // [STAGES][128 columns x 128 k]
+    uint8_t* sX = smem + rows::STAGES * rows::B_BYTES;    // [STAGES][16 rows of A x 128 k]
+    uint8_t* sOnes = sX + rows::STAGES * rows::A_BYTES;   // [16 rows x 128 k] of ones
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + rows::ONES_BYTES);
+    uint64_t* full = bars;
+    uint64_t* empty = bars + rows::STAGES;
+    uint64_t* tfull = bars + 2 * rows::STAGES;       // [2]
+    uint64_t* tempty = bars + 2 * rows::STAGES + 2;  // [2]
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * rows::STAGES + 4);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    volatile int* go = reinterpret_cast<volatile int*>(tmem_holder + 2);  // [2]: a segment's wait outcome, its ticket
+    int32_t* row_sum = reinterpret_cast<int32_t*>(tmem_holder + 4);        // [16]
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int worker = blockIdx.x;
+    const int workers = gridDim.x;
+    const int kbt = p.k_blocks_total;
+    const int64_t u0 = p.units * worker / workers;
+    const int64_t u1 = p.units * (worker + 1) / workers;
+    const bool need_col_sums = p.epi.za != nullptr;  // za * colsum(B)
+    pdl_trigger();
+
+    for (int i = threadIdx.x; i < rows::ONES_BYTES / 16; i += blockDim.x)
+        reinterpret_cast<uint4*>(sOnes)[i] = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> visible to the tensor cores
+    if (threadIdx.x == 0) {
+        for (int st = 0; st < rows::STAGES; st++) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], 1);
+        }
+        for (int a = 0; a < 2; a++) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 4);  // the four epilogue warps
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_b);
+    }
+    pdl_wait();  // the preceding grid is done: its outputs are readable and its TMEM is free
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, 2 * rows::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    if (warp == 0) {
+        for (int64_t u = u0; u < u1; u++) {
+            const int it = static_cast<int>(u - u0);
+            const int st = it % rows::STAGES;
+            const uint32_t ph = (it / rows::STAGES) & 1;
+            const int t = static_cast<int>(u / kbt);
+            const int kc = static_cast<int>(u - static_cast<int64_t>(t) * kbt) * rows::BK;
+            const int tile = t % p.tiles, b = t / p.tiles;
+            const int ba = p.a_batched ? b : 0, bb = p.b_batched ? b : 0;
+            if (!mbar_wait(&empty[st], ph ^ 1, abort_flag)) break;
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&full[st], rows::B_BYTES + rows::A_BYTES);
+                if constexpr (B_KMAJOR)
+                    tma_load_3d(sB + st * rows::B_BYTES, &tmap_b, &full[st], kc, tile * rows::BN, bb);
+                else
+                    tma_load_3d(sB + st * rows::B_BYTES, &tmap_b, &full[st], tile * rows::BN, kc, bb);
+                tma_load_3d(sX + st * rows::A_BYTES, &tmap_a, &full[st], kc, 0, ba);
+            }
+            __syncwarp();
+        }
+    } else if (warp == 1) {
+        int seg = 0;
+        for (int64_t u = u0; u < u1; u++) {
+            const int it = static_cast<int>(u - u0);
+            const int st = it % rows::STAGES;
+            const uint32_t ph = (it / rows::STAGES) & 1;
+            const int kb = static_cast<int>(u % kbt);
+            const bool first = u == u0 || kb == 0;
+            const bool last = u == u1 - 1 || kb == kbt - 1;
+            const int acc = seg & 1;
+            if (first && !mbar_wait(&tempty[acc], ((seg >> 1) & 1) ^ 1, abort_flag)) break;
+            if (!mbar_wait(&full[st], ph, abort_flag)) break;
+            tc_fence_after();
+            if (lane == 0) {
+                const uint32_t b_addr = smem_u32(sB + st * rows::B_BYTES);
+                const uint32_t x_addr = smem_u32(sX + st * rows::A_BYTES);
+                const uint32_t o_addr = smem_u32(sOnes);
+                const uint32_t d = tmem_base + acc * rows::TMEM_COLS;
+#pragma unroll
+                for (int kk = 0; kk < rows::BK / 32; kk++) {
+                    const uint64_t adesc = B_KMAJOR ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
+                                                    : smem_desc_sw128(b_addr + kk * 32 * 128, rows::B_BYTES, 1024);
+                    const uint32_t accum = (first && kk == 0) ? 0u : 1u;
+                    mma_i8(d, adesc, smem_desc_sw128(x_addr + kk * 32, 16, 1024), idesc, accum);
+                    if (need_col_sums)
+                        mma_i8(d + rows::MAXM, adesc, smem_desc_sw128(o_addr + kk * 32, 16, 1024), idesc, accum);
+                }
+                mma_commit(&empty[st]);
+                if (last) mma_commit(&tfull[acc]);
+            }
+            __syncwarp();
+            seg += last ? 1 : 0;
+        }
+    } else {
+        const int t128 = threadIdx.x - 64;
+        const int col = (warp & 3) * 32 + lane;  // this thread's TMEM lane: column of the tile
+        const Epilogue& e = p.epi;
+        int seg = 0;
+        for (int64_t u = u0; u < u1;) {
+            const int t = static_cast<int>(u / kbt);
+            const int kb0 = static_cast<int>(u - static_cast<int64_t>(t) * kbt);
+            const int kb1 = static_cast<int>(kb0 + (u1 - u) < kbt ? kb0 + (u1 - u) : kbt);
+            const int tile = t % p.tiles, b = t / p.tiles;
+            const int ba = p.a_batched ? b : 0;
+            const int acc = seg & 1;
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the previous segment is done with row_sum and go
+            if (e.zb != nullptr) {
+                // Row sums of A over this segment's K range, while its MMAs run: eight threads per row.
+                const int r = t128 >> 3, part = t128 & 7;
+                int32_t sum = 0;
+                if (r < p.m) {
+                    const uint8_t* row = p.a + ba * p.stride_a + r * p.lda;
+                    const int k_end = min(p.k, kb1 * rows::BK);
+                    const int chunks = k_end >> 4;
+                    for (int c = kb0 * (rows::BK / 16) + part; c < chunks; c += 8) {
+                        const uint4 w = __ldg(reinterpret_cast<const uint4*>(row) + c);
+                        if (e.za_signed) {
+                            sum = __dp4a(static_cast<int>(w.x), 0x01010101, sum);
+                            sum = __dp4a(static_cast<int>(w.y), 0x01010101, sum);
+                            sum = __dp4a(static_cast<int>(w.z), 0x01010101, sum);
+                            sum = __dp4a(static_cast<int>(w.w), 0x01010101, sum);
+                        } else {
+                            unsigned su = static_cast<unsigned>(sum);
+                            su = __dp4a(w.x, 0x01010101u, su);
+                            su = __dp4a(w.y, 0x01010101u, su);
+                            su = __dp4a(w.z, 0x01010101u, su);
+                            su = __dp4a(w.w, 0x01010101u, su);
+                            sum = static_cast<int32_t>(su);
+                        }
+                    }
+                    for (int kk = (chunks << 4) + part; kk < k_end; kk += 8) {  // the last k % 16 bytes
+                        const uint8_t v = __ldg(row + kk);
+                        sum += e.za_signed ? static_cast<int32_t>(static_cast<int8_t>(v)) : v;
+                    }
+                }
+                sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+                sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+                sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 4);
+                if (part == 0) row_sum[r] = sum;
+            }
+            if (threadIdx.x == 64) go[0] = mbar_wait(&tfull[acc], (seg >> 1) & 1, abort_flag) ? 1 : 0;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            const bool ok = go[0] != 0;
+            uint32_t r[32];
+            if (ok) {
+                tc_fence_after();
+                tmem_ld_32x32b_x32(tmem_base + acc * rows::TMEM_COLS + (static_cast<uint32_t>((warp & 3) * 32) << 16), r);
+                tmem_ld_wait();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[acc]);
+            bool finish = ok;
+            if (kb0 != 0 || kb1 != kbt) {
+                // A partial segment: leave its record, add its K blocks to the tile's ticket (also after a failed
+                // wait, so that the tickets stay balanced); the segment completing the tile finishes it.
+                const int slot = u == u0 ? 0 : 1;
+                int32_t* mine = p.split_part + (static_cast<int64_t>(worker) * 2 + slot) * PART_INTS;
+                if (ok) {
+#pragma unroll
+                    for (int v = 0; v < 17; v++) __stcg(mine + v * rows::BN + col, static_cast<int32_t>(r[v]));
+                    if (t128 < rows::MAXM) __stcg(mine + 17 * rows::BN + t128, row_sum[t128]);
+                }
+                __threadfence();
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (threadIdx.x == 64) {
+                    unsigned int* ticket = p.split_ticket + t;
+                    const unsigned int add = static_cast<unsigned int>(kb1 - kb0);
+                    const unsigned int old = atomicAdd(ticket, add);
+                    const bool complete = old + add == static_cast<unsigned int>(kbt);
+                    if (complete) atomicExch(ticket, 0u);
+                    go[1] = complete ? 1 : 0;
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                finish = ok && go[1] != 0;
+                if (finish) {
+                    __threadfence();
+                    const int64_t tu0 = static_cast<int64_t>(t) * kbt;
+                    const int w_first = rows_owner(tu0, p.units, workers);
+                    const int w_last = rows_owner(tu0 + kbt - 1, p.units, workers);
+                    int32_t rs = 0;
+                    for (int w = w_first; w <= w_last; w++) {
+                        if (w == worker) continue;
+                        const int wslot = p.units * w / workers >= tu0 ? 0 : 1;  // its first segment, or its last
+                        const int32_t* rec = p.split_part + (static_cast<int64_t>(w) * 2 + wslot) * PART_INTS;
+#pragma unroll
+                        for (int v = 0; v < 17; v++) r[v] += static_cast<uint32_t>(__ldcg(rec + v * rows::BN + col));
+                        if (t128 < rows::MAXM) rs += __ldcg(rec + 17 * rows::BN + t128);
+                    }
+                    if (t128 < rows::MAXM) row_sum[t128] += rs;
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                }
+            }
+            if (finish) {
+                const int n = tile * rows::BN + col;
+                if (n < p.n) {
+                    const uint32_t csb = r[16];  // sum over K of B[k, n]
+                    const int32_t zb = zp_value(e.zb, e.zb_vector, e.zb_signed, n);
+                    const uint32_t bias = e.int_bias ? static_cast<uint32_t>(__ldg(e.int_bias + n)) : 0u;
+#pragma unroll
+                    for (int m = 0; m < rows::MAXM; m++) {
+                        if (m < p.m) {
+                            const int32_t za = zp_value(e.za, e.za_vector, e.za_signed, m);
+                            uint32_t sm = r[m];
+                            if (e.zb != nullptr)
+                                sm += static_cast<uint32_t>(p.k) * static_cast<uint32_t>(za) * static_cast<uint32_t>(zb) -
+                                      static_cast<uint32_t>(zb) * static_cast<uint32_t>(row_sum[m]);
+                            if (e.za != nullptr) sm -= static_cast<uint32_t>(za) * csb;
+                            store_one<OUT>(e, b, m, n, sm + bias);
+                        }
+                    }
+                }
+            }
+            seg++;
+            u = static_cast<int64_t>(t) * kbt + kb1;
+        }
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 2 * rows::TMEM_COLS);
+    }
+    if (threadIdx.x == 0 && *abort_flag) atomicExch(p.error_flag, 1);
+}
+
 // ---- byte sums of two matrices in one launch ------------------------------------------------------------------------
 //
 // The zero-point correction needs the byte sums over K of A's rows and of B's columns. Each is a stream of the
@@ -420,6 +689,43 @@ static LaunchFn bind_rows_t(const RowsParams& p, const CUtensorMap& ma, const CU
     };
 }
 
+template <bool B_KMAJOR, int OUT>
+static LaunchFn bind_rows_stream_t(const RowsParams& p, const CUtensorMap& ma, const CUtensorMap& mb, dim3 grid,
+                                   uint32_t idesc) {
+    return [=](cudaStream_t stream) -> cudaError_t {
+        auto kern = int8_gemm_rows_stream_kernel<B_KMAJOR, OUT>;
+        static uint64_t configured = 0;
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return e;
+        const uint64_t bit = uint64_t(1) << (dev & 63);
+        if (!(configured & bit)) {
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rows::SMEM_BYTES);
+            if (e != cudaSuccess) return e;
+            configured |= bit;
+        }
+        return launch_pdl(kern, grid, dim3(rows::THREADS), rows::SMEM_BYTES, stream, ma, mb, p, idesc);
+    };
+}
+
+// The even split pays when one CTA per column tile would leave most SMs idle: at most one tile for every two SMs.
+// (Measured on B200: 8, 32 and 64 tiles of 8 to 64 K blocks ran 1.3 to 1.8 times faster split; 112 and 224 tiles
+// ran slower, the workers' scattered K positions costing more DRAM locality than the balance gains.) Two workers
+// per SM; each gets at least 8 units.
+int rows_workers(const GemmLaunch& L) {
+    const int64_t tiles = static_cast<int64_t>((L.n + rows::BN - 1) / rows::BN) * L.batch;
+    const int64_t kb = (L.k + rows::BK - 1) / rows::BK;
+    const int64_t sms = L.num_sms;
+    if (kb < 16 || sms < 1 || 2 * tiles > sms) return 0;
+    int64_t w = 2 * sms;
+    if (w > tiles * kb / 8) w = tiles * kb / 8;
+    return w < 2 ? 0 : static_cast<int>(w);
+}
+
+int64_t rows_part_ints(const GemmLaunch&, int workers) { return static_cast<int64_t>(workers) * 2 * PART_INTS; }
+
+int64_t rows_tickets(const GemmLaunch& L) { return static_cast<int64_t>((L.n + rows::BN - 1) / rows::BN) * L.batch; }
+
 LaunchFn prepare_gemm_rows(const GemmLaunch& L, cudaError_t* err) {
     *err = cudaErrorInvalidValue;
     const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
@@ -449,10 +755,27 @@ LaunchFn prepare_gemm_rows(const GemmLaunch& L, cudaError_t* err) {
     p.sums_stride = 0;
     p.sums_split_stride = 0;
     p.k_blocks_total = p.k_blocks;
+    p.tiles = (L.n + rows::BN - 1) / rows::BN;
+    p.units = static_cast<int64_t>(p.tiles) * L.batch * p.k_blocks;
+    p.split_part = L.rows_part;
+    p.split_ticket = L.rows_ticket;
     // The MMA's A operand is B (its type, MN-major unless B is stored N x K); its B operand is A (or the ones).
     const uint32_t idesc = idesc_i8(L.b_signed, L.a_signed, !L.trans_b, false, rows::BN, rows::MAXM);
-    const dim3 grid((L.n + rows::BN - 1) / rows::BN, L.batch);
     const bool km = L.trans_b != 0;
+    if (L.rows_part != nullptr && L.rows_ticket != nullptr && L.rows_workers > 0) {
+        const dim3 grid(static_cast<unsigned>(L.rows_workers));
+        switch (L.epi.out_kind) {
+            case OUT_I32: return km ? bind_rows_stream_t<true, OUT_I32>(p, ma, mb, grid, idesc)
+                                    : bind_rows_stream_t<false, OUT_I32>(p, ma, mb, grid, idesc);
+            case OUT_F32: return km ? bind_rows_stream_t<true, OUT_F32>(p, ma, mb, grid, idesc)
+                                    : bind_rows_stream_t<false, OUT_F32>(p, ma, mb, grid, idesc);
+            case OUT_U8: return km ? bind_rows_stream_t<true, OUT_U8>(p, ma, mb, grid, idesc)
+                                   : bind_rows_stream_t<false, OUT_U8>(p, ma, mb, grid, idesc);
+            default: return km ? bind_rows_stream_t<true, OUT_S8>(p, ma, mb, grid, idesc)
+                               : bind_rows_stream_t<false, OUT_S8>(p, ma, mb, grid, idesc);
+        }
+    }
+    const dim3 grid((L.n + rows::BN - 1) / rows::BN, L.batch);
     switch (L.epi.out_kind) {
         case OUT_I32: return km ? bind_rows_t<true, OUT_I32>(p, ma, mb, grid, idesc)
                                 : bind_rows_t<false, OUT_I32>(p, ma, mb, grid, idesc);

@@ -411,3 +411,33 @@ def test_config_sizes_checksums_and_sampled_rows(device, workload):
     with og.Int8Gemm(device) as gemm:
         kern = full_size_check(device, gemm, m, n, k, batch, a_signed, zp, trans_b)
         assert kern.startswith("tensor-core")
+
+
+@pytest.mark.parametrize("m,n,k,batch,trans_b", [
+    (16, 300, 2048, 1, False),    # 3 column tiles over 6 workers: every tile split
+    (7, 1000, 4100, 1, False),    # ragged K (the last K block holds 4 bytes), 33 workers
+    (1, 128, 2560, 3, False),     # batched B, one row
+    (16, 384, 3072, 2, True),     # B stored N x K
+    (12, 2048, 8192, 1, False),   # 16 tiles over 128 workers, each tile met by eight segments
+])
+def test_few_rows_even_split_is_bit_exact(device, m, n, k, batch, trans_b):
+    """The few-rows kernel with its (column tile, K block) units split evenly across persistent workers (partial
+    segments meet through records and tickets; the segment completing a tile adds the others' dot products, column
+    sums of B and row sums of A, then finishes it): int32 with every zero-point mode, the float form and the
+    requantized form, against the oracle, twice in a row on one instance (the tickets return to zero)."""
+    gemm = og.Int8Gemm(device, CONFIGS["tensor-core-auto"])
+    try:
+        for rep in range(2):
+            for za_mode, zb_mode, a_s, b_s in ((0, 0, True, True), (1, 2, False, True), (2, 1, True, False),
+                                               (1, 1, False, False)):
+                c = align_case(Case("k-split", problem(m, n, k, batch=batch, trans_b=trans_b), a_s, b_s,
+                                    za_mode, zb_mode))
+                bad, kernel = run_int32(device, gemm, c, 1000 * rep + 10 * za_mode + zb_mode)
+                assert kernel == "tensor-core-rows", kernel
+                assert bad == 0, f"zp modes {za_mode}/{zb_mode}: {bad} mismatches"
+            if batch == 1 and not trans_b:
+                assert float_case(device, gemm, m, n, k, True, True, True, 31 + rep, aligned=True) == 0
+                assert requant_case(device, gemm, m, n, k, True, False, 5, True, 41 + rep, True, True,
+                                    aligned=True) == 0
+    finally:
+        gemm.dispose()

@@ -108,12 +108,11 @@ int byte_sum_splits(const GemmLaunch& L, int max_splits);
 LaunchFn prepare_byte_sums(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, int splits, cudaError_t* err);
 cudaError_t launch_byte_sums(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, cudaStream_t stream);
 cudaError_t launch_byte_sums_simt(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, cudaStream_t stream);
-// Sums over K of every column of a K x cols (k_major = false) or cols x K (k_major = true) byte matrix, through the
-// tensor cores (og_gemm_rows.cu), K split `splits` ways (partials at out + split * batches * cols).
-int sums_splits(int cols, int k, int batches, int num_sms, int max_splits);
 // The byte sums of A's rows and B's columns (either may be null) in one launch of the tensor-core sums kernel.
 LaunchFn prepare_byte_sums_pair_tc(const GemmLaunch& L, int32_t* row_sums, int32_t* col_sums, int splits,
                                    cudaError_t* err);
+// Sums over K of every column of a K x cols (k_major = false) or cols x K (k_major = true) byte matrix, through the
+// tensor cores (og_gemm_rows.cu), K split `splits` ways (partials at out + split * batches * cols).
 LaunchFn prepare_byte_sums_tc(const uint8_t* mat, int cols, int k, int64_t ld, int64_t bstride, int batches,
                               bool k_major, bool is_signed, int32_t* out, int splits, int* error_flag,
                               cudaError_t* err);

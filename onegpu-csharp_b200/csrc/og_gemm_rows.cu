@@ -652,18 +652,6 @@ done:
 bool make_tensor_map_u8(CUtensorMap* map, const void* base, uint64_t x, uint64_t y, uint64_t z, uint64_t stride_y,
                         uint64_t stride_z, uint32_t box_x, uint32_t box_y);
 
-// How many K splits the sums-only launch over `cols` columns and `batches` batches uses: enough CTAs for two per SM,
-// at most `max_splits`, and never an empty split.
-int sums_splits(int cols, int k, int batches, int num_sms, int max_splits) {
-    const int tiles = (cols + rows::BN - 1) / rows::BN * batches;
-    const int kb = (k + rows::BK - 1) / rows::BK;
-    int s = (2 * num_sms + tiles - 1) / tiles;
-    s = s < 1 ? 1 : (s > max_splits ? max_splits : s);
-    s = s > kb ? kb : s;
-    const int per = (kb + s - 1) / s;
-    return (kb + per - 1) / per;
-}
-
 bool rows_eligible(const GemmLaunch& L) {
     return L.m >= 1 && L.m <= rows::MAXM && L.batch <= 65535 && tc_eligible(L);
 }
@@ -806,7 +794,7 @@ LaunchFn prepare_byte_sums_tc(const uint8_t* mat, int cols, int k, int64_t ld, i
     p.n = cols;
     p.k = k;
     p.k_blocks_total = (k + rows::BK - 1) / rows::BK;
-    p.k_blocks = (p.k_blocks_total + splits - 1) / splits;  // every split gets at least one K block (see sums_splits)
+    p.k_blocks = (p.k_blocks_total + splits - 1) / splits;  // every split gets at least one K block (see byte_sum_splits)
     p.a_batched = 0;
     p.b_batched = batches > 1;
     p.error_flag = error_flag;
@@ -833,7 +821,7 @@ static bool sums_job(SumsJob& j, CUtensorMap& map, const uint8_t* mat, int cols,
     j.batches = batches;
     j.splits = splits;
     j.k_blocks_total = (k + rows::BK - 1) / rows::BK;
-    j.k_blocks = (j.k_blocks_total + splits - 1) / splits;  // every split gets at least one K block (sums_splits)
+    j.k_blocks = (j.k_blocks_total + splits - 1) / splits;  // every split gets at least one K block (byte_sum_splits)
     j.kmajor = k_major ? 1 : 0;
     j.batched = batches > 1;
     j.idesc = idesc_i8(is_signed, false, !k_major, false, rows::BN, rows::MAXM);

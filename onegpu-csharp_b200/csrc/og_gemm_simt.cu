@@ -257,12 +257,16 @@ int byte_sum_splits(const GemmLaunch& L, int max_splits) {
     if (!sums_on_tensor_cores(L)) return 1;
     const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
     const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
-    const int sa = L.epi.zb != nullptr ? sums_splits(L.m, L.k, ba, L.num_sms, max_splits) : 1;
-    const int sb = L.epi.za != nullptr ? sums_splits(L.n, L.k, bb, L.num_sms, max_splits) : 1;
-    // One count for both operands (they share K, so neither gets an empty split).
+    // Both operands' tiles run in one launch (two CTAs per SM): as many K splits as fit all of them in one round of
+    // resident CTAs (a second, partial round would cost a whole CTA's time again), at most max_splits and one K block
+    // per split. One count for both operands (they share K, so neither gets an empty split).
+    const int64_t ta = L.epi.zb != nullptr ? int64_t((L.m + 127) / 128) * ba : 0;
+    const int64_t tb = L.epi.za != nullptr ? int64_t((L.n + 127) / 128) * bb : 0;
     const int kb = (L.k + 127) / 128;
-    const int s = sa > sb ? sa : sb;
-    const int per = (kb + s - 1) / s;
+    int64_t s = ta + tb > 0 ? (2 * int64_t(L.num_sms)) / (ta + tb) : 1;
+    s = s < 1 ? 1 : (s > max_splits ? max_splits : s);
+    s = s > kb ? kb : s;
+    const int per = static_cast<int>((kb + s - 1) / s);
     return (kb + per - 1) / per;
 }
 

@@ -46,10 +46,10 @@ struct Cfg {
     static constexpr int B_COLS = BN / CG;            // columns of B staged by one CTA
     static constexpr int B_BYTES = B_COLS * BK;       // 32 KB or 16 KB per CTA
     static constexpr int B_BOX = 128 * BK;            // one 128-column box of an MN-major B
-    static constexpr int STAGES = CG == 1 ? 4 : 5;
+    static constexpr int STAGES = CG == 1 ? 4 : 6;
     static constexpr int TERMS_BYTES = 5 * 4 * BN;     // per-column epilogue terms
     static constexpr int BOX_BYTES = 32 * 64;          // one 32-row x 16-word store box (64-byte rows)
-    static constexpr int BOXES = CG == 1 ? 1 : 2;      // store boxes per epilogue warp
+    static constexpr int BOXES = 1;                    // store boxes per epilogue warp
     static constexpr int STAGING_BYTES = EPI_WARPS * BOXES * BOX_BYTES;
     static constexpr int SMEM_BYTES =
         STAGES * (A_BYTES + B_BYTES) + STAGING_BYTES + 1024 /* alignment */ + 256 /* barriers */ + TERMS_BYTES;

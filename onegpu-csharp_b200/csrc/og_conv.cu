@@ -14,6 +14,11 @@
 //    instance (rows padded to 16 bytes) for the same reason;
 //  * without caller scratch, the batch runs in chunks of at most 256 MiB of columns (the reference: 64 MiB).
 // A padded position holds the zero point of x, so after the product subtracts that zero point it adds nothing.
+//
+// The unfolding (pack) kernels, by geometry: one-dimensional rows with width stride 1 or 2 (conv_pack_row_kernel: a
+// warp per input row, register windows of aligned words), other planes that fit shared memory (conv_pack_plane_kernel:
+// the plane staged and re-laid as phase rows, each output row then a contiguous slice), and the rest
+// (conv_pack_kernel: gathers from global memory).
 #include <cuda_runtime.h>
 
 #include <algorithm>

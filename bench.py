@@ -17,6 +17,7 @@ reference's int8 product (oracle/, all host threads) on a bounded row sample of 
 from __future__ import annotations
 
 import argparse
+import functools
 import json
 import os
 import re
@@ -200,8 +201,9 @@ class L2Flush:
                   "remains), steps timed by CUDA events"
 
 
+@functools.lru_cache(maxsize=None)
 def family_inputs(name: str):
-    """Seeded synthetic inputs of a family workload (host arrays) and its algorithmic work per step."""
+    """Seeded synthetic inputs of a family workload (host arrays, made once) and its algorithmic work per step."""
     f = FAMILIES[name]
     rng = np.random.default_rng(77)
     if name == "conv":
@@ -224,6 +226,9 @@ def family_inputs(name: str):
                 work=5.0 * count)
 
 
+_CONV_SAMPLE = {}  # target seconds -> output channels of the ConvInteger sample
+
+
 def cpu_family(name: str, threads: int, target_s: float):
     """The oracle's restatement of the reference's CPU definition on a bounded sample: (value, cores, sample)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -232,14 +237,24 @@ def cpu_family(name: str, threads: int, target_s: float):
     f = FAMILIES[name]
     d = family_inputs(name)
     if name == "conv":
-        p = dict(batch=1, cin=f["cin"], h=1, w=f["length"], cout=f["cout"], kh=1, kw=f["kernel"], stride_h=1,
-                 stride_w=f["stride"], pad_left=f["pad"], pad_right=f["pad"])
+        # One image; as many output channels as fit the target time (found once by doubling from 8).
         one = d["x"][: f["cin"] * f["length"]]
-        t0 = time.perf_counter()
-        oracle.conv_integer(p, one, False, d["w"], True, d["xz"][:1], d["wz"], True, threads=threads)
-        dt = time.perf_counter() - t0
-        return d["work"] / f["batch"] / dt / 1e12, threads, f"1 of {f['batch']} images ({dt:.1f} s), direct " \
-            f"convolution og_oracle_conv_integer (restates ConvIntegerTests.Reference) on {threads} threads"
+        cout = _CONV_SAMPLE.get(target_s, 8)
+        while True:
+            p = dict(batch=1, cin=f["cin"], h=1, w=f["length"], cout=cout, kh=1, kw=f["kernel"], stride_h=1,
+                     stride_w=f["stride"], pad_left=f["pad"], pad_right=f["pad"])
+            t0 = time.perf_counter()
+            oracle.conv_integer(p, one, False, d["w"][: cout * f["cin"] * f["kernel"]], True, d["xz"][:1],
+                                d["wz"][:cout], True, threads=threads)
+            dt = time.perf_counter() - t0
+            if dt >= 0.5 * target_s or cout >= f["cout"] or target_s in _CONV_SAMPLE:
+                break
+            cout = min(f["cout"], cout * 2)
+        _CONV_SAMPLE[target_s] = cout
+        work = d["work"] / f["batch"] * cout / f["cout"]
+        return work / dt / 1e12, threads, f"{cout} of {f['cout']} output channels of 1 of {f['batch']} images " \
+            f"({dt:.2f} s), direct convolution og_oracle_conv_integer (restates ConvIntegerTests.Reference) on " \
+            f"{threads} threads"
     n = min(d["count"], 1 << 23)
     t0 = time.perf_counter()
     reps = 0
@@ -264,8 +279,9 @@ def run_family_reference(args, rank: int, world: int):
     values, cores, sample = [], 1, ""
     for _ in range(args.warmup):
         cpu_family(args.workload, threads, 0.05)
+    per_step = min(args.cpu_seconds, max(0.01, REFERENCE_SECONDS / max(args.steps, 1)))
     for _ in range(args.steps):
-        v, cores, sample = cpu_family(args.workload, threads, max(0.5, args.cpu_seconds / max(args.steps, 1)))
+        v, cores, sample = cpu_family(args.workload, threads, per_step)
         values.append(v)
     v = statistics.median(values)
     d = family_inputs(args.workload)
@@ -427,15 +443,33 @@ def run_family(args, rank: int, world: int, local_rank: int):
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import og_oracle as oracle
+
     w = WORKLOADS[args.workload]
     threads = os.cpu_count() or 1
-    per_step = max(1.0, args.cpu_seconds / max(args.steps, 1))
+    n, k = w["n"], w["k"]
+    # Every step is the same bounded sample (rows of A against the whole B), sized so that the K steps together take
+    # about REFERENCE_SECONDS (at most args.cpu_seconds each); B and the rows are made once.
+    per_step = min(args.cpu_seconds, max(0.01, REFERENCE_SECONDS / max(args.steps, 1)))
+    b = oracle.bytes_(k * n, 31)
+    rows = 4
+    for _ in range(6):  # calibration (part of the warm-up)
+        a = oracle.bytes_(rows * k, 30)
+        t0 = time.perf_counter()
+        oracle.int8_gemm(a, True, b, True, m=rows, n=n, k=k, threads=threads)
+        dt = time.perf_counter() - t0
+        if 0.7 * per_step <= dt <= 1.4 * per_step or rows >= w["m"]:
+            break
+        rows = int(min(w["m"], max(1, rows * per_step / max(dt, 1e-4))))
+    a = oracle.bytes_(rows * k, 30)
     for _ in range(args.warmup):
-        cpu_gemm_tops(w["n"], w["k"], threads, 0.2, 4)
-    values, rows = [], 0
+        oracle.int8_gemm(a, True, b, True, m=rows, n=n, k=k, threads=threads)
+    values = []
     for _ in range(args.steps):
-        tops, dt, rows = cpu_gemm_tops(w["n"], w["k"], threads, per_step, w["m"])
-        values.append(tops)
+        t0 = time.perf_counter()
+        oracle.int8_gemm(a, True, b, True, m=rows, n=n, k=k, threads=threads)
+        values.append(2.0 * rows * n * k / (time.perf_counter() - t0) / 1e12)
     tops = statistics.median(values)
     full_ms = 2.0 * w["batch"] * w["m"] * w["n"] * w["k"] / (tops * 1e12) * 1e3
     sample = (f"{rows} of {w['m']} rows of A against the full B ({w['n']} x K {w['k']}) per step, extrapolated; "
@@ -449,6 +483,9 @@ def run_reference(args, rank: int, world: int):
                              "sample": sample},
             "e2e": {"value": round(tops, 6), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+REFERENCE_SECONDS = 120.0  # the reference arm's timed steps together, whatever --steps is
 
 
 def run_ours(args, rank: int, world: int, local_rank: int, dist):

@@ -1,11 +1,13 @@
 // The tensor-core int8 product for sm_100a: tcgen05.mma.kind::i8 with int32 accumulators in TMEM, operands staged by
 // TMA into 128-byte-swizzled shared memory, warp-specialised and persistent.
 //
-// One CTA per SM walks the output tiles (BM x BN = 128 x 256 of one batch) in a grouped order so that concurrently
-// running CTAs share A rows and B columns in L2. Warp 0 issues the TMA loads of a STAGES-deep ring of K blocks
-// (BK = 128 bytes); warp 1 owns the TMEM allocation and issues the MMAs (four 128x256x32 instructions per K block)
-// into one of two accumulators; warps 2-5 drain the other accumulator (tcgen05.ld), apply the zero-point
-// correction and the epilogue and store C while the next tile is being multiplied.
+// One CTA per SM (or a CTA pair with cta_group::2, 256 x 256 tiles) walks the output tiles (BM x BN = 128 x 256 of
+// one batch per CTA) in a grouped order so that concurrently running CTAs share A rows and B columns in L2. Warp 0
+// issues the TMA loads of a STAGES-deep ring of K blocks (BK = 128 bytes); warp 1 owns the TMEM allocation and
+// issues the MMAs (four K = 32 instructions per K block) into one of two accumulators; warps 2-9 drain the other
+// accumulator (tcgen05.ld; two warps per TMEM lane quadrant, each half of the columns), apply the zero-point
+// correction and the epilogue and store C (through one shared-memory box per warp and TMA stores) while the next
+// tile is being multiplied.
 //
 // A is M x K row-major (K-major for the MMA). B is either K x N row-major (TransposeB = false; MN-major for the MMA,
 // loaded as two 128-column boxes) or N x K (TransposeB = true; K-major). The MMA multiplies the operands' own

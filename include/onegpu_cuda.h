@@ -174,6 +174,21 @@ OG_API og_status og_device_timestamp(og_device* device, og_timestamps* set, uint
 /* GpuDevice.TryReadTimestamps: nanoseconds of each timestamp relative to timestamp `first`; waits for them. */
 OG_API og_status og_timestamps_read(og_timestamps* set, uint32_t first, uint32_t count, double* ns);
 
+/* ---- CUDA graphs of submitted work (no counterpart in the reference, whose encoders are re-submitted) ------------
+ * Launch-bound work such as a decode step is recorded once and replayed as one graph launch. Between
+ * og_device_capture_begin and og_device_capture_end the device stream is captured (relaxed mode): work submitted to
+ * the device then (og_device_submit, og_device_timestamp, og_buffer_fill) is recorded, not run. Encode and submit
+ * the same work once before capturing it: a kernel instance's first encoding of a shape may allocate and clear its
+ * scratch, which a capture would refuse. Calls that wait for the device (og_device_wait_idle, the blocking
+ * transfers) fail while a capture is open. A graph reads and writes the buffers it was recorded with, as
+ * they are when it is launched; it must not outlive them or the kernel instances (Int8Gemm, ...) that recorded it. */
+typedef struct og_graph og_graph;
+OG_API og_status og_device_capture_begin(og_device* device);
+OG_API og_status og_device_capture_end(og_device* device, og_graph** out);
+/* Replays the graph on its device's stream, in stream order with other submitted work. */
+OG_API og_status og_graph_launch(og_graph* graph);
+OG_API og_status og_graph_destroy(og_graph* graph);
+
 /* ---- Int8Gemm (src/RecursiveAI.OneGpu.Kernels/Int8Gemm.cs:124-683) --------------------------------------------- */
 
 typedef struct og_int8_gemm og_int8_gemm;

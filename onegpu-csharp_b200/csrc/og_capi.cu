@@ -140,6 +140,12 @@ struct og_readback {
     int* status_host = nullptr;  // the device's failure word as it stood when the copy ran
 };
 
+struct og_graph {
+    og_device* device = nullptr;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
 struct og_timestamps {
     og_device* device = nullptr;
     std::vector<cudaEvent_t> events;
@@ -865,6 +871,54 @@ OG_API og_status og_device_submit(og_device* d, og_encoder* e) {
                           "", "", ""};
         use(d);
         for (auto& op : e->ops) check_cuda(op(d->stream), "Submit");
+    });
+}
+
+OG_API og_status og_device_capture_begin(og_device* d) {
+    return guard([&] {
+        if (d == nullptr) null_arg("GpuDevice", "device");
+        use(d);
+        check_cuda(cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeRelaxed), "BeginCapture");
+    });
+}
+
+OG_API og_status og_device_capture_end(og_device* d, og_graph** out) {
+    return guard([&] {
+        if (d == nullptr) null_arg("GpuDevice", "device");
+        if (out == nullptr) null_arg("GpuDevice", "out");
+        use(d);
+        cudaGraph_t graph = nullptr;
+        check_cuda(cudaStreamEndCapture(d->stream, &graph), "EndCapture");
+        cudaGraphExec_t exec = nullptr;
+        const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+        if (e != cudaSuccess) {
+            cudaGraphDestroy(graph);
+            check_cuda(e, "EndCapture");
+        }
+        auto* g = new og_graph();
+        g->device = d;
+        g->graph = graph;
+        g->exec = exec;
+        *out = g;
+    });
+}
+
+OG_API og_status og_graph_launch(og_graph* g) {
+    return guard([&] {
+        if (g == nullptr) null_arg("GpuGraph", "graph");
+        use(g->device);
+        check_cuda(cudaGraphLaunch(g->exec, g->device->stream), "GraphLaunch");
+    });
+}
+
+OG_API og_status og_graph_destroy(og_graph* g) {
+    return guard([&] {
+        if (g == nullptr) return;
+        use(g->device);
+        cudaStreamSynchronize(g->device->stream);
+        cudaGraphExecDestroy(g->exec);
+        cudaGraphDestroy(g->graph);
+        delete g;
     });
 }
 

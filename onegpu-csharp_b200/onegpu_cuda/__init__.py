@@ -113,6 +113,10 @@ EXPORTS = {
     "og_timestamps_destroy": [_P],
     "og_encoder_timestamp": [_P, _P, ctypes.c_uint32],
     "og_device_timestamp": [_P, _P, ctypes.c_uint32],
+    "og_device_capture_begin": [_P],
+    "og_device_capture_end": [_P, _PP],
+    "og_graph_launch": [_P],
+    "og_graph_destroy": [_P],
     "og_timestamps_read": [_P, ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(ctypes.c_double)],
     "og_int8_gemm_create": [_P, ctypes.POINTER(og_int8_gemm_options), _PP],
     "og_int8_gemm_destroy": [_P],
@@ -323,6 +327,22 @@ class GpuCommandEncoder:
         _check(_lib.og_encoder_timestamp(self.handle, stamps.handle, index))
 
 
+class GpuGraph:
+    """A CUDA graph of submitted work (og_graph): launch() replays it on the device stream."""
+
+    def __init__(self, device: "GpuDevice", handle: ctypes.c_void_p):
+        self.device = device
+        self.handle = handle
+
+    def launch(self) -> None:
+        _check(_lib.og_graph_launch(self.handle))
+
+    def dispose(self) -> None:
+        if self.handle:
+            _check(_lib.og_graph_destroy(self.handle))
+            self.handle = None
+
+
 class GpuTimestampSet:
     def __init__(self, device: "GpuDevice", count: int):
         self.device = device
@@ -415,6 +435,16 @@ class GpuDevice:
 
     def timestamp(self, stamps: GpuTimestampSet, index: int) -> None:
         _check(_lib.og_device_timestamp(self.handle, stamps.handle, index))
+
+    def capture_begin(self) -> None:
+        """og_device_capture_begin: work submitted from now on is recorded into a CUDA graph, not run."""
+        _check(_lib.og_device_capture_begin(self.handle))
+
+    def capture_end(self) -> "GpuGraph":
+        """og_device_capture_end: the recorded work as a graph to replay with GpuGraph.launch."""
+        h = ctypes.c_void_p()
+        _check(_lib.og_device_capture_end(self.handle, ctypes.byref(h)))
+        return GpuGraph(self, h)
 
     def wait_idle(self) -> None:
         _check(_lib.og_device_wait_idle(self.handle))

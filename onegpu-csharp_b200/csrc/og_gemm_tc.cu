@@ -638,7 +638,8 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
     }
 
 done:
-    if (tma_store && warp >= 2 && lane == 0) bulk_wait_group_all();  // stores finished before shared memory goes
+    // The stores have read their boxes before shared memory goes (their global writes complete with the grid).
+    if (tma_store && warp >= 2 && lane == 0) bulk_wait_group_read<0>();
     __syncthreads();
     if constexpr (CG == 2) cluster_sync_all();  // neither CTA frees the pair's TMEM while the other still reads it
     if (warp == 1) {

@@ -441,3 +441,33 @@ def test_few_rows_even_split_is_bit_exact(device, m, n, k, batch, trans_b):
                                     aligned=True) == 0
     finally:
         gemm.dispose()
+
+
+@pytest.mark.parametrize("cfg", ["default", "portable", "tensor-core-1sm", "tensor-core-2sm"])
+def test_config_1_matmulinteger_is_bit_exact(device, cfg):
+    """Config 1 at its size: A u8 [256 x 384] uniform 0..255 with scalar zero point 128, B s8 [384 x 512] uniform
+    -128..127 with zero point 0, int32 output, against the oracle (the reference's CPU case)."""
+    rng = np.random.default_rng(0)
+    m, k, n = 256, 384, 512
+    a = rng.integers(0, 256, size=m * k, dtype=np.int16).astype(np.uint8)
+    b = rng.integers(-128, 128, size=k * n, dtype=np.int16).astype(np.int8)
+    p = problem(m, n, k)
+    want = oracle.int8_gemm(a, False, b.view(np.uint8), True, np.array([128], np.uint8), False,
+                            np.array([0], np.uint8), False, **oracle_shape(p))
+    gemm = og.Int8Gemm(device, CONFIGS[cfg])
+    bufs = [device.create_buffer(np.uint8, a), device.create_buffer(np.int8, b),
+            device.create_buffer(np.int32, np.full(m * n + 2, SENTINEL, np.int32)),
+            device.create_buffer(np.uint8, np.array([128, 0, 0, 0], np.uint8)),
+            device.create_buffer(np.int8, np.zeros(4, np.int8))]
+    try:
+        enc = device.begin_commands()
+        gemm.encode_int32(enc, og.Int8GemmProblem(**p), bufs[0], bufs[1], bufs[2], og.Int8Operand(bufs[3], 0),
+                          og.Int8Operand(bufs[4], 0))
+        device.submit(enc)
+        got = bufs[2].read()
+        assert np.array_equal(got[:m * n], want), gemm.last_kernel
+        assert np.all(got[m * n:] == SENTINEL)
+    finally:
+        for v in bufs:
+            v.dispose()
+        gemm.dispose()

@@ -712,9 +712,20 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         if world == 1 and not args.no_cpu:
             threads = os.cpu_count() or 1
             tops, dt, rows = cpu_gemm_tops(shard_n, K, threads, args.cpu_seconds, M)
-            cpu = {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port",
-                   "sample": f"{rows} of {M} rows x {shard_n} x K {K} on {threads} threads "
-                             f"({dt:.1f} s), extrapolated to TOPS"}
+            sample = f"{rows} of {M} rows x {shard_n} x K {K} on {threads} threads ({dt:.1f} s), extrapolated to TOPS"
+            if dq is not None:
+                # Config 2's step also quantizes the activations: the oracle's DynamicReference over the whole x
+                # (one thread), added to the product's extrapolated time.
+                sys.path.insert(0, os.path.join(ROOT, "oracle"))
+                import og_oracle as oracle
+
+                t0 = time.perf_counter()
+                oracle.dynamic_quantize(x_host)
+                dq_s = time.perf_counter() - t0
+                gemm_s = 2.0 * M * shard_n * K / (tops * 1e12)
+                tops = 2.0 * M * shard_n * K / (gemm_s + dq_s) / 1e12
+                sample += f"; plus DynamicQuantizeLinear of all {x_host.size} elements on 1 thread ({dq_s:.2f} s)"
+            cpu = {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample}
         clk = clocks.summary()
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps,

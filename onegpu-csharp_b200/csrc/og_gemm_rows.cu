@@ -17,6 +17,8 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "og_gemm.h"
 #include "og_kernels.cuh"
 #include "og_ptx.cuh"
@@ -663,15 +665,15 @@ static LaunchFn bind_rows_t(const RowsParams& p, const CUtensorMap& ma, const CU
                             uint32_t idesc) {
     return [=](cudaStream_t stream) -> cudaError_t {
         auto kern = int8_gemm_rows_kernel<B_KMAJOR, OUT>;
-        static uint64_t configured = 0;
+        static std::atomic<uint64_t> configured{0};  // devices whose attribute is set
         int dev = 0;
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
         const uint64_t bit = uint64_t(1) << (dev & 63);
-        if (!(configured & bit)) {
+        if (!(configured.load() & bit)) {
             e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rows::SMEM_BYTES);
             if (e != cudaSuccess) return e;
-            configured |= bit;
+            configured.fetch_or(bit);
         }
         return launch_pdl(kern, grid, dim3(rows::THREADS), rows::SMEM_BYTES, stream, ma, mb, p, idesc);
     };
@@ -682,15 +684,15 @@ static LaunchFn bind_rows_stream_t(const RowsParams& p, const CUtensorMap& ma, c
                                    uint32_t idesc) {
     return [=](cudaStream_t stream) -> cudaError_t {
         auto kern = int8_gemm_rows_stream_kernel<B_KMAJOR, OUT>;
-        static uint64_t configured = 0;
+        static std::atomic<uint64_t> configured{0};  // devices whose attribute is set
         int dev = 0;
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
         const uint64_t bit = uint64_t(1) << (dev & 63);
-        if (!(configured & bit)) {
+        if (!(configured.load() & bit)) {
             e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rows::SMEM_BYTES);
             if (e != cudaSuccess) return e;
-            configured |= bit;
+            configured.fetch_or(bit);
         }
         return launch_pdl(kern, grid, dim3(rows::THREADS), rows::SMEM_BYTES, stream, ma, mb, p, idesc);
     };
@@ -866,16 +868,16 @@ LaunchFn prepare_byte_sums_pair_tc(const GemmLaunch& L, int32_t* row_sums, int32
     const CUtensorMap m0 = maps[0], m1 = maps[1];
     const dim3 grid(static_cast<unsigned>(ctas));
     return [=](cudaStream_t stream) -> cudaError_t {
-        static uint64_t configured = 0;
+        static std::atomic<uint64_t> configured{0};  // devices whose attribute is set
         int dev = 0;
         cudaError_t e = cudaGetDevice(&dev);
         if (e != cudaSuccess) return e;
         const uint64_t bit = uint64_t(1) << (dev & 63);
-        if (!(configured & bit)) {
+        if (!(configured.load() & bit)) {
             e = cudaFuncSetAttribute(int8_byte_sums_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      SUMS_SMEM_BYTES);
             if (e != cudaSuccess) return e;
-            configured |= bit;
+            configured.fetch_or(bit);
         }
         return launch_pdl(int8_byte_sums_kernel, grid, dim3(rows::THREADS), SUMS_SMEM_BYTES, stream, m0, m1, p);
     };

@@ -18,6 +18,8 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -745,15 +747,15 @@ bool tc_eligible(const GemmLaunch& L) {
 
 // Sets the kernel's dynamic shared-memory limit once per device (the attribute is per device).
 template <class K>
-static cudaError_t configure(K kern, int smem, uint64_t& configured) {
+static cudaError_t configure(K kern, int smem, std::atomic<uint64_t>& configured) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     const uint64_t bit = uint64_t(1) << (dev & 63);
-    if (!(configured & bit)) {
+    if (!(configured.load() & bit)) {
         e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
-        configured |= bit;
+        configured.fetch_or(bit);
     }
     return cudaSuccess;
 }
@@ -766,7 +768,7 @@ static LaunchFn bind_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensor
     using C = tc::Cfg<CG>;
     const uint32_t idesc = idesc_i8(L.a_signed, L.b_signed, false, B_MN, C::BM, tc::BN);
     return [=](cudaStream_t stream) -> cudaError_t {
-        static uint64_t configured = 0;
+        static std::atomic<uint64_t> configured{0};  // devices whose attribute is set
         if constexpr (CG == 2) {
             auto kern = int8_gemm_tc2_kernel<B_MN, OUT>;
             cudaError_t e = configure(kern, C::SMEM_BYTES, configured);

@@ -156,7 +156,7 @@ struct og_int8_gemm {
     bool allow_dot = true;
     int kernel = OG_KERNEL_AUTO;
     int tile = 0;
-    int stream_k = 0;  // 0 by size, 1 never, 2 whenever possible
+    int stream_k = 0;  // 0 and 1: whole tiles per SM pair; 2: stream-K whenever the last wave of tiles is partial
     std::string variant;
     std::string last = "none";
     std::vector<void*> scratch;  // int32 byte-sum buffers; older ones live until destroy (recorded work may name them)

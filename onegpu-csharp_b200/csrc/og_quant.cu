@@ -40,6 +40,7 @@ struct QuantArgs {
     uint32_t inner_magic, axis_magic;  // j / inner and q / axis_len by div_magic
     int32_t inner_shift, axis_shift;
     int vec_params;       // DequantizeLinear: every vector's E parameters are consecutive and aligned (inner = 1)
+    int keep_out;         // QuantizeLinear: store with the default cache policy (a consumer follows), not streaming
 };
 
 // Fills in the division constants of a's inner and axis_len.
@@ -343,7 +344,10 @@ __global__ void __launch_bounds__(QTHREADS) quantize_kernel(const QuantArgs a) {
             param_next(a, c);
         }
     }
-    __stcs(reinterpret_cast<uint4*>(y + first), make_uint4(w[0], w[1], w[2], w[3]));
+    if (a.keep_out)
+        *reinterpret_cast<uint4*>(y + first) = make_uint4(w[0], w[1], w[2], w[3]);
+    else
+        __stcs(reinterpret_cast<uint4*>(y + first), make_uint4(w[0], w[1], w[2], w[3]));
 }
 
 // Splits the elements into a scalar head (up to the output's first boundary of `out_align` bytes), whole vectors of E
@@ -403,6 +407,7 @@ cudaError_t launch_quantize_u8_tensor(const float* x, int64_t count, uint8_t* y,
     a.axis_len = 1;
     a.inner = 1;
     a.out = y;
+    a.keep_out = 1;  // the product (and its byte sums) read the bytes next: leave them in L2
     return launch_quantize(a, false, false, s);
 }
 

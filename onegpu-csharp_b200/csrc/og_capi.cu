@@ -163,6 +163,9 @@ struct og_int8_gemm {
     int64_t scratch_elements = 0;
     void* sk_buf = nullptr;      // stream-K hand-over buffer of the tensor-core product, allocated on first need
     int64_t sk_bytes = 0;
+    // Pitched copies of operands that TMA cannot load in place (A, B; the latest of each; older ones live until destroy)
+    void* stage[2] = {nullptr, nullptr};
+    int64_t stage_bytes[2] = {0, 0};
     // Partials and tickets of the evenly split few-rows product (the latest pair; older ones live until destroy)
     std::vector<void*> rows_bufs;
     int32_t* rows_part = nullptr;
@@ -452,9 +455,85 @@ int32_t* own_scratch(og_int8_gemm* g, int64_t elements) {
 }
 
 // Chooses the kernel and records the product (and, for the tensor-core path with zero points, the byte sums).
+// Device memory for a staged operand (0: A, 1: B) from the instance, growing geometrically.
+uint8_t* own_stage(og_int8_gemm* g, int which, int64_t bytes) {
+    if (g->stage[which] != nullptr && g->stage_bytes[which] >= bytes) return static_cast<uint8_t*>(g->stage[which]);
+    int64_t len = std::max<int64_t>(bytes, std::max<int64_t>(int64_t(1) << 20, g->stage_bytes[which] * 2));
+    void* p = nullptr;
+    check_cuda(cudaMalloc(&p, static_cast<size_t>(len)), "Int8Gemm staged operand");
+    g->scratch.push_back(p);  // freed with the instance
+    g->stage[which] = p;
+    g->stage_bytes[which] = len;
+    return static_cast<uint8_t*>(p);
+}
+
+// Copies one operand (`rows` x `width` bytes per batch, `ld` apart, batches `stride` apart) into a pitched buffer of
+// the instance whose rows start on 16-byte boundaries, recording the copies; returns the new pitch.
+int64_t stage_operand(og_int8_gemm* g, og_encoder* enc, int which, const uint8_t*& base, int64_t ld, int64_t& stride,
+                      int batches, int64_t rows, int64_t width) {
+    const int64_t pitch = (width + 15) & ~int64_t(15);
+    uint8_t* dst = own_stage(g, which, batches * rows * pitch);
+    const uint8_t* src = base;
+    const int64_t sstride = stride;
+    if (batches == 1 || sstride == rows * ld) {
+        // One two-dimensional copy covers every batch (shared, or dense batches).
+        const int64_t height = (batches == 1 ? 1 : batches) * rows;
+        enc->ops.push_back([=](cudaStream_t s) {
+            return cudaMemcpy2DAsync(dst, static_cast<size_t>(pitch), src, static_cast<size_t>(ld),
+                                     static_cast<size_t>(width), static_cast<size_t>(height), cudaMemcpyDeviceToDevice,
+                                     s);
+        });
+    } else {
+        enc->ops.push_back([=](cudaStream_t s) {
+            for (int b = 0; b < batches; b++) {
+                const cudaError_t e = cudaMemcpy2DAsync(dst + b * rows * pitch, static_cast<size_t>(pitch),
+                                                        src + b * sstride, static_cast<size_t>(ld),
+                                                        static_cast<size_t>(width), static_cast<size_t>(rows),
+                                                        cudaMemcpyDeviceToDevice, s);
+                if (e != cudaSuccess) return e;
+            }
+            return cudaSuccess;
+        });
+    }
+    base = dst;
+    stride = batches > 1 ? rows * pitch : 0;
+    return pitch;
+}
+
+// Products large enough for the tensor cores whose A or B rows (or batches) do not start on 16-byte boundaries, so
+// that TMA cannot load them in place: the misaligned operand is copied into a pitched buffer (rows padded to 16 bytes;
+// the padding is never read) and the tensor-core product runs on the copy. The copy moves each operand byte once;
+// the portable kernel it replaces runs far below the tensor cores' rate at these sizes.
+constexpr int64_t kStageMinOps = int64_t(1) << 27;
+
+bool stage_for_tensor_cores(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch& L) {
+    if (L.k < 1 || L.m < 1 || L.n < 1 || 2.0 * L.m * L.n * L.k * L.batch < double(kStageMinOps)) return false;
+    auto misaligned = [](const uint8_t* p, int64_t ld, int64_t stride, int batches) {
+        return (reinterpret_cast<uintptr_t>(p) & 15) != 0 || (ld & 15) != 0 || (batches > 1 && (stride & 15) != 0);
+    };
+    const int ba = (L.batch > 1 && L.stride_a != 0) ? L.batch : 1;
+    const int bb = (L.batch > 1 && L.stride_b != 0) ? L.batch : 1;
+    bool staged = false;
+    if (misaligned(L.a, L.lda, L.stride_a, ba)) {
+        L.lda = stage_operand(g, enc, 0, L.a, L.lda, L.stride_a, ba, L.m, L.k);
+        staged = true;
+    }
+    if (misaligned(L.b, L.ldb, L.stride_b, bb)) {
+        const int64_t rows = L.trans_b ? L.n : L.k, width = L.trans_b ? L.k : L.n;
+        L.ldb = stage_operand(g, enc, 1, L.b, L.ldb, L.stride_b, bb, rows, width);
+        staged = true;
+    }
+    return staged;
+}
+
 void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_operand* caller_scratch) {
     const bool want_tc = g->allow_dot && g->kernel != OG_KERNEL_PORTABLE;
     bool tc = want_tc && og::tc_eligible(L);
+    bool staged = false;
+    if (want_tc && !tc && g->kernel == OG_KERNEL_AUTO) {
+        staged = stage_for_tensor_cores(g, enc, L);
+        tc = staged && og::tc_eligible(L);
+    }
     if (g->kernel == OG_KERNEL_TENSOR_CORE && !tc) {
         unsupported(kGemm,
                     "the tensor-core kernel needs K >= 1 and operands whose rows and batches start on 16-byte "
@@ -494,7 +573,7 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
         cudaError_t err;
         og::LaunchFn fn = og::prepare_gemm_rows(L, &err);  // tensor maps built now, at record time
         check_cuda(err, "Int8Gemm tensor maps");
-        g->last = "tensor-core-rows";
+        g->last = staged ? "tensor-core-rows-staged" : "tensor-core-rows";
         enc->ops.push_back(std::move(fn));
         enc->dispatches += 1;
         return;
@@ -549,7 +628,7 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
     og::LaunchFn fn = og::prepare_gemm_tc(L, &err);  // tensor maps built now, at record time
     check_cuda(err, "Int8Gemm tensor maps");
     g->last = std::string(og::tc_cta_group(L) == 2 ? "tensor-core-2sm" : "tensor-core-1sm") +
-              (stream_k ? "-stream-k" : "");
+              (stream_k ? "-stream-k" : "") + (staged ? "-staged" : "");
     enc->ops.push_back(std::move(fn));
     enc->dispatches += 1;
 }

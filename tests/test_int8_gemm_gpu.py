@@ -471,3 +471,31 @@ def test_config_1_matmulinteger_is_bit_exact(device, cfg):
         for v in bufs:
             v.dispose()
         gemm.dispose()
+
+
+@pytest.mark.parametrize("m,n,k,batch,trans_b,off_a,off_b", [
+    (512, 640, 1000, 1, False, 0, 0),    # A's rows 1000 bytes apart
+    (300, 1000, 1024, 1, False, 0, 0),   # B's rows 1000 bytes apart
+    (384, 520, 1000, 1, True, 3, 5),     # both, B stored N x K, bases off 16-byte boundaries
+    (256, 512, 999, 3, False, 0, 0),     # batched A and B, dense batches of odd size
+    (8, 8192, 3000, 1, False, 1, 0),     # few rows
+])
+def test_misaligned_operands_take_the_tensor_cores(device, m, n, k, batch, trans_b, off_a, off_b):
+    """Products large enough for the tensor cores whose operand rows or batches do not start on 16-byte boundaries:
+    the misaligned operands are copied into pitched buffers and the tensor-core product runs on the copies. int32 with
+    every zero-point mode, then the float and requantized forms, against the oracle."""
+    gemm = og.Int8Gemm(device)
+    try:
+        kernels = set()
+        for za_mode, zb_mode, a_s, b_s in ((1, 2, False, True), (2, 1, True, False), (0, 0, True, True)):
+            c = Case("staged", problem(m, n, k, batch=batch, trans_b=trans_b, off_a=off_a, off_b=off_b), a_s, b_s,
+                     za_mode, zb_mode)
+            bad, kernel = run_int32(device, gemm, c, 300 + za_mode)
+            kernels.add(kernel)
+            assert bad == 0, f"zp modes {za_mode}/{zb_mode} via {kernel}"
+        assert all(kr.startswith("tensor-core") and kr.endswith("-staged") for kr in kernels), kernels
+        if batch == 1 and not trans_b and off_a == 0 and off_b == 0:
+            assert float_case(device, gemm, m, n, k, True, True, True, 310) == 0
+            assert requant_case(device, gemm, m, n, k, True, False, 4, True, 311, True, True) == 0
+    finally:
+        gemm.dispose()

@@ -305,7 +305,23 @@ struct RowTaps {
 
 // One input row's output words. KW = 0: any tap count and dilation (tap positions found at run time); KW > 0: that
 // many taps of unit dilation with the window offset O fixed.
-template <int SW, int KW, int O>
+template <bool SMEM>
+__device__ __forceinline__ uint32_t row_word(const uint32_t* p) {
+    if constexpr (SMEM)
+        return *p;
+    else
+        return __ldg(p);
+}
+template <bool SMEM>
+__device__ __forceinline__ uint32_t row_byte(const uint8_t* p) {
+    if constexpr (SMEM)
+        return *p;
+    else
+        return __ldg(p);
+}
+
+// `row` is the input row in global memory, or (SMEM) its copy in shared memory at the same offset modulo 8.
+template <int SW, int KW, int O, bool SMEM = false>
 __device__ __forceinline__ void row_words(const PackArgs& a, const uint8_t* row, uint8_t* dst0, int32_t o,
                                           int32_t lane, uint32_t pad) {
     constexpr int NW = RowWindow<SW>::NW;
@@ -322,7 +338,7 @@ __device__ __forceinline__ void row_words(const PackArgs& a, const uint8_t* row,
             if (fast[u]) {
                 const uint32_t* wp = reinterpret_cast<const uint32_t*>(row + lo);
 #pragma unroll
-                for (int k = 0; k < NW; k++) win[u][k] = __ldg(wp + k);
+                for (int k = 0; k < NW; k++) win[u][k] = row_word<SMEM>(wp + k);
             }
         }
 #pragma unroll
@@ -348,7 +364,8 @@ __device__ __forceinline__ void row_words(const PackArgs& a, const uint8_t* row,
                     for (int e = 0; e < 4; e++) {
                         const int32_t ix = SW * (ox0 + e) + d;
                         uint32_t v = pad;
-                        if (ox0 + e < a.ow && static_cast<uint32_t>(ix) < static_cast<uint32_t>(a.w)) v = __ldg(row + ix);
+                        if (ox0 + e < a.ow && static_cast<uint32_t>(ix) < static_cast<uint32_t>(a.w))
+                            v = row_byte<SMEM>(row + ix);
                         word |= v << (8 * e);
                     }
                 }
@@ -388,6 +405,69 @@ __global__ void __launch_bounds__(PACK_THREADS, 4) conv_pack_row_kernel(const Pa
     }
 }
 
+// The row kernel with each warp's rows staged in shared memory: while a warp packs one row from its copy, the next
+// row of its grid-stride sequence is on its way (8-byte cp.async; the bytes before the row's first 8-byte boundary
+// and after its last one by plain loads), so a warp keeps a whole row in flight instead of a few words per lane.
+// The copy keeps the row's offset modulo 8, so the word windows are the row kernel's.
+template <int SW, int KW>
+__global__ void __launch_bounds__(PACK_THREADS, 2) conv_pack_row_staged_kernel(const PackArgs a, int32_t planes,
+                                                                              int32_t cap) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) uint8_t row_s[];
+    const int32_t lane = static_cast<int32_t>(threadIdx.x) & 31;
+    uint8_t* const bufs = row_s + (threadIdx.x >> 5) * 2 * cap;  // this warp's two row buffers
+    const int32_t warps = static_cast<int32_t>(gridDim.x) * (PACK_THREADS / 32);
+    const uint32_t pad = a.zp != nullptr ? __ldg(a.zp) : 0u;
+    auto plane_row = [&](int32_t plane, int32_t& ig, int32_t& c) {
+        ig = div_magic(plane, a.cin_g_magic, a.cin_g_shift);
+        c = plane - ig * a.cin_g;
+        const int32_t img = div_magic(ig, a.groups_magic, a.groups_shift);
+        const int32_t g = ig - img * a.groups;
+        return a.x + (static_cast<int64_t>(img) * a.cin + g * a.cin_g + c) * static_cast<int64_t>(a.w);
+    };
+    auto stage = [&](const uint8_t* row, uint8_t* buf) {
+        uint8_t* dst = buf + (reinterpret_cast<uintptr_t>(row) & 7);
+        int32_t head = static_cast<int32_t>((8 - (reinterpret_cast<uintptr_t>(row) & 7)) & 7);
+        if (head > a.w) head = a.w;
+        const int32_t chunks = (a.w - head) >> 3;
+        for (int32_t i = lane; i < head; i += 32) dst[i] = __ldg(row + i);
+        for (int32_t i = lane; i < chunks; i += 32) cp_async8(dst + head + 8 * i, row + head + 8 * i);
+        for (int32_t i = head + 8 * chunks + lane; i < a.w; i += 32) dst[i] = __ldg(row + i);
+        cp_async_commit();
+    };
+    int32_t plane = static_cast<int32_t>((blockIdx.x * PACK_THREADS + threadIdx.x) >> 5);
+    int32_t it = 0, ig, c;
+    if (plane < planes) stage(plane_row(plane, ig, c), bufs);
+    for (; plane < planes; plane += warps, it++) {
+        const uint8_t* row = plane_row(plane, ig, c);
+        const int32_t next = plane + warps;
+        if (next < planes) {
+            int32_t ig2, c2;
+            stage(plane_row(next, ig2, c2), bufs + ((it + 1) & 1) * cap);
+        } else {
+            cp_async_commit();  // an empty group keeps one group per step
+        }
+        cp_async_wait_group<1>();  // this row's copies are done
+        __syncwarp();
+        const uint8_t* srow = bufs + (it & 1) * cap + (reinterpret_cast<uintptr_t>(row) & 7);
+        uint8_t* dst0 = a.cols + (static_cast<int64_t>(ig) * a.rows + static_cast<int64_t>(c) * a.kw) * a.ld;
+        const int32_t o = static_cast<int32_t>((reinterpret_cast<uintptr_t>(row) - static_cast<uintptr_t>(a.pw)) & 3);
+        if constexpr (KW == 0) {
+            row_words<SW, 0, 0, true>(a, srow, dst0, o, lane, pad);
+        } else {
+            switch (o) {
+                case 0: row_words<SW, KW, 0, true>(a, srow, dst0, o, lane, pad); break;
+                case 1: row_words<SW, KW, 1, true>(a, srow, dst0, o, lane, pad); break;
+                case 2: row_words<SW, KW, 2, true>(a, srow, dst0, o, lane, pad); break;
+                default: row_words<SW, KW, 3, true>(a, srow, dst0, o, lane, pad); break;
+            }
+        }
+        __syncwarp();  // the warp is done with this buffer before it is refilled
+    }
+    cp_async_wait_all();
+}
+
 static cudaError_t launch_conv_pack(const PackArgs& a, int64_t planes, int num_sms, cudaStream_t s) {
     const bool wide = a.ld % 16 == 0 && (reinterpret_cast<uintptr_t>(a.cols) & 15) == 0;
     const int64_t hw = static_cast<int64_t>(a.h) * a.w;
@@ -401,6 +481,28 @@ static cudaError_t launch_conv_pack(const PackArgs& a, int64_t planes, int num_s
         const int64_t cap = 8 * static_cast<int64_t>(num_sms);
         const unsigned grid = static_cast<unsigned>(blocks < cap ? blocks : cap);
         const int32_t np = static_cast<int32_t>(planes);
+        // Rows up to ~6 KB are staged in shared memory (two buffers per warp, at least two CTAs per SM).
+        const int64_t row_cap = ((static_cast<int64_t>(a.w) + 8 + 15) & ~int64_t(15));
+        const int64_t smem = 2 * row_cap * (PACK_THREADS / 32);
+        if (smem <= 100 * 1024) {
+            int per_sm = static_cast<int>((200 * 1024) / smem);
+            per_sm = per_sm < 1 ? 1 : (per_sm > 2 ? 2 : per_sm);  // its registers allow two CTAs per SM
+            const int64_t resident = static_cast<int64_t>(per_sm) * num_sms;
+            const unsigned sgrid = static_cast<unsigned>(blocks < resident ? blocks : resident);
+            const int32_t c32 = static_cast<int32_t>(row_cap);
+            const size_t bytes = static_cast<size_t>(smem);
+            auto go = [&](auto kernel) -> cudaError_t {
+                if (bytes > 48 * 1024) {
+                    const cudaError_t e =
+                        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+                    if (e != cudaSuccess) return e;
+                }
+                return launch_pdl(kernel, dim3(sgrid), dim3(PACK_THREADS), bytes, s, a, np, c32);
+            };
+            if (a.kw == 3 && a.dw == 1)
+                return a.sw == 1 ? go(conv_pack_row_staged_kernel<1, 3>) : go(conv_pack_row_staged_kernel<2, 3>);
+            return a.sw == 1 ? go(conv_pack_row_staged_kernel<1, 0>) : go(conv_pack_row_staged_kernel<2, 0>);
+        }
         if (a.kw == 3 && a.dw == 1)  // the common three-tap kernel: every tap position a constant
             return a.sw == 1 ? launch_pdl(conv_pack_row_kernel<1, 3>, dim3(grid), dim3(PACK_THREADS), 0, s, a, np)
                              : launch_pdl(conv_pack_row_kernel<2, 3>, dim3(grid), dim3(PACK_THREADS), 0, s, a, np);

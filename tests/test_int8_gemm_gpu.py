@@ -499,3 +499,23 @@ def test_misaligned_operands_take_the_tensor_cores(device, m, n, k, batch, trans
             assert requant_case(device, gemm, m, n, k, True, False, 4, True, 311, True, True) == 0
     finally:
         gemm.dispose()
+
+
+@pytest.mark.parametrize("cfg", ["tensor-core-1sm", "tensor-core-2sm"])
+@pytest.mark.parametrize("m,n,k,batch,trans_b", [
+    (200, 600, 8192, 1, False),   # K of 64 whole blocks, split across the sums CTAs
+    (200, 600, 8200, 1, False),   # a partial last K block
+    (260, 1030, 777, 3, False),   # ragged column tiles, batched A and B, an odd K
+    (384, 700, 3000, 2, True),    # B stored N x K
+    (150, 530, 5, 1, False),      # K inside one block
+])
+def test_zero_point_byte_sums_are_bit_exact(device, cfg, m, n, k, batch, trans_b):
+    """The byte sums of the zero-point correction (row sums of A, column sums of B, through the tensor-core sums
+    kernel and added up by the product's epilogue) for every zero-point mode and signedness, against the oracle."""
+    with og.Int8Gemm(device, CONFIGS[cfg]) as gemm:
+        for za_mode, zb_mode, a_s, b_s in ((1, 2, False, True), (2, 1, True, False), (2, 2, True, True),
+                                           (1, 0, False, True), (0, 2, False, True)):
+            c = align_case(Case("sums", problem(m, n, k, batch=batch, trans_b=trans_b), a_s, b_s, za_mode, zb_mode))
+            bad, kernel = run_int32(device, gemm, c, 400 + 3 * za_mode + zb_mode)
+            assert kernel == cfg
+            assert bad == 0, f"zp modes {za_mode}/{zb_mode} signed {a_s}/{b_s}"

@@ -29,6 +29,13 @@ def test_every_declared_entry_point_is_exported():
     assert sorted(og.EXPORTS) == names
 
 
+def test_every_entry_point_has_a_csharp_binding():
+    """INTEGRATION.md's P/Invoke block declares each entry point the header declares, and nothing else."""
+    doc = open(os.path.join(os.path.dirname(HEADER), "..", "INTEGRATION.md"), encoding="utf-8").read()
+    bound = sorted(set(re.findall(r"\[LibraryImport\(Lib\)\][^;]*?\b(og_\w+)\s*\(", doc)))
+    assert bound == declared_symbols()
+
+
 def test_no_device_here_is_reported_not_crashed():
     if og.device_count() > 0:
         pytest.skip("a CUDA device is visible")

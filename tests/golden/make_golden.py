@@ -1,7 +1,7 @@
 """Generates tests/golden/reference_cases.json from the reference repository's own test files.
 
-Run in a container where the reference is mounted (default /root/reference); the GPU box never runs this script, the
-tests only read the JSON it wrote.
+Run where the reference repository is checked out, with its root as --reference; the GPU box never runs this script,
+the tests only read the JSON it wrote.
 
 What it records:
   * the case tables of the reference's int8 tests, read as text from the C# sources (shapes, fills, signedness and
@@ -314,7 +314,7 @@ def run_int32_case(case: dict, seed: int) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the reference repository")
     ap.add_argument("--out", default=os.path.join(os.path.dirname(os.path.abspath(__file__)),
                                                   "reference_cases.json"))
     args = ap.parse_args()

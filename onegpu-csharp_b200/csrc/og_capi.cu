@@ -1300,15 +1300,18 @@ OG_API og_status og_dynamic_quantize_encode(og_dynamic_quantize* q, og_encoder* 
         if (q == nullptr) throw OgError{OG_ERROR_INVALID_HANDLE, kDq, "dq", "null handle", "", "", ""};
         if (enc == nullptr) null_arg(kDq, "encoder");
         check_dq(x, offset_x, count, y, offset_y, scale, offset_scale, zp, offset_zp);
+        use(q->device);
         const float* xp = static_cast<const float*>(x->ptr) + offset_x;
         uint8_t* yp = static_cast<uint8_t*>(y->ptr) + offset_y;
         float* sp = static_cast<float*>(scale->ptr) + offset_scale;
         uint8_t* zpp = static_cast<uint8_t*>(zp->ptr) + offset_zp;
         og::DqScratch* scr = q->scratch;
         const int sms = q->device->sm_count;
+        int* status = q->device->status;
         const int64_t n = count;
-        enc->ops.push_back([=](cudaStream_t s) { return og::launch_dynamic_quantize(xp, n, yp, sp, zpp, scr, sms, s); });
-        enc->dispatches += 2;
+        enc->ops.push_back(
+            [=](cudaStream_t s) { return og::launch_dynamic_quantize(xp, n, yp, sp, zpp, scr, sms, status, s); });
+        enc->dispatches += og::dq_single_kernel(xp, n, yp) ? 1 : 2;
     });
 }
 

@@ -124,7 +124,11 @@ struct DqScratch;
 cudaError_t launch_quantize_u8_tensor(const float* x, int64_t count, uint8_t* y, const float* scale,
                                       const uint8_t* zero_point, cudaStream_t s);
 size_t dq_scratch_bytes();
+// Whether launch_dynamic_quantize runs as one kernel (range, grid barrier, quantize from on-chip copies of x) rather
+// than the range and quantize passes: large tensors, x 16-byte and y 4-byte aligned, one 1024-thread CTA with 224 KB
+// of shared memory fitting on every SM.
+bool dq_single_kernel(const float* x, int64_t count, const uint8_t* y);
 cudaError_t launch_dynamic_quantize(const float* x, int64_t count, uint8_t* y, float* scale_out, uint8_t* zp_out,
-                                    DqScratch* scratch, int num_sms, cudaStream_t stream);
+                                    DqScratch* scratch, int num_sms, int* error_flag, cudaStream_t stream);
 
 }  // namespace og

@@ -27,13 +27,16 @@ __device__ __forceinline__ float rne_quotient_r(float x, float s, float r, bool 
     return rne_quotient_exact(x, s);
 }
 
-// Clamps to the output type's range; NaN gives its lowest value (fmaxf returns the other operand for NaN).
+// Clamps an integer-valued v (a rounded quotient plus a zero point) to the output type's range and returns its byte;
+// NaN gives the lowest value (fmaxf returns the other operand for NaN). The clamped integer c lies in [-128, 255], so
+// c + 1.5 * 2^23 is exact and lies in [2^23, 2^24), where the float's mantissa is c + 2^22: its low byte is c's two's
+// complement byte, with no float-to-integer conversion.
 template <bool SIGNED>
 __device__ __forceinline__ uint32_t saturate_byte(float v) {
     const float lo = SIGNED ? -128.0f : 0.0f;
     const float hi = SIGNED ? 127.0f : 255.0f;
     v = fminf(fmaxf(v, lo), hi);
-    return static_cast<uint32_t>(static_cast<int32_t>(v)) & 0xFFu;
+    return __float_as_uint(__fadd_rn(v, 12582912.0f)) & 0xFFu;
 }
 
 }  // namespace og

@@ -167,3 +167,71 @@ def test_dynamic_quantize_near_ties(device):
                 for v in (bx, by, bs, bz):
                     v.dispose()
                 assert bad == 0, f"range [{lo}, {hi}] count {count}: {bad} bytes differ"
+
+
+def _run_dq(device, dq, x, off_x, off_y):
+    """One DynamicQuantizeLinear through the C ABI with sentinel bytes around the output; returns (y, scale, zero
+    point, launches recorded, stray bytes)."""
+    count = x.size
+    bx = device.create_buffer(np.float32, np.concatenate([np.zeros(off_x, np.float32), x]))
+    by = device.create_buffer(np.uint8, np.full(off_y + count + 8, 0x3C, np.uint8))
+    bs = device.create_buffer(np.float32, 1)
+    bz = device.create_buffer(np.uint8, np.full(4, 0xEE, np.uint8))
+    try:
+        enc = device.begin_commands()
+        dq.encode(enc, bx, off_x, count, by, off_y, bs, 0, bz, 0)
+        launches = enc.dispatch_count
+        device.submit(enc)
+        y, s, z = by.read(), bs.read()[0], bz.read()
+    finally:
+        for v in (bx, by, bs, bz):
+            v.dispose()
+    stray = int(np.count_nonzero(y[:off_y] != 0x3C)) + int(np.count_nonzero(y[off_y + count:] != 0x3C))
+    stray += int(np.count_nonzero(z[1:] != 0xEE))
+    return y[off_y:off_y + count], s, int(z[0]), launches, stray
+
+
+@pytest.mark.parametrize("count", [1 << 18, (1 << 18) + 3, 1_000_003, 4096 * 4096])
+def test_dynamic_quantize_single_kernel_is_bit_exact(device, count):
+    """Tensors of 2^18 elements and more whose input starts on a 16-byte boundary run as one kernel (range, grid
+    barrier, quantize from the copies kept in shared memory and registers, the rest read again): every distribution of
+    DynamicQuantizeIsBitExact (Int8Tests.cs:632-647) against the oracle, at the threshold, with a tail of elements past
+    the last whole float4, with slices that have a re-read rest, and at config 2's size; misaligned inputs still take
+    the two launches."""
+    kinds = golden()["tables"]["dq_counts"]["kinds"]
+    with og.DynamicQuantizeKernels(device) as dq:
+        for seed, kind in enumerate(kinds, start=count % 1000):
+            x = oracle.dq_input(count, seed, kind)
+            wy, ws, wz = oracle.dynamic_quantize(x)
+            for off_x, off_y, launches_want in ((0, 0, 1), (4, 8, 1), (1, 0, 2)):
+                y, s, z, launches, stray = _run_dq(device, dq, x, off_x, off_y)
+                what = f"kind {kind} offsets {off_x}/{off_y}"
+                assert launches == launches_want, what
+                assert stray == 0, what
+                assert np.array_equal(y, wy), what
+                assert np.float32(s).view(np.uint32) == np.float32(ws).view(np.uint32), what
+                assert z == wz, what
+
+
+def test_dynamic_quantize_single_kernel_special_values(device):
+    """NaN (skipped by the range, quantized to 0), infinities (an infinite scale: zero point 0) and an all-zero tensor
+    (scale 1, zero point 0) through the single kernel."""
+    count = 3 * (1 << 18) + 1
+    rng = np.random.default_rng(5)
+    base = rng.standard_normal(count).astype(np.float32)
+    cases = []
+    x = base.copy()
+    x[rng.choice(count, 1000, replace=False)] = np.nan
+    cases.append(x)
+    x = base.copy()
+    x[[7, count - 1]] = [np.inf, -np.inf]
+    cases.append(x)
+    cases.append(np.zeros(count, np.float32))
+    with og.DynamicQuantizeKernels(device) as dq:
+        for i, x in enumerate(cases):
+            wy, ws, wz = oracle.dynamic_quantize(x)
+            y, s, z, launches, stray = _run_dq(device, dq, x, 0, 0)
+            assert launches == 1 and stray == 0, i
+            assert np.array_equal(y, wy), i
+            assert np.float32(s).view(np.uint32) == np.float32(ws).view(np.uint32), i
+            assert z == wz, i

@@ -2,7 +2,8 @@
 og_graph_launch, against the oracle: each replay reads the buffers' contents as they are when it is launched. Covers
 the few-rows product split across workers (per-tile tickets that every launch must leave at zero), the tensor-core
 product with its byte-sums pass, and the DynamicQuantizeLinear -> dequantize-product chain (launches that overlap
-through programmatic dependent launch inside the graph)."""
+through programmatic dependent launch inside the graph; at 2^18 elements the quantization is the single cooperative
+kernel with its grid barrier)."""
 import numpy as np
 import pytest
 

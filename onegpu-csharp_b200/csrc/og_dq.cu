@@ -387,7 +387,10 @@ cudaError_t launch_dynamic_quantize(const float* x, int64_t count, uint8_t* y, f
         attr[0].val.cooperative = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        return cudaLaunchKernelEx(&cfg, dq_fused_kernel, x, count, y, scratch, scale_out, zp_out, error_flag);
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, dq_fused_kernel, x, count, y, scratch, scale_out, zp_out,
+                                                 error_flag);
+        if (e != cudaErrorCooperativeLaunchTooLarge) return e;
+        cudaGetLastError();  // refused before anything ran (the grid cannot be resident at once): two launches instead
     }
     int64_t blocks = (count + DQ_THREADS * 16 - 1) / (DQ_THREADS * 16);
     const int64_t cap = 4 * static_cast<int64_t>(num_sms) < DQ_MAX_BLOCKS ? 4 * static_cast<int64_t>(num_sms)

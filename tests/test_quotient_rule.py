@@ -45,3 +45,47 @@ def test_rule_declines_ties_nan_and_huge():
     with np.errstate(all="ignore"):
         _, fast = _rule(np.array([0.125, -0.375, np.nan, np.inf, 3e38, 1.1e6], F32), r)
     assert not fast.any()
+
+
+def _byte_through_bits(x: np.ndarray, s: np.float32, zp: int):
+    """(byte, taken) of DynamicQuantizeLinear's single-kernel path: cz = zp + 1.5 * 2^23, t = RN(RN(x r) + cz); the
+    rule's test on m = RN(x r) with d = m - (t - cz); where taken, t's bits clamped to [0x4B400000, 0x4B4000FF] give
+    the byte in their low 8 bits, elsewhere clamp(rint(RN(x / s)) + zp) with NaN to 0."""
+    r = F32(1) / s
+    cz = F32(F32(zp) + F32(12582912.0))
+    with np.errstate(all="ignore"):
+        m = (x * r).astype(F32)
+        t = (m + cz).astype(F32)
+        d = (m - (t - cz).astype(F32)).astype(F32)
+        test = (np.abs(m).astype(np.float64) * 2.0 ** -20 + np.abs(d).astype(np.float64)).astype(F32)
+        taken = (test < F32(0.5 - 2.0 ** -19)) & bool(np.isfinite(r) and abs(r) >= np.finfo(np.float32).tiny)
+        bits = np.clip(t.view(np.uint32), 0x4B400000, 0x4B4000FF) & 0xFF
+        v = (np.rint((x / s).astype(F32)) + F32(zp)).astype(F32)
+        slow = np.where(np.isnan(v), 0, np.clip(v, 0, 255))
+    return np.where(taken, bits, slow).astype(np.int64), taken
+
+
+def test_byte_through_bits_matches_the_definition():
+    """clamp(rint(x / s) + zp, 0, 255) with the division correctly rounded, NaN to 0, for DynamicQuantizeLinear's
+    scales (range / 255) and zero points, inputs crowded around half-integer quotients, huge quotients, NaN and
+    infinities."""
+    rng = np.random.default_rng(11)
+    taken_total = 0
+    for trial in range(120):
+        lo = -abs(rng.standard_normal()) * 10 ** rng.uniform(-3, 3)
+        hi = abs(rng.standard_normal()) * 10 ** rng.uniform(-3, 3)
+        s = F32((F32(hi) - F32(lo)) / F32(255))
+        zp = int(np.clip(np.rint(-(F32(lo) / s)), 0, 255))
+        k = rng.integers(-300, 300, size=20000).astype(np.float64)
+        ties = ((k + 0.5) * np.float64(s)).astype(F32)
+        near = (ties.view(np.int32) + rng.integers(-4, 5, size=ties.size).astype(np.int32)).view(F32)
+        x = np.concatenate([rng.uniform(lo, hi, 40000).astype(F32), ties, near,
+                            (rng.standard_normal(2000) * 1e7 * np.float64(s)).astype(F32),
+                            np.array([np.nan, np.inf, -np.inf, 0.0, -0.0], F32)])
+        got, taken = _byte_through_bits(x, s, zp)
+        with np.errstate(all="ignore"):
+            v = (np.rint((x / s).astype(F32)) + F32(zp)).astype(F32)
+        want = np.where(np.isnan(v), 0, np.clip(v, 0, 255)).astype(np.int64)
+        assert np.array_equal(got, want), f"scale {s} zero point {zp}"
+        taken_total += int(taken.sum())
+    assert taken_total > 4_000_000

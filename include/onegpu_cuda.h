@@ -269,20 +269,33 @@ OG_API og_status og_int8_gemm_encode_requantized(og_int8_gemm* gemm, og_encoder*
                                                  const og_operand* scratch);
 
 /* EncodeInt32 for callers that cannot allocate device memory. No counterpart in the reference.
- * Some callers cannot call cudaMalloc: code recording work while a CUDA graph is captured in the global capture mode
- * (where cudaMalloc is not permitted), and hosts that give all device memory to their own pool. Int8Gemm allocates
- * the scratch of the zero-point byte sums on demand; this entry point allocates nothing (no cudaMalloc, no cudaFree)
- * and keeps those sums in a fixed array of the library instead: at most 1,048,576 int32 (4 MiB, held on every GPU that
- * loads the library until exit), i.e. batchA * M (when B has a zero point) + batchB * N (when A has one); a product
- * needing more is refused with OG_ERROR_UNSUPPORTED. It runs the product on `stream` (a cudaStream_t, NULL for the
+ * Some callers cannot call cudaMalloc while they run products: serving hosts that reserve all of a GPU's memory for
+ * their own pool at start-up, engines whose execution step only hands a kernel pre-sized workspaces and forbids
+ * allocating inside it, and latency-bound loops (a decode step) that cannot afford cudaMalloc's implicit device
+ * synchronisation. Int8Gemm allocates the scratch of the zero-point byte sums on demand; this entry point allocates
+ * nothing (no cudaMalloc, no cudaFree, no allocating library call) and keeps those sums in a fixed array of the
+ * library instead: at most 1,048,576 int32 (4 MiB, held on every GPU that loads the library until exit), i.e.
+ * batchA * M (when B has a zero point) + batchB * N (when A has one); a product needing more is refused with
+ * OG_ERROR_UNSUPPORTED (capability "NoAllocScratch"). It runs the product on `stream` (a cudaStream_t, NULL for the
  * default stream) of the current device, after the same checks as og_int8_gemm_encode_int32 and with the same
- * kernels, and returns once the work is queued (a kernel-side watchdog failure is not reported here).
- * The first call on a device looks up the array's device address and sets the kernels' shared-memory limit: make that
- * first call before any stream capture. All calls share the array and it keeps the last call's contents (what must
- * start at zero is cleared on the stream before use); calls whose work overlaps on the GPU race on it. */
+ * kernels, and returns once the work is queued; a kernel whose bounded wait gave up is reported by
+ * og_int8_gemm_noalloc_status. The first call on a device (of this entry point or of the two below) looks up the
+ * array's device address (cudaGetSymbolAddress, checked) and the SM count: make that first call before any stream
+ * capture. The first product of each kernel kind on a device also sets that kernel's shared-memory limit. All calls
+ * share the array and it keeps the last call's contents (what must start at zero is cleared on the stream before
+ * use); calls whose work overlaps on the GPU (unordered streams) race on it. */
 OG_API og_status og_int8_gemm_int32_noalloc(void* stream, const og_int8_gemm_problem* problem, const og_buffer* a,
                                             const og_buffer* b, const og_buffer* c, const og_operand* zero_point_a,
                                             const og_operand* zero_point_b, const og_operand* bias);
+/* The failure word of the allocation-free products on the current device (companion of og_int8_gemm_int32_noalloc,
+ * no counterpart in the reference): waits for `stream`, then returns OG_ERROR_COMMAND_FAILED (capability "Watchdog")
+ * if a kernel of such a product gave up a bounded wait and skipped its work since the last check, clearing the word;
+ * OG_OK otherwise. Allocates nothing. */
+OG_API og_status og_int8_gemm_noalloc_status(void* stream);
+/* Queues on `stream` a kernel whose bounded wait (limit_us, 1 .. 2000000) runs out and raises the allocation-free
+ * products' failure word, the way a stalled product kernel does (no fault, nothing left in flight): tests use it to
+ * check that og_int8_gemm_noalloc_status reports such a failure. No counterpart in the reference. */
+OG_API og_status og_int8_gemm_noalloc_watchdog_selftest(void* stream, uint32_t limit_us);
 
 /* The argument checks of the three forms alone (no device needed): the same checks, in the same order, that the
  * encode functions run before recording (Int8Gemm.cs:230-253, 270-314, 336-363, 419-501). */

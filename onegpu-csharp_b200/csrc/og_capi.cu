@@ -4,11 +4,13 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <climits>
 #include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <functional>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -1319,17 +1321,22 @@ OG_API og_status og_dynamic_quantize_encode(og_dynamic_quantize* q, og_encoder* 
 
 // ---- EncodeInt32 without allocation ---------------------------------------------------------------------------------
 //
-// Some callers cannot call cudaMalloc: code that records its work while a CUDA graph is being captured in the global
-// capture mode (where cudaMalloc is not permitted), and hosts that hand all device memory to their own pool and forbid
-// any other allocation. Int8Gemm allocates (and grows) the scratch of the byte sums that the zero-point correction
-// needs on its first products, so such callers get og_int8_gemm_int32_noalloc instead: the same product, the same
-// checks, the same kernels, with the byte sums kept in a fixed array of device memory that is part of this library.
+// Some callers cannot call cudaMalloc while they run products: serving hosts that reserve all of a GPU's memory for
+// their own pool at start-up (any other allocation fails or eats into the pool), engines whose execution step only
+// hands a kernel pre-sized workspaces and forbids allocation inside it, and latency-bound loops (a decode step) that
+// cannot afford cudaMalloc's implicit device synchronisation. Int8Gemm allocates (and grows) the scratch of the byte
+// sums that the zero-point correction needs on its first products, so such callers get og_int8_gemm_int32_noalloc
+// instead: the same product, the same checks, the same kernels, with the byte sums kept in a fixed array of device
+// memory that is part of this library.
 //
 // The array holds at most kNoAllocSumElements int32 sums (row sums of A for every batch of A when B has a zero point,
 // plus column sums of B for every batch of B when A has one); larger requests are refused. Every GPU that loads the
 // library keeps the array (4 MiB) until the process exits. All calls share it and it keeps the last call's contents:
 // the column sums, which are accumulated with atomics, are cleared on the stream before each use, and calls whose
 // work overlaps on the GPU (different streams, no ordering between them) race on it.
+//
+// The kernels of these calls report a bounded wait that gave up through the word g_noalloc_status of the device,
+// not through an og_device: og_int8_gemm_noalloc_status reads it back on the caller's stream and clears it.
 
 namespace {
 
@@ -1339,16 +1346,18 @@ static __device__ __align__(256) int32_t g_noalloc_sums[kNoAllocSumElements];
 static __device__ __align__(256) int g_noalloc_status[64];
 
 struct NoAllocDevice {
-    bool ready = false;
+    std::atomic<bool> ready{false};
     int32_t* sums = nullptr;
     int* status = nullptr;
     int sm_count = 0;
 };
 
 NoAllocDevice g_noalloc[64];
+std::mutex g_noalloc_setup;
 
 // The device addresses of the arrays for the current device, looked up on the first call on that device (host code
-// may not use the symbols as addresses: they name host-side stand-ins).
+// may not use the symbols as addresses: they name host-side stand-ins). Host threads making their first call on one
+// device at once are serialised by g_noalloc_setup; the fields are published by the release store of `ready`.
 const NoAllocDevice& noalloc_device() {
     int dev = 0;
     check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
@@ -1356,15 +1365,19 @@ const NoAllocDevice& noalloc_device() {
         unsupported(kGemm, "device ordinal out of range for the allocation-free entry point", "Device", "< 64",
                     std::to_string(dev));
     NoAllocDevice& d = g_noalloc[dev];
-    if (!d.ready) {
+    if (d.ready.load(std::memory_order_acquire)) return d;
+    std::lock_guard<std::mutex> lock(g_noalloc_setup);
+    if (!d.ready.load(std::memory_order_relaxed)) {
         void* sums = nullptr;
         void* status = nullptr;
+        int sms = 0;
         check_cuda(cudaGetSymbolAddress(&sums, g_noalloc_sums), "cudaGetSymbolAddress");
         check_cuda(cudaGetSymbolAddress(&status, g_noalloc_status), "cudaGetSymbolAddress");
-        check_cuda(cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
+        check_cuda(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev), "cudaDeviceGetAttribute");
         d.sums = static_cast<int32_t*>(sums);
         d.status = static_cast<int*>(status);
-        d.ready = true;
+        d.sm_count = sms;
+        d.ready.store(true, std::memory_order_release);
     }
     return d;
 }
@@ -1442,6 +1455,36 @@ OG_API og_status og_int8_gemm_int32_noalloc(void* stream, const og_int8_gemm_pro
                        "og_int8_gemm_int32_noalloc");
         }
         check_cuda(og::launch_gemm_tc(L, s), "og_int8_gemm_int32_noalloc");
+    });
+}
+
+OG_API og_status og_int8_gemm_noalloc_status(void* stream) {
+    return guard([&] {
+        const NoAllocDevice& d = noalloc_device();
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        int word = 0;  // pageable host memory: the copy lands before cudaStreamSynchronize returns
+        check_cuda(cudaMemcpyAsync(&word, d.status, sizeof(int), cudaMemcpyDeviceToHost, s), "status readback");
+        check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+        if (word != 0) {
+            check_cuda(cudaMemsetAsync(d.status, 0, sizeof(int), s), "status reset");
+            check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+            throw OgError{OG_ERROR_COMMAND_FAILED, kGemm, "",
+                          "a kernel of an allocation-free product gave up waiting on its own pipeline (watchdog) and "
+                          "skipped its work",
+                          "Watchdog", "", ""};
+        }
+    });
+}
+
+OG_API og_status og_int8_gemm_noalloc_watchdog_selftest(void* stream, uint32_t limit_us) {
+    return guard([&] {
+        if (limit_us < 1 || limit_us > 2000000)
+            throw OgError{OG_ERROR_ARGUMENT_RANGE, kGemm, "limitMicroseconds",
+                          "the self-test wait limit is 1 .. 2000000 microseconds", "", "", ""};
+        const NoAllocDevice& d = noalloc_device();
+        og::watchdog_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(d.status,
+                                                                                     uint64_t(limit_us) * 1000);
+        check_cuda(cudaGetLastError(), "watchdog self-test launch");
     });
 }
 

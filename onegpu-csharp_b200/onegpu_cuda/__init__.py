@@ -132,6 +132,8 @@ EXPORTS = {
     "og_int8_gemm_encode_dequantize": [_P, _P, _PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD, _OPD, _OPD, _OPD],
     "og_int8_gemm_check_dequantize": [_PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD, _OPD, _OPD, _OPD],
     "og_int8_gemm_int32_noalloc": [_P, _PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD],
+    "og_int8_gemm_noalloc_status": [_P],
+    "og_int8_gemm_noalloc_watchdog_selftest": [_P, ctypes.c_uint32],
     "og_int8_gemm_check_int32": [_PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD],
     "og_int8_gemm_check_float": [_PROB, _BUF, _BUF, _BUF, _OPD, _OPD, _OPD, _OPD, _OPD],
     "og_int8_gemm_check_requantized": [_PROB, _BUF, _BUF, _BUF, _OPD, ctypes.c_int32, _OPD, _OPD, _OPD, _OPD],
@@ -673,12 +675,26 @@ def buffer_spec(dtype, length: int, null: bool = False) -> _BufferSpec:
 
 
 def int8_gemm_int32_noalloc(stream: int, problem, a, b, c, zero_point_a=None, zero_point_b=None, bias=None) -> None:
-    """EncodeInt32 for callers that cannot allocate device memory (og_int8_gemm_int32_noalloc): queues the product on
-    `stream` of the current device, keeping the zero-point byte sums in the library's fixed array instead of
-    allocated scratch. No counterpart in the reference."""
+    """EncodeInt32 for callers that cannot allocate device memory while they run products (a host whose pool owns
+    the GPU's memory, an engine step that forbids allocation, a latency-bound loop): og_int8_gemm_int32_noalloc
+    queues the product on `stream` of the current device, keeping the zero-point byte sums in the library's fixed
+    array (at most 1,048,576 int32) instead of allocated scratch. No counterpart in the reference."""
     p = problem.c_struct()
     _check(_lib.og_int8_gemm_int32_noalloc(ctypes.c_void_p(stream), ctypes.byref(p), _buf(a), _buf(b), _buf(c),
                                            _opd(zero_point_a), _opd(zero_point_b), _opd(bias)))
+
+
+def int8_gemm_noalloc_status(stream: int) -> None:
+    """Waits for `stream` and raises GpuCommandFailedException (reason "Watchdog") if a kernel of an allocation-free
+    product on the current device gave up a bounded wait since the last check (og_int8_gemm_noalloc_status); the
+    failure word is cleared."""
+    _check(_lib.og_int8_gemm_noalloc_status(ctypes.c_void_p(stream)))
+
+
+def int8_gemm_noalloc_watchdog_selftest(stream: int, limit_us: int) -> None:
+    """Queues a kernel whose bounded wait runs out after `limit_us` and raises the allocation-free products' failure
+    word, with no fault (og_int8_gemm_noalloc_watchdog_selftest)."""
+    _check(_lib.og_int8_gemm_noalloc_watchdog_selftest(ctypes.c_void_p(stream), int(limit_us)))
 
 
 def check_int32(problem, a, b, c, zero_point_a=None, zero_point_b=None, bias=None) -> None:

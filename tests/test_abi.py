@@ -29,10 +29,13 @@ def test_every_declared_entry_point_is_exported():
     assert sorted(og.EXPORTS) == names
 
 
+CSHARP = os.path.join(os.path.dirname(HEADER), "..", "onegpu-csharp_b200", "csharp", "RecursiveAI.OneGpu.Cuda")
+
+
 def test_every_entry_point_has_a_csharp_binding():
-    """INTEGRATION.md's P/Invoke block declares each entry point the header declares, and nothing else."""
-    doc = open(os.path.join(os.path.dirname(HEADER), "..", "INTEGRATION.md"), encoding="utf-8").read()
-    bound = sorted(set(re.findall(r"\[LibraryImport\(Lib\)\][^;]*?\b(og_\w+)\s*\(", doc)))
+    """The C# P/Invoke declarations (Native.cs) bind each entry point the header declares, and nothing else."""
+    src = open(os.path.join(CSHARP, "Native.cs"), encoding="utf-8").read()
+    bound = sorted(set(re.findall(r"\[LibraryImport\(Lib\)\][^;]*?\b(og_\w+)\s*\(", src)))
     assert bound == declared_symbols()
 
 

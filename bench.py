@@ -1,18 +1,21 @@
 """Benchmark of the int8 GEMM path (BASELINE.json metric: Int8Gemm TOPS at 8192^3 s8 x s8 -> s32).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c3|c2|c4|c5|conv|dequant|quant]
-                    [--impl ours|reference]
+                    [--impl ours|reference] [--no-extra]
 
 One step is one Int8Gemm.EncodeInt32 + Submit of the workload (config 3 by default: A int8 [8192 x 8192] x B int8
 [8192 x 8192], zero points absent, int32 C) with inputs resident in HBM; L2 is left cold and clean before every step
 (a 512 MB write, then a 256 MB read of other data, stream-ordered) and the step itself is timed with CUDA events on
-the device stream. With N > 1 (torchrun, one process per GPU,
-NCCL only for the barrier and the max-over-ranks of the times) the product is sharded by onegpu_cuda.shard with no
-collective in the data path ("strong" scaling: the total work is fixed): a batched workload by batch (rank g computes
+the device stream. With N > 1 (torchrun, one process per GPU) the product is sharded by onegpu_cuda.shard with no
+collective in its data path ("strong" scaling: the total work is fixed): a batched workload by batch (rank g computes
 its batches from its batches of A and the shared B), the others by 256-column slabs of B (rank g computes its columns
-from the full A and its slab of B). `e2e` runs the same product through the C ABI from pinned host buffers (uploads of A and the B
-slab, the product, readback of C), timed on the device. `--impl reference` times the CPU restatement of the
-reference's int8 product (oracle/, all host threads) on a bounded row sample of the same workload.
+from the full A and its slab of B); times are the max over ranks. The default line also carries, measured in the
+same run at the same N, config 5 (`c5`: decode, N-sharded, GB/s against HBM) and config 4 (`c4`: batched QKV,
+batch-sharded), and at N > 1 the gather of the sharded result onto rank 0 over NVLink (`gather`, og_comm_gather_columns,
+outside `value`). `e2e` runs the same product through the C ABI from pinned host buffers (uploads of the step's inputs
+- at N > 1 each rank only its 1/N of the replicated operand, all-gathered over NVLink -, the product, readback of the
+rank's result), pipelined over two buffer sets. `--impl reference` times the CPU restatement of the reference's int8
+product (oracle/, all host threads) on a bounded row sample of the same workload.
 """
 from __future__ import annotations
 
@@ -35,16 +38,19 @@ sys.path.insert(0, os.path.join(ROOT, "onegpu-csharp_b200"))
 METRIC = "Int8Gemm TOPS at 8192³ s8×s8→s32, % int8 tensor peak, 1/2/4/8 B200"
 
 WORKLOADS = {
-    # name: (M, N, K, batch, a_signed, za, zb, out, description)
-    "c3": dict(m=8192, n=8192, k=8192, batch=1, a_signed=True, zp=False, out="i32",
-               desc="square s8 x s8 -> s32, 8192^3, zero points absent"),
-    "c2": dict(m=4096, n=4096, k=4096, batch=1, a_signed=False, zp=True, out="f32", dql=True,
-               desc="DynamicQuantizeLinear of f32 [4096 x 4096] ~ N(0,1) to u8, then u8 x s8 (per-column zp) -> f32 "
-                    "dequantized by a_scale * b_scale[col], 4096^3; one step = both"),
-    "c4": dict(m=2048, n=12288, k=4096, batch=8, a_signed=False, zp=True, out="i32",
-               desc="batched QKV u8 (zp) x shared s8 (per-column zp) -> s32, 8 x 2048 x 12288 x 4096"),
-    "c5": dict(m=16, n=28672, k=8192, batch=1, a_signed=False, zp=True, out="i32",
-               desc="decode u8 (zp 128) x s8 (per-column zp) -> s32, 16 x 28672 x 8192"),
+    # a: how A is made (s8 / u8 uniform bytes, or DynamicQuantizeLinear of N(0, sigma) floats); zb: the range of the
+    # per-column zero points of B (None: no zero points); out: i32 sums, or f32 dequantized by a_scale * b_scale[col]
+    "c3": dict(m=8192, n=8192, k=8192, batch=1, a="s8", zb=None, b_lo=-128, out="i32",
+               desc="square s8 x s8 -> s32, 8192^3, both operands uniform -128..127, zero points absent"),
+    "c2": dict(m=4096, n=4096, k=4096, batch=1, a="dql", sigma=1.0, zb=8, b_lo=-127, out="f32", dql_in_step=True,
+               desc="DynamicQuantizeLinear of f32 [4096 x 4096] ~ N(0,1) to u8, then u8 x s8 (per-column zp -8..8) -> "
+                    "f32 dequantized by a_scale * b_scale[col], 4096^3; one step = both"),
+    "c4": dict(m=2048, n=12288, k=4096, batch=8, a="dql", sigma=0.5, zb=8, b_lo=-127, out="i32",
+               desc="batched QKV: u8 A = DynamicQuantizeLinear of N(0, 0.5) over the whole [8, 2048, 4096] tensor (its "
+                    "zero point) x shared s8 B [4096 x 12288] -127..127 (per-column zp -8..8) -> s32"),
+    "c5": dict(m=16, n=28672, k=8192, batch=1, a="u8", za=128, zb=4, b_lo=-127, out="f32",
+               desc="decode: u8 A [16 x 8192] (zp 128) x s8 B [8192 x 28672] -127..127 (per-column zp -4..4), int32 "
+                    "sums dequantized to f32 by a_scale 0.02 * b_scale[col] (0.001..0.02) in the product's epilogue"),
 }
 
 # The other kernel families of the path (not BASELINE configs): measured the same way, one JSON line each.
@@ -100,7 +106,7 @@ def nvml_index(local_rank: int):
 
 
 class ClockSampler:
-    """SM clock, power and clock-event (throttle) reasons of one GPU, read through NVML every 20 ms while the timed
+    """SM clock, power and clock-event (throttle) reasons of one GPU, read through NVML every 5 ms while the timed
     region runs (read-only queries; nothing is set)."""
 
     REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4,
@@ -141,7 +147,7 @@ class ClockSampler:
                 self.samples.append((mhz, watts, reasons))
             except Exception:  # noqa: BLE001
                 pass
-            time.sleep(0.02)
+            time.sleep(0.005)
 
     def __exit__(self, *exc):
         self.stop.set()
@@ -477,8 +483,8 @@ def run_reference(args, rank: int, world: int):
     line = {"metric": METRIC, "impl": "reference", "value": round(tops, 6), "unit": "TOPS", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(full_ms, 3), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": f"{args.workload}: {w['desc']}", "parallelism": "host threads",
-                       "sample": sample},
+            "config": {"workload": f"{args.workload}: {w['desc']}", "m": w["m"], "n": w["n"], "k": w["k"],
+                       "batch": w["batch"], "parallelism": "host threads", "sample": sample},
             "cpu_baseline": {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(tops, 6), "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -488,96 +494,178 @@ def run_reference(args, rank: int, world: int):
 REFERENCE_SECONDS = 120.0  # the reference arm's timed steps together, whatever --steps is
 
 
-def run_ours(args, rank: int, world: int, local_rank: int, dist):
-    import onegpu_cuda as og
+class Workload:
+    """One rank's part of a BASELINE config, resident in HBM: its shard of the operands (batched products by batch with
+    B shared; the others by 256-column slabs of B, A replicated), the output, and how to record one step."""
 
-    from onegpu_cuda import shard as sh
-
-    w = WORKLOADS[args.workload]
-    dev = og.GpuDevice(local_rank)
-    M, N, K, B = w["m"], w["n"], w["k"], w["batch"]
-    # Batched products are split by batch (B shared), the others by 256-column slabs of B.
-    by_batch = B > 1
-    extent, align = (B, 1) if by_batch else (N, sh.TILE_COLUMNS)
-    if min(s.width for s in sh.split(extent, world, align)) == 0:  # decided alike on every rank
-        raise SystemExit(f"{args.workload} has fewer shards than the {world} ranks")
-    part = sh.shard_of(extent, world, rank, align)
-    shard_n = N if by_batch else part.width
-    B_local = part.width if by_batch else B
-    rng = np.random.default_rng(1234)
-    a_dtype = np.int8 if w["a_signed"] else np.uint8
-    # Synthetic inputs with the config's distributions, generated on the host once (each rank draws the whole
-    # operands from the same seed and keeps its shard).
-    a_full = rng.integers(-128 if w["a_signed"] else 0, 128 if w["a_signed"] else 256, size=(B, M, K),
-                          dtype=np.int16).astype(a_dtype)
-    a_host = (sh.batch_slab(a_full, part) if by_batch else a_full).reshape(-1)
-    del a_full
-    b_full_cols = rng.integers(-128 if args.workload == "c3" else -127, 128, size=(K, N), dtype=np.int16)
-    b_host = (b_full_cols if by_batch else sh.column_slab(b_full_cols, part)).astype(np.int8).reshape(-1)
-    del b_full_cols
-    a = dev.create_buffer(a_dtype, a_host)
-    b = dev.create_buffer(np.int8, b_host)
-    count = B_local * M * shard_n
-    out_dtype = {"i32": np.int32, "f32": np.float32}[w["out"]]
-    c = dev.create_buffer(out_dtype, count)
-    zpa = zpb = scale = None
-    extra = []
-    if w["zp"]:
-        za = dev.create_buffer(a_dtype, np.array([128 if not w["a_signed"] else 0], a_dtype))
-        zb = dev.create_buffer(np.int8, rng.integers(-8, 9, size=shard_n).astype(np.int8))
-        zpa, zpb = og.Int8Operand(za, 0), og.Int8Operand(zb, 0, True)
-        extra += [za, zb]
-    dq = x_dev = None
-    if w.get("dql"):
-        # Config 2: the activations arrive as float32 ~ N(0, 1); DynamicQuantizeLinear turns them into A (u8) with a
-        # scale and zero point on the device, and the product dequantizes with a_scale * b_scale[col].
-        x_host = rng.standard_normal(size=M * K, dtype=np.float32)
-        x_dev = dev.create_buffer(np.float32, x_host)
-        a_scale = dev.create_buffer(np.float32, 1)
-        za = dev.create_buffer(np.uint8, 1)
-        zb = dev.create_buffer(np.int8, rng.integers(-8, 9, size=shard_n).astype(np.int8))
-        b_scale = dev.create_buffer(np.float32, rng.uniform(0.001, 0.02, size=shard_n).astype(np.float32))
-        zpa, zpb = og.Int8Operand(za, 0), og.Int8Operand(zb, 0, True)
-        dq = og.DynamicQuantizeKernels(dev)
-        extra += [x_dev, a_scale, za, zb, b_scale]
-        a_host = x_host  # what the e2e leg uploads
-    elif w["out"] == "f32":
-        s = dev.create_buffer(np.float32, rng.uniform(0.001, 0.02, size=shard_n).astype(np.float32) * 0.02)
-        scale = og.Int8Operand(s, 0, True)
-        extra.append(s)
-    flush = L2Flush(dev, local_rank)
-    prob = og.Int8GemmProblem(M, shard_n, K, batch=B_local, stride_a=M * K if B_local > 1 else 0, stride_b=0)
-    gemm = og.Int8Gemm(dev)
-
-    def encode(enc, a=a, b=b, c=c, x_dev=x_dev):
-        if dq is not None:
-            dq.encode(enc, x_dev, 0, M * K, a, 0, a_scale, 0, za, 0)
-            gemm.encode_dequantize(enc, prob, a, b, c, og.Int8Operand(a_scale, 0), og.Int8Operand(b_scale, 0, True),
-                                   zpa, zpb)
-        elif w["out"] == "f32":
-            gemm.encode_float(enc, prob, a, b, c, scale, zpa, zpb)
+    def __init__(self, og, sh, dev, name: str, world: int, rank: int, seed: int = 1234):
+        w = WORKLOADS[name]
+        self.name, self.w = name, w
+        self.M, self.N, self.K, self.B = M, N, K, B = w["m"], w["n"], w["k"], w["batch"]
+        self.by_batch = B > 1
+        extent, align = (B, 1) if self.by_batch else (N, sh.TILE_COLUMNS)
+        self.shards = sh.split(extent, world, align)
+        if min(s.width for s in self.shards) == 0:  # decided alike on every rank
+            raise SystemExit(f"{name} has fewer shards than the {world} ranks")
+        self.part = part = self.shards[rank]
+        self.shard_n = N if self.by_batch else part.width
+        self.B_local = part.width if self.by_batch else B
+        self.dev = dev
+        rng = np.random.default_rng(seed)
+        self.bufs, self.extra = {}, []
+        self.dq = None
+        a_kind = w["a"]
+        self.a_dtype = np.int8 if a_kind == "s8" else np.uint8
+        # B (K x N, row-major): every rank draws the whole operand from one seed and keeps its shard.
+        b_full = rng.integers(w["b_lo"], 128, size=(K, N), dtype=np.int16)
+        self.b_host = (b_full if self.by_batch else sh.column_slab(b_full, part)).astype(np.int8).reshape(-1)
+        del b_full
+        self.bufs["b"] = dev.create_buffer(np.int8, self.b_host)
+        zp = None
+        if a_kind == "dql":
+            # float activations ~ N(0, sigma) quantized by this library's DynamicQuantizeLinear over the whole tensor
+            x = (rng.standard_normal(size=B * M * K, dtype=np.float32) * np.float32(w["sigma"]))
+            self.x_host = x
+            self.bufs["x"] = dev.create_buffer(np.float32, x)
+            self.bufs["a"] = dev.create_buffer(np.uint8, B * M * K)
+            self.a_scale = dev.create_buffer(np.float32, 1)
+            self.za = dev.create_buffer(np.uint8, 4)
+            self.extra += [self.a_scale, self.za]
+            self.dq = og.DynamicQuantizeKernels(dev)
+            enc = dev.begin_commands()
+            self.dq.encode(enc, self.bufs["x"], 0, B * M * K, self.bufs["a"], 0, self.a_scale, 0, self.za, 0)
+            dev.submit(enc)
+            dev.wait_idle()
+            self.a_zero_point = int(self.za.read()[0])
+            if not w.get("dql_in_step"):
+                self.a_host = self.bufs["a"].read()  # what the e2e leg uploads
+                if self.by_batch:
+                    self.a_host = self.a_host.reshape(B, M * K)[part.start:part.stop].reshape(-1)
+                    self.bufs["a"].dispose()
+                    self.bufs["a"] = dev.create_buffer(np.uint8, self.a_host)
+                self.bufs["x"].dispose()
+                del self.bufs["x"]
+                self.x_host = None
         else:
-            gemm.encode_int32(enc, prob, a, b, c, zpa, zpb)
+            lo, hi = (-128, 128) if a_kind == "s8" else (0, 256)
+            a_full = rng.integers(lo, hi, size=(B, M, K), dtype=np.int16).astype(self.a_dtype)
+            self.a_host = (sh.batch_slab(a_full, part) if self.by_batch else a_full).reshape(-1)
+            del a_full
+            self.bufs["a"] = dev.create_buffer(self.a_dtype, self.a_host)
+            self.x_host = None
+            if "za" in w:
+                self.za = dev.create_buffer(np.uint8, np.array([w["za"], 0, 0, 0], np.uint8))
+                self.extra.append(self.za)
+                self.a_zero_point = w["za"]
+        self.zpa = og.Int8Operand(self.za, 0) if (a_kind == "dql" or "za" in w) else None
+        self.zpb = None
+        if w["zb"] is not None:
+            zb_full = rng.integers(-w["zb"], w["zb"] + 1, size=N).astype(np.int8)
+            zb = zb_full if self.by_batch else sh.column_vector(zb_full, part)
+            self.zb = dev.create_buffer(np.int8, zb)
+            self.extra.append(self.zb)
+            self.zpb = og.Int8Operand(self.zb, 0, True)
+        self.count = self.B_local * M * self.shard_n
+        self.out_dtype = np.float32 if w["out"] == "f32" else np.int32
+        self.bufs["c"] = dev.create_buffer(self.out_dtype, self.count)
+        if w["out"] == "f32":
+            if a_kind != "dql":
+                self.a_scale = dev.create_buffer(np.float32, np.array([0.02], np.float32))
+                self.extra.append(self.a_scale)
+            bs_full = rng.uniform(0.001, 0.02, size=N).astype(np.float32)
+            self.b_scale = dev.create_buffer(np.float32, bs_full if self.by_batch else sh.column_vector(bs_full, part))
+            self.extra.append(self.b_scale)
+        self.problem = og.Int8GemmProblem(M, self.shard_n, K, batch=self.B_local,
+                                          stride_a=M * K if self.B_local > 1 else 0, stride_b=0)
+        self.gemm = og.Int8Gemm(dev)
+        self.og = og
+        self.ops_total = 2.0 * B * M * N * K
+        self.ops_shard = 2.0 * self.B_local * M * self.shard_n * K
+        # Bytes one launch must move at least: A, the B slab, C, and the zero-point / scale vectors (plus, for the
+        # config-2 step, x read and A written by DynamicQuantizeLinear and read again by the product).
+        self.algo_bytes = (self.B_local * M * K + K * self.shard_n + self.count * np.dtype(self.out_dtype).itemsize
+                           + (self.shard_n if w["zb"] is not None else 0)
+                           + (4 * self.shard_n if w["out"] == "f32" else 0)
+                           + (4 * M * K + 2 * M * K if w.get("dql_in_step") else 0))
 
-    stamps = og.GpuTimestampSet(dev, 2 * args.steps)
+    @property
+    def first_host(self):
+        """What a step's upload starts with: x for the config-2 chain, A otherwise."""
+        return self.x_host if self.w.get("dql_in_step") else self.a_host
+
+    def encode(self, enc, a=None, b=None, c=None, x=None):
+        og = self.og
+        a = a or self.bufs["a"]
+        b = b or self.bufs["b"]
+        c = c or self.bufs["c"]
+        if self.w.get("dql_in_step"):
+            self.dq.encode(enc, x or self.bufs["x"], 0, self.M * self.K, a, 0, self.a_scale, 0, self.za, 0)
+        if self.w["out"] == "f32":
+            self.gemm.encode_dequantize(enc, self.problem, a, b, c, og.Int8Operand(self.a_scale, 0),
+                                        og.Int8Operand(self.b_scale, 0, True), self.zpa, self.zpb)
+        else:
+            self.gemm.encode_int32(enc, self.problem, a, b, c, self.zpa, self.zpb)
+
+    def dispose(self):
+        for v in list(self.bufs.values()) + self.extra:
+            v.dispose()
+        if self.dq is not None:
+            self.dq.dispose()
+        self.gemm.dispose()
+
+
+def timed_steps(dev, og, flush, wl: Workload, steps: int, warmup: int, barrier=None):
+    """Runs `warmup` untimed and `steps` timed steps (L2 flushed before each, CUDA events around the step on the
+    device stream); returns the per-step nanoseconds and the number of kernel launches recorded in the timed steps."""
+    stamps = og.GpuTimestampSet(dev, 2 * steps)
 
     def step(i=None):
         flush(i if i is not None else 0)
         enc = dev.begin_commands()
         if i is not None:
             enc.write_timestamp(stamps, 2 * i)
-        encode(enc)
+        wl.encode(enc)
         if i is not None:
             enc.write_timestamp(stamps, 2 * i + 1)
-        launches = enc.dispatch_count
+        n = enc.dispatch_count
         dev.submit(enc)
-        return launches
+        return n
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     dev.wait_idle()
-    kernel = gemm.last_kernel
+    if barrier is not None:
+        barrier()
     launches = 0
+    t0 = time.perf_counter()
+    for i in range(steps):
+        launches += step(i)
+    dev.wait_idle()
+    wall = time.perf_counter() - t0
+    if barrier is not None:
+        barrier()
+    ts = stamps.read(0)
+    stamps.dispose()
+    return [ts[2 * i + 1] - ts[2 * i] for i in range(steps)], launches, wall
+
+
+def roofline_peaks(clk: dict, sustained_time: bool):
+    """The int8 tensor denominator: twice the measured dense bf16 rate, the sustained figure when the run's own clock
+    record shows the power cap (or the timed region is long enough to reach it), the burst figure otherwise."""
+    peaks = load_peaks()
+    capped = "sw_power_cap" in (clk.get("reasons") or [])
+    sustained = capped or sustained_time
+    burst, sust = 2.0 * peaks["bf16_tflops"], 2.0 * peaks["bf16_tflops_sustained"]
+    return peaks, (sust if sustained else burst), ("sustained" if sustained else "burst"), burst, sust, capped
+
+
+def run_ours(args, rank: int, world: int, local_rank: int, dist):
+    import onegpu_cuda as og
+
+    from onegpu_cuda import shard as sh
+
+    dev = og.GpuDevice(local_rank)
+    flush = L2Flush(dev, local_rank)
 
     def barrier():
         if dist is not None:
@@ -585,16 +673,10 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
             dist.barrier(device_ids=[local_rank])
             torch.cuda.synchronize(local_rank)
 
-    barrier()
+    wl = Workload(og, sh, dev, args.workload, world, rank)
     with ClockSampler(local_rank) as clocks:
-        t0 = time.perf_counter()
-        for i in range(args.steps):
-            launches += step(i)
-        dev.wait_idle()
-        wall = time.perf_counter() - t0
-    barrier()
-    ts = stamps.read(0)
-    per_step_ns = [ts[2 * i + 1] - ts[2 * i] for i in range(args.steps)]
+        per_step_ns, launches, wall = timed_steps(dev, og, flush, wl, args.steps, args.warmup, barrier)
+    kernel, variant = wl.gemm.last_kernel, wl.gemm.variant
     gemm_ns = sum(per_step_ns)
 
     # Decode also as a CUDA graph: the step (the product alone) captured once and replayed back to back. B (235 MB)
@@ -604,7 +686,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         replays = 200
         dev.capture_begin()
         genc = dev.begin_commands()
-        encode(genc)
+        wl.encode(genc)
         dev.submit(genc)
         graph = dev.capture_end()
         gstamps = og.GpuTimestampSet(dev, 2)
@@ -620,31 +702,83 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         graph.dispose()
         gstamps.dispose()
 
+    # Communicator for N > 1 (NCCL over NVLink): the id made on rank 0 and handed out through the process group.
+    comm = None
+    if dist is not None:
+        box = [og.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        comm = og.Communicator(dev, world, rank, box[0])
+
+    # The gather of the sharded result onto rank 0 over NVLink, timed apart from `value` (every rank takes part).
+    gather = None
+    if comm is not None:
+        full = dev.create_buffer(wl.out_dtype, wl.B * wl.M * wl.N) if rank == 0 else None
+        esize = np.dtype(wl.out_dtype).itemsize
+        if wl.by_batch:  # batch shards are contiguous: one row of each rank's whole shard
+            widths, gb, gm = [s.width * wl.M * wl.N for s in wl.shards], 1, 1
+        else:
+            widths, gb, gm = [s.width for s in wl.shards], wl.B, wl.M
+        gst = og.GpuTimestampSet(dev, 2 * 6)
+        for i in range(-2, 6):
+            if i >= 0:
+                dev.timestamp(gst, 2 * i)
+            comm.gather_columns(wl.bufs["c"].ptr, esize, gb, gm, widths, full.ptr if full is not None else 0, 0)
+            if i >= 0:
+                dev.timestamp(gst, 2 * i + 1)
+        gts = gst.read(0)
+        gst.dispose()
+        g_ns = statistics.median(gts[2 * i + 1] - gts[2 * i] for i in range(6))
+        if full is not None:
+            full.dispose()
+        received = (wl.B * wl.M * wl.N - wl.count) * esize
+        gather = {"ns": g_ns, "bytes_into_root": int(received)}
+
     # e2e through the C ABI from page-locked host memory, pipelined over two sets of device buffers: every step
-    # uploads its inputs (A and the B slab; x for c2) on the copy engine, runs the product, and reads its whole result
-    # back, while the next step's upload and the previous step's readback overlap it. Timed by the host clock from the
-    # first upload to the last readback.
-    first_host = x_host if dq is not None else a_host
-    h2d = first_host.nbytes + b_host.nbytes
-    d2h = count * np.dtype(out_dtype).itemsize
-    pin_in = og.PinnedHost(h2d)
+    # uploads its inputs on the copy engine (at N > 1 each rank only its 1/N of the replicated operand, which the
+    # ranks then all-gather over NVLink), runs the product, and reads its shard of the result back, while the next
+    # step's upload and the previous step's readback overlap it. Timed by the host clock from the first upload to
+    # the last readback; the max over ranks.
+    first_host, b_host = wl.first_host, wl.b_host
+    # A replicated (column shards) or B replicated (batch shards): each rank uploads its rows of it.
+    split_a = comm is not None and not wl.by_batch and first_host.nbytes % world == 0
+    split_b = comm is not None and wl.by_batch and b_host.nbytes % world == 0
+    up_first = first_host.nbytes // world if split_a else first_host.nbytes
+    up_b = b_host.nbytes // world if split_b else b_host.nbytes
+    h2d = up_first + up_b
+    d2h = wl.count * np.dtype(wl.out_dtype).itemsize
+    pin_in = og.PinnedHost(up_first + up_b)
     pin_out = og.PinnedHost(2 * d2h)
-    pin_in.view(np.uint8, first_host.nbytes)[:] = first_host.view(np.uint8)
-    pin_in.view(np.uint8, b_host.nbytes, first_host.nbytes)[:] = b_host.view(np.uint8)
-    spare = dict(a=dev.create_buffer(a_dtype, B_local * M * K), b=dev.create_buffer(np.int8, b_host.size),
-                 c=dev.create_buffer(out_dtype, count),
-                 x_dev=dev.create_buffer(np.float32, M * K) if dq is not None else None)
-    sets = [dict(a=a, b=b, c=c, x_dev=x_dev), spare]
+    fv = first_host.view(np.uint8)
+    bv = b_host.view(np.uint8)
+    pin_in.view(np.uint8, up_first)[:] = fv[rank * up_first:(rank + 1) * up_first] if split_a else fv
+    pin_in.view(np.uint8, up_b, up_first)[:] = bv[rank * up_b:(rank + 1) * up_b] if split_b else bv
+    first_key = "x" if wl.w.get("dql_in_step") else "a"
+    first_dtype = np.float32 if first_key == "x" else wl.a_dtype
+    spare = dict(a=dev.create_buffer(wl.a_dtype, wl.bufs["a"].length), b=dev.create_buffer(np.int8, b_host.size),
+                 c=dev.create_buffer(wl.out_dtype, wl.count))
+    if first_key == "x":
+        spare["x"] = dev.create_buffer(np.float32, wl.bufs["x"].length)
+    part_first = [dev.create_buffer(np.uint8, up_first) for _ in range(2)] if split_a else None
+    part_b = [dev.create_buffer(np.uint8, up_b) for _ in range(2)] if split_b else None
+    sets = [dict(wl.bufs), spare]
 
     def e2e_step(i, tickets):
         bs = sets[i % 2]
         if len(tickets) >= 2:
             tickets[-2].wait()  # the step that last used this buffer set has been read back, so it has finished
-        dst_first = bs["x_dev"] if dq is not None else bs["a"]
-        dev.write_async(dst_first.ptr, pin_in.ptr, first_host.nbytes)
-        dev.write_async(bs["b"].ptr, pin_in.ptr + first_host.nbytes, b_host.nbytes)
+        dst_first = bs[first_key]
+        if split_a:
+            dev.write_async(part_first[i % 2].ptr, pin_in.ptr, up_first)
+            comm.all_gather(part_first[i % 2].ptr, up_first, dst_first.ptr)
+        else:
+            dev.write_async(dst_first.ptr, pin_in.ptr, up_first)
+        if split_b:
+            dev.write_async(part_b[i % 2].ptr, pin_in.ptr + up_first, up_b)
+            comm.all_gather(part_b[i % 2].ptr, up_b, bs["b"].ptr)
+        else:
+            dev.write_async(bs["b"].ptr, pin_in.ptr + up_first, up_b)
         enc = dev.begin_commands()
-        encode(enc, **bs)
+        wl.encode(enc, **{k: v for k, v in bs.items() if k in ("a", "b", "c", "x")})
         dev.submit(enc)
         tickets.append(dev.read_async(pin_out.ptr + (i % 2) * d2h, bs["c"].ptr, d2h))
 
@@ -653,6 +787,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         e2e_step(i, tickets)
     for t in tickets[-2:]:
         t.wait()
+    barrier()
     tickets = []
     e2e_steps = min(args.steps, 20)
     t0 = time.perf_counter()
@@ -661,19 +796,19 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
     for t in tickets[-2:]:
         t.wait()
     e2e_ns = (time.perf_counter() - t0) * 1e9 / e2e_steps * args.steps
+    barrier()
     pin_in.dispose()
     pin_out.dispose()
-    for v in spare.values():
-        if v is not None:
-            v.dispose()
+    for v in list(spare.values()) + (part_first or []) + (part_b or []):
+        v.dispose()
 
     # cuBLAS (torch._int_mm) on the same shard for context: library int8 throughput on this GPU.
     lib_tops = None
     if args.workload == "c3" and not args.no_library:
         try:
             import torch
-            ta = torch.from_numpy(a_host.reshape(M, K)).cuda(local_rank)
-            tb = torch.from_numpy(b_host.reshape(K, shard_n)).cuda(local_rank)
+            ta = torch.from_numpy(wl.a_host.reshape(wl.M, wl.K)).cuda(local_rank)
+            tb = torch.from_numpy(wl.b_host.reshape(wl.K, wl.shard_n)).cuda(local_rank)
             for _ in range(3):
                 torch._int_mm(ta, tb)
             torch.cuda.synchronize(local_rank)
@@ -683,82 +818,121 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
                 torch._int_mm(ta, tb)
             e1.record()
             torch.cuda.synchronize(local_rank)
-            lib_tops = 2.0 * M * shard_n * K * 5 / (e0.elapsed_time(e1) * 1e-3) / 1e12
+            lib_tops = 2.0 * wl.M * wl.shard_n * wl.K * 5 / (e0.elapsed_time(e1) * 1e-3) / 1e12
             del ta, tb
         except Exception as exc:  # noqa: BLE001 - context only
             lib_tops = f"unavailable: {type(exc).__name__}"
 
-    if dist is not None:
-        gemm_ns, e2e_ns = sh.max_over_ranks(dist, [gemm_ns, e2e_ns], device=f"cuda:{local_rank}")
+    # The other multi-GPU configs at this N, measured in the same run (a few steps each): config 5 (decode,
+    # N-sharded, HBM-bound) and config 4 (batched QKV, batch-sharded).
+    subs = {}
+    if args.workload == "c3" and not args.no_extra:
+        for name in ("c5", "c4"):
+            sub = Workload(og, sh, dev, name, world, rank, seed=4321)
+            ns, sub_launches, _ = timed_steps(dev, og, flush, sub, min(args.steps, 20), 3, barrier)
+            subs[name] = dict(ns=statistics.mean(ns), total=sum(ns), steps=len(ns), kernel=sub.gemm.last_kernel,
+                              ops_total=sub.ops_total, ops_shard=sub.ops_shard, algo_bytes=sub.algo_bytes,
+                              launches=sub_launches, desc=sub.w["desc"],
+                              parallelism=("batch" if sub.by_batch else "N") + f"-shard x{world}")
+            sub.dispose()
 
-    total_ops = 2.0 * B * M * N * K
+    wl.dispose()
+    # Max over ranks of every time (the slowest rank sets the step).
+    keys = ["gemm", "e2e"] + (["gather"] if gather else []) + [f"{k}_total" for k in subs] + [f"{k}_ns" for k in subs]
+    vals = [gemm_ns, e2e_ns] + ([gather["ns"]] if gather else []) + [subs[k]["total"] for k in subs] + \
+           [subs[k]["ns"] for k in subs]
+    if dist is not None:
+        vals = sh.max_over_ranks(dist, vals, device=f"cuda:{local_rank}")
+    mx = dict(zip(keys, vals))
+    gemm_ns, e2e_ns = mx["gemm"], mx["e2e"]
+
     ms_per_step = gemm_ns / args.steps / 1e6
-    value = total_ops / (ms_per_step * 1e-3) / 1e12
+    value = wl.ops_total / (ms_per_step * 1e-3) / 1e12
     per_launch_s = statistics.mean(per_step_ns) * 1e-9
-    shard_ops = 2.0 * B_local * M * shard_n * K
-    achieved = shard_ops / per_launch_s / 1e12
-    # Bytes one launch must move at least: A, the B slab, C, and the zero-point / scale vectors.
-    algo_bytes = (a_host.nbytes + b_host.nbytes + count * np.dtype(out_dtype).itemsize
-                  + (shard_n + 1 if w["zp"] else 0) + (4 * shard_n if w["out"] == "f32" else 0)
-                  + (2 * M * K if w.get("dql") else 0))  # the quantized A written by DQL and read by the product
-    peaks = load_peaks()
-    # A timed region of back-to-back launches longer than a second settles at the power-capped clock: compare with
-    # the sustained figure then, with the burst figure for short runs.
-    sustained = gemm_ns * 1e-9 > 1.0 or wall > 1.0
-    peak_kind = "sustained" if sustained else "burst"
-    peak = 2.0 * (peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"])
+    achieved = wl.ops_shard / per_launch_s / 1e12
     if rank == 0:
+        clk = clocks.summary()
+        peaks, peak, peak_kind, burst, sust, capped = roofline_peaks(clk, gemm_ns * 1e-9 > 1.0 or wall > 1.0)
         cpu = None
         if world == 1 and not args.no_cpu:
             threads = os.cpu_count() or 1
-            tops, dt, rows = cpu_gemm_tops(shard_n, K, threads, args.cpu_seconds, M)
-            sample = f"{rows} of {M} rows x {shard_n} x K {K} on {threads} threads ({dt:.1f} s), extrapolated to TOPS"
-            if dq is not None:
+            tops, dt, rows = cpu_gemm_tops(wl.shard_n, wl.K, threads, args.cpu_seconds, wl.M)
+            sample = (f"{rows} of {wl.M} rows x {wl.shard_n} x K {wl.K} on {threads} threads ({dt:.1f} s), "
+                      f"extrapolated to TOPS")
+            if wl.w.get("dql_in_step"):
                 # Config 2's step also quantizes the activations: the oracle's DynamicReference over the whole x
                 # (one thread), added to the product's extrapolated time.
                 sys.path.insert(0, os.path.join(ROOT, "oracle"))
                 import og_oracle as oracle
 
                 t0 = time.perf_counter()
-                oracle.dynamic_quantize(x_host)
+                oracle.dynamic_quantize(wl.x_host)
                 dq_s = time.perf_counter() - t0
-                gemm_s = 2.0 * M * shard_n * K / (tops * 1e12)
-                tops = 2.0 * M * shard_n * K / (gemm_s + dq_s) / 1e12
-                sample += f"; plus DynamicQuantizeLinear of all {x_host.size} elements on 1 thread ({dq_s:.2f} s)"
+                gemm_s = 2.0 * wl.M * wl.shard_n * wl.K / (tops * 1e12)
+                tops = 2.0 * wl.M * wl.shard_n * wl.K / (gemm_s + dq_s) / 1e12
+                sample += f"; plus DynamicQuantizeLinear of all {wl.x_host.size} elements on 1 thread ({dq_s:.2f} s)"
             cpu = {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample}
-        clk = clocks.summary()
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": f"{args.workload}: {w['desc']}", "m": M, "n": N, "k": K, "batch": B,
-                       "parallelism": (f"{'batch' if by_batch else 'N'}-shard x{world}" if world > 1
+            "config": {"workload": f"{args.workload}: {wl.w['desc']}", "m": wl.M, "n": wl.N, "k": wl.K,
+                       "batch": wl.B,
+                       "parallelism": (f"{'batch' if wl.by_batch else 'N'}-shard x{world}" if world > 1
                                        else "single GPU"),
                        "l2": L2Flush.DESCRIPTION,
-                       "kernel": kernel, "variant": gemm.variant},
+                       "kernel": kernel, "variant": variant},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": round(peak, 1), "unit": "TOPS",
                          "frac": round(achieved / peak, 4), "traffic": profile_traffic(args.workload),
-                         "peak_source": f"2 x {peaks['source']} dense bf16 {peak_kind} "
-                                        f"({peak / 2.0} TF/s): the int8 dense rate is twice bf16 on B200"},
-            "hbm": {"algorithmic_bytes_per_launch": int(algo_bytes),
-                    "achieved_gbs": round(algo_bytes / per_launch_s / 1e9, 1), "peak_gbs": peaks["hbm_gbs"],
-                    "frac": round(algo_bytes / per_launch_s / 1e9 / peaks["hbm_gbs"], 4)},
+                         "peak_source": f"2 x {peaks['source']} dense bf16 {peak_kind} ({peak / 2.0} TF/s): the int8 "
+                                        f"dense rate is twice bf16 on B200"
+                                        + ("; sw_power_cap seen during the timed steps" if capped else ""),
+                         "peak_burst": round(burst, 1), "frac_of_burst": round(achieved / burst, 4),
+                         "peak_sustained": round(sust, 1), "frac_of_sustained": round(achieved / sust, 4)},
+            "hbm": {"algorithmic_bytes_per_launch": int(wl.algo_bytes),
+                    "achieved_gbs": round(wl.algo_bytes / per_launch_s / 1e9, 1), "peak_gbs": peaks["hbm_gbs"],
+                    "frac": round(wl.algo_bytes / per_launch_s / 1e9 / peaks["hbm_gbs"], 4)},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(total_ops / (e2e_ns / args.steps * 1e-9) / 1e12, 3), "unit": "TOPS",
-                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "e2e": {"value": round(wl.ops_total / (e2e_ns / args.steps * 1e-9) / 1e12, 3), "unit": "TOPS",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                    "replicated_operand": ("A uploaded 1/N per rank, all-gathered over NVLink" if split_a else
+                                           "B uploaded 1/N per rank, all-gathered over NVLink" if split_b else None)},
             "gpu_launches": int(launches),
             "clocks": clk,
             "library_int8_tops": round(lib_tops, 3) if isinstance(lib_tops, float) else lib_tops,
             "graph_replay": graph_replay,
             "wall_s": round(wall, 3),
         }
+        if gather:
+            line["gather"] = {"us": round(mx["gather"] / 1e3, 2),
+                              "gbs": round(gather["bytes_into_root"] / mx["gather"], 1),
+                              "bytes_into_root": gather["bytes_into_root"], "root": 0,
+                              "how": "NCCL send/recv over NVLink into staging, placed by pitched copies "
+                                     "(og_comm_gather_columns); not part of value"}
+        for name, d in subs.items():
+            ms = mx[f"{name}_total"] / d["steps"] / 1e6
+            per_launch = mx[f"{name}_ns"] * 1e-9
+            if name == "c5":
+                total_bytes = d["algo_bytes"] * world  # every rank moves its own slab
+                line["c5"] = {"workload": d["desc"], "parallelism": d["parallelism"], "kernel": d["kernel"],
+                              "us_per_step": round(ms * 1e3, 2), "value": round(total_bytes / (ms * 1e-3) / 1e9, 1),
+                              "unit": "GB/s", "per_gpu_gbs": round(d["algo_bytes"] / per_launch / 1e9, 1),
+                              "frac": round(d["algo_bytes"] / per_launch / 1e9 / peaks["hbm_gbs"], 4),
+                              "peak_gbs": peaks["hbm_gbs"], "algorithmic_bytes_per_gpu": int(d["algo_bytes"]),
+                              "steps": d["steps"], "gpu_launches": d["launches"]}
+            else:
+                line["c4"] = {"workload": d["desc"], "parallelism": d["parallelism"], "kernel": d["kernel"],
+                              "us_per_step": round(ms * 1e3, 2),
+                              "value": round(d["ops_total"] / (ms * 1e-3) / 1e12, 1), "unit": "TOPS",
+                              "per_gpu_tops": round(d["ops_shard"] / per_launch / 1e12, 1),
+                              "frac": round(d["ops_shard"] / per_launch / 1e12 / peak, 4), "peak": round(peak, 1),
+                              "steps": d["steps"], "gpu_launches": d["launches"]}
         print(json.dumps(line), flush=True)
-    for v in [a, b, c] + extra:
-        v.dispose()
-    if dq is not None:
-        dq.dispose()
-    gemm.dispose()
-    stamps.dispose()
+    if comm is not None:
+        comm.dispose()
+    flush_dispose = getattr(flush, "dispose", None)
+    if flush_dispose:
+        flush_dispose()
     dev.dispose()
 
 
@@ -772,6 +946,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-library", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the c4 / c5 measurements of the default line")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

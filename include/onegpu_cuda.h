@@ -411,6 +411,31 @@ OG_API og_status og_conv_integer_check(const og_conv_problem* problem, const og_
                                        const og_operand* w_zero_point, const og_buffer* scratch,
                                        int32_t scratch_offset);
 
+/* ---- Several GPUs of one node: NCCL over NVLink (no counterpart in the reference, whose devices never exchange
+ * data: MultiDeviceTests.cs:6-107) -------------------------------------------------------------------------------
+ * The product shards with no reduction (by batch, or by column slabs of B), so no collective runs inside it. These
+ * calls move what surrounds it: the column shards of a result gathered onto the one device that needs the whole
+ * result, and an operand that every rank uploaded one part of replicated onto all ranks. One og_comm per device
+ * (one process or thread per GPU); every call is queued on that device's stream, in order with submitted work, and
+ * every rank makes the same calls in the same order. NCCL (libnccl.so.2) is loaded at the first call; without it the
+ * calls fail with OG_ERROR_UNSUPPORTED (capability "NCCL"). */
+#define OG_COMM_ID_BYTES 128
+typedef struct og_comm og_comm;
+/* A new communicator id (NCCL's unique id): made by one rank and handed to all the others by the host. */
+OG_API og_status og_comm_unique_id(uint8_t* id /* OG_COMM_ID_BYTES */);
+/* Joins rank `rank` of `nranks` on `device`; every rank calls it with the same id, concurrently. */
+OG_API og_status og_comm_create(og_device* device, int32_t nranks, int32_t rank, const uint8_t* id, og_comm** out);
+/* Waits for the device's stream, then releases the communicator and its staging memory. */
+OG_API og_status og_comm_destroy(og_comm* comm);
+/* Gathers the column shards of a dense result [batch][m][N] (N = the sum of widths[0 .. nranks-1]) onto `root`:
+ * rank r passes its shard [batch][m][widths[r]] (columns [widths[0] + ... + widths[r-1], + widths[r]) of the result)
+ * as `shard`, elements of elem_bytes bytes (1, 2, 4 or 8); root also passes the whole result `out`. The other ranks'
+ * shards arrive over NVLink into a staging buffer of the communicator and are put in place with pitched copies. */
+OG_API og_status og_comm_gather_columns(og_comm* comm, const void* shard, int32_t elem_bytes, int32_t batch, int32_t m,
+                                        const int32_t* widths, void* out, int32_t root);
+/* ncclAllGather: recv (nranks * bytes) receives every rank's `bytes` of send, in rank order. */
+OG_API og_status og_comm_all_gather(og_comm* comm, const void* send, uint64_t bytes, void* recv);
+
 #ifdef __cplusplus
 }
 #endif

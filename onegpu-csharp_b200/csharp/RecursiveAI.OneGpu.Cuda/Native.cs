@@ -157,4 +157,13 @@ internal static unsafe partial class Native
         int scratchOffset);
     [LibraryImport(Lib)] internal static partial int og_conv_integer_check(OgConvProblem* p, OgBuffer* x, OgBuffer* w,
         OgBuffer* y, OgOperand* xZeroPoint, OgOperand* wZeroPoint, OgBuffer* scratch, int scratchOffset);
+
+    // Several GPUs of one node (NCCL over NVLink): gathering column shards of a result, replicating an operand.
+    [LibraryImport(Lib)] internal static partial int og_comm_unique_id(byte* id);
+    [LibraryImport(Lib)] internal static partial int og_comm_create(nint device, int nranks, int rank, byte* id,
+        nint* comm);
+    [LibraryImport(Lib)] internal static partial int og_comm_destroy(nint comm);
+    [LibraryImport(Lib)] internal static partial int og_comm_gather_columns(nint comm, nint shard, int elemBytes,
+        int batch, int m, int* widths, nint output, int root);
+    [LibraryImport(Lib)] internal static partial int og_comm_all_gather(nint comm, nint send, ulong bytes, nint recv);
 }

@@ -158,7 +158,7 @@ struct og_int8_gemm {
     bool allow_dot = true;
     int kernel = OG_KERNEL_AUTO;
     int tile = 0;
-    int stream_k = 0;  // 0 and 1: whole tiles per SM pair; 2: stream-K whenever the last wave of tiles is partial
+    int stream_k = 0;  // 0: whole tiles + the split tail of int32 products; 1: whole tiles only; 2: stream-K
     std::string variant;
     std::string last = "none";
     std::vector<void*> scratch;  // int32 byte-sum buffers; older ones live until destroy (recorded work may name them)
@@ -224,6 +224,13 @@ void non_negative(const char* arg, int32_t v) {
 void check_vector(const char* name, const og_operand* o, int32_t n) {
     if (o->buffer.ptr == nullptr) null_arg(kGemm, name);
     range(kGemm, name, o->buffer.length, o->offset, o->is_vector ? n : 1);
+}
+
+// CheckVector with isVector = true: biases are always one value per column (Int8Gemm.cs:242,296,656), whatever the
+// operand's IsVector says; the kernels read bias[n] for every column n.
+void check_column_vector(const char* name, const og_operand* o, int32_t n) {
+    if (o->buffer.ptr == nullptr) null_arg(kGemm, name);
+    range(kGemm, name, o->buffer.length, o->offset, n);
 }
 
 // CheckRange of an operand matrix.
@@ -295,7 +302,7 @@ Prepared check_int32(const og_int8_gemm_problem* p, const og_buffer* a, const og
     require_type(kGemm, c, "c", OG_I32);
     range(kGemm, "c", c->length, p->offset_c, result_count(p));
     if (bias != nullptr) {
-        check_vector("bias", bias, p->n);
+        check_column_vector("bias", bias, p->n);
         require_type(kGemm, &bias->buffer, "bias", OG_I32);
     }
     return pr;
@@ -312,12 +319,12 @@ Prepared check_float(const og_int8_gemm_problem* p, const og_buffer* a, const og
     check_vector("scale", scale, p->n);
     require_type(kGemm, &scale->buffer, "scale", OG_F32);
     if (fbias != nullptr) {
-        check_vector("floatBias", fbias, p->n);
+        check_column_vector("floatBias", fbias, p->n);
         require_type(kGemm, &fbias->buffer, "floatBias", OG_F32);
     }
     if (!pr.ok) return pr;
     if (ibias != nullptr) {
-        check_vector("intBias", ibias, p->n);
+        check_column_vector("intBias", ibias, p->n);
         require_type(kGemm, &ibias->buffer, "intBias", OG_I32);
     }
     return pr;
@@ -340,12 +347,12 @@ Prepared check_dequantize(const og_int8_gemm_problem* p, const og_buffer* a, con
     check_vector("bScale", b_scale, p->n);
     require_type(kGemm, &b_scale->buffer, "bScale", OG_F32);
     if (fbias != nullptr) {
-        check_vector("floatBias", fbias, p->n);
+        check_column_vector("floatBias", fbias, p->n);
         require_type(kGemm, &fbias->buffer, "floatBias", OG_F32);
     }
     if (!pr.ok) return pr;
     if (ibias != nullptr) {
-        check_vector("intBias", ibias, p->n);
+        check_column_vector("intBias", ibias, p->n);
         require_type(kGemm, &ibias->buffer, "intBias", OG_I32);
     }
     return pr;
@@ -372,7 +379,7 @@ Prepared check_requantized(const og_int8_gemm_problem* p, const og_buffer* a, co
         require_type(kGemm, &scratch->buffer, "scratch", OG_I32);
     }
     if (ibias != nullptr) {
-        check_vector("intBias", ibias, p->n);
+        check_column_vector("intBias", ibias, p->n);
         require_type(kGemm, &ibias->buffer, "intBias", OG_I32);
     }
     return pr;
@@ -613,9 +620,9 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
         enc->ops.push_back(std::move(sums));
         enc->dispatches += 1;
     }
-    const bool stream_k = og::sk_wanted(L);
-    if (stream_k) {
-        // Products whose last wave of tiles would leave SMs idle split the (tile, K block) work evenly across the
+    const int split = og::tc_split_mode(L);
+    if (split != 0) {
+        // Products whose last wave of tiles would leave SMs idle split some of the (tile, K block) work across the
         // workers; split tiles meet through this buffer. Recorded launches of one instance run in stream order, so
         // they share it.
         if (g->sk_buf == nullptr) {
@@ -630,7 +637,7 @@ void record_gemm(og_int8_gemm* g, og_encoder* enc, og::GemmLaunch L, const og_op
     og::LaunchFn fn = og::prepare_gemm_tc(L, &err);  // tensor maps built now, at record time
     check_cuda(err, "Int8Gemm tensor maps");
     g->last = std::string(og::tc_cta_group(L) == 2 ? "tensor-core-2sm" : "tensor-core-1sm") +
-              (stream_k ? "-stream-k" : "") + (staged ? "-staged" : "");
+              (split == 2 ? "-stream-k" : split == 1 ? "-split-tail" : "") + (staged ? "-staged" : "");
     enc->ops.push_back(std::move(fn));
     enc->dispatches += 1;
 }

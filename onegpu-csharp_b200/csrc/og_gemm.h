@@ -25,7 +25,9 @@ struct GemmLaunch {
     int num_sms;
     int* error_flag;
     int tile;  // tensor-core tile rows: 0 chooses by size, 128 one CTA per tile, 256 a CTA pair (cta_group::2)
-    int stream_k = 0;  // 2: split the (tile, K block) work evenly across the workers (stream-K); otherwise whole tiles
+    // 0: whole tiles, and for int32 results the tiles past the last full wave split in K (the split tail);
+    // 1: whole tiles only; 2: split the (tile, K block) work evenly across the workers (stream-K)
+    int stream_k = 0;
     // Stream-K hand-over buffers of the tensor-core product (one device buffer of sk_bytes_needed(num_sms) bytes,
     // split by sk_bind); null leaves every worker whole tiles.
     int32_t* sk_part = nullptr;
@@ -42,7 +44,10 @@ struct GemmLaunch {
 // Bytes of the stream-K hand-over buffer for a device with num_sms SMs, and the split of one such buffer.
 int64_t sk_bytes_needed(int num_sms);
 void sk_bind(GemmLaunch& L, void* buffer, int64_t bytes);
-// True when the tensor-core product of L would split tiles between workers (stream-K) given the buffers.
+// How the tensor-core product of L would split tiles between workers given the hand-over buffer: 0 not at all
+// (whole tiles), 1 the split tail (int32 results: the tiles past the last full wave split in K, put together in C by
+// TMA reductions), 2 stream-K (option 2). sk_wanted: the mode is not 0, so the launch needs the buffer.
+int tc_split_mode(const GemmLaunch& L);
 bool sk_wanted(const GemmLaunch& L);
 
 // A launch whose host-side preparation (tensor maps, parameters) is already done: calling it only launches.

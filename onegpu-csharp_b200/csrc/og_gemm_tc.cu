@@ -18,6 +18,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 
 #include <cstdio>
@@ -63,6 +64,7 @@ struct Cfg {
 struct TcParams {
     int m, n, k;
     int tiles_m, tiles_n;
+    int group_m;  // output tiles per raster group along M
     int batch;
     int a_batched, b_batched;
     int k_blocks;
@@ -81,6 +83,19 @@ struct TcParams {
     int32_t* sk_part;       // [slots][CG][8 chunks][8 quads][128 rows][4] int32
     unsigned int* sk_flag;  // [slots] flags, then the generation and the ticket
     int sk_slots;
+    // Split tail (int32 results): tiles [0, dp_tiles) are whole tiles dealt round-robin to the workers; the K blocks
+    // of the remaining tiles (tail_units of them) are split into equal contiguous ranges over the first tail_workers
+    // workers, each worker taking its range before its whole tiles. The tail tiles are put together in C itself:
+    // every CTA first clears its share of them (the epilogue warps, while the first MMAs run) and counts itself in
+    // tail_zeroed; then every segment adds its sums with TMA reductions, after that count is complete, the segment
+    // holding K block 0 of its tile adding the zero-point terms and bias too. The last CTA to finish sets the count
+    // back to zero, with the stream-K generation and ticket that follow sk_flag's slots.
+    int tail_split;
+    int tail_first;  // a worker takes its tail range before (1) or after (0) its whole tiles
+    int dp_tiles;
+    int64_t tail_units;
+    int tail_workers;
+    unsigned int* tail_zeroed;
 };
 
 // One piece of a worker's work: K blocks [kb0, kb1) of a tile.
@@ -89,27 +104,44 @@ struct WorkItem {
 };
 
 struct WorkCursor {
-    int64_t u, u1;  // stream-K: the worker's remaining units
-    int tile;       // otherwise: the next tile
+    int64_t u, u1;  // stream-K, or the split tail: the worker's remaining units
+    int tile;       // whole tiles: the next tile
 };
 
 __device__ __forceinline__ void work_begin(const TcParams& p, int worker, int workers, WorkCursor& c) {
-    c.u = p.units * worker / workers;
-    c.u1 = p.units * (worker + 1) / workers;
+    if (p.stream_k) {
+        c.u = p.units * worker / workers;
+        c.u1 = p.units * (worker + 1) / workers;
+    } else if (p.tail_split && worker < p.tail_workers) {
+        c.u = p.tail_units * worker / p.tail_workers;
+        c.u1 = p.tail_units * (worker + 1) / p.tail_workers;
+    } else {
+        c.u = c.u1 = 0;
+    }
     c.tile = worker;
 }
 
+// A worker of the split tail takes its range of tail units before its whole tiles (tail_first; after them
+// otherwise): the reductions of its tail segments then overlap the MMAs of its whole tiles, and every worker ends on
+// a whole tile whose epilogue is a plain store.
 __device__ __forceinline__ bool work_next(const TcParams& p, int workers, WorkCursor& c, WorkItem& w) {
-    if (p.stream_k) {
-        if (c.u >= c.u1) return false;
-        w.tile = static_cast<int>(c.u / p.k_blocks);
-        w.kb0 = static_cast<int>(c.u - static_cast<int64_t>(w.tile) * p.k_blocks);
+    if (!p.stream_k && !p.tail_first && c.tile < p.dp_tiles) {
+        w.tile = c.tile;
+        w.kb0 = 0;
+        w.kb1 = p.k_blocks;
+        c.tile += workers;
+        return true;
+    }
+    if (c.u < c.u1) {
+        const int t = static_cast<int>(c.u / p.k_blocks);
+        w.kb0 = static_cast<int>(c.u - static_cast<int64_t>(t) * p.k_blocks);
         const int64_t end = static_cast<int64_t>(w.kb0) + (c.u1 - c.u);
         w.kb1 = end < p.k_blocks ? static_cast<int>(end) : p.k_blocks;
+        w.tile = p.stream_k ? t : p.dp_tiles + t;
         c.u += w.kb1 - w.kb0;
         return true;
     }
-    if (c.tile >= p.total_tiles) return false;
+    if (p.stream_k || c.tile >= p.dp_tiles) return false;
     w.tile = c.tile;
     w.kb0 = 0;
     w.kb1 = p.k_blocks;
@@ -145,6 +177,23 @@ __device__ __forceinline__ bool flag_wait(const unsigned int* flag, unsigned int
     }
 }
 
+// Waits (bounded) until *word has reached `count`; false when the wait gave up or another role of this CTA raised the
+// abort flag.
+__device__ __forceinline__ bool count_wait(const unsigned int* word, unsigned int count, volatile int* abort) {
+    const uint64_t t0 = global_timer_ns();
+    while (true) {
+        unsigned int v;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(word) : "memory");
+        if (v >= count) return true;
+        if (*abort) return false;
+        if (global_timer_ns() - t0 > OG_WAIT_LIMIT_NS) {
+            *abort = 1;
+            return false;
+        }
+        __nanosleep(64);
+    }
+}
+
 // Adds the handed-over sums (already copied into this CTA's shared memory, same layout) to chunk c of a row.
 __device__ __forceinline__ void sk_add(const int32_t* slot_smem, int c, int row, uint32_t (&r)[32]) {
 #pragma unroll
@@ -162,10 +211,10 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& b,
     const int per_batch = p.tiles_m * p.tiles_n;
     b = tile / per_batch;
     const int r = tile - b * per_batch;
-    const int group_span = tc::GROUP_M * p.tiles_n;
+    const int group_span = p.group_m * p.tiles_n;
     const int group = r / group_span;
-    const int first_m = group * tc::GROUP_M;
-    const int gsize = min(p.tiles_m - first_m, tc::GROUP_M);
+    const int first_m = group * p.group_m;
+    const int gsize = min(p.tiles_m - first_m, p.group_m);
     const int in_group = r - group * group_span;
     tm = first_m + in_group % gsize;
     tn = in_group / gsize;
@@ -391,7 +440,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
     if (tma_store && warp == 2 && lane == 0) prefetch_tmap(&tmap_c);
     pdl_wait();  // the preceding grid is done: its outputs are readable and its TMEM is free
     // This launch's stream-K generation: flags set to it belong to this launch.
-    if (threadIdx.x == 0) *sk_gen = p.stream_k ? __ldcg(p.sk_flag + p.sk_slots) + 1u : 0u;
+    if (threadIdx.x == 0) *sk_gen = (p.stream_k || p.tail_split) ? __ldcg(p.sk_flag + p.sk_slots) + 1u : 0u;
     if (warp == 1) {
         if constexpr (CG == 2) {
             tmem_alloc_pair(tmem_holder, tc::TMEM_COLS);
@@ -514,6 +563,30 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         // Column terms are needed unless the result is the raw int32 sum.
         const bool terms = OUT != OUT_I32 || e.za != nullptr || e.zb != nullptr || e.int_bias != nullptr;
         const bool za_per_row = e.za != nullptr && e.za_vector;
+        if (p.tail_split) {
+            // Clear this CTA's share of the tail tiles (rows of 256 columns, dealt to the epilogue warps of the grid in
+            // turn) while the first MMAs run, then count the CTA in the launch's tally. C's rows start on 16-byte
+            // boundaries and N is a multiple of 4 (the TMA-store condition), so whole 16-byte stores stay inside C.
+            const int64_t rows_total = static_cast<int64_t>(p.total_tiles - p.dp_tiles) * C::BM;
+            for (int64_t r = static_cast<int64_t>(blockIdx.x) * tc::EPI_WARPS + ew; r < rows_total;
+                 r += static_cast<int64_t>(gridDim.x) * tc::EPI_WARPS) {
+                int zb_, ztm, ztn;
+                tile_coords<C::BM>(p, p.dp_tiles + static_cast<int>(r / C::BM), zb_, ztm, ztn);
+                const int zm = ztm * C::BM + static_cast<int>(r % C::BM);
+                if (zm >= p.m) continue;
+                uint32_t* zrow = static_cast<uint32_t*>(e.c) + zb_ * e.batch_stride_c + static_cast<int64_t>(zm) * e.ldc;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int zn = ztn * tc::BN + h * 128 + lane * 4;
+                    if (zn < p.n) *reinterpret_cast<uint4*>(zrow + zn) = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            __threadfence();
+            fence_proxy_async_global();
+            asm volatile("bar.sync 1, %0;" ::"n"(tc::EPI_THREADS) : "memory");
+            if (threadIdx.x == 64) atomicAdd(p.tail_zeroed, 1u);
+        }
+        bool tail_ready = false;  // thread 64: the whole grid has cleared the tail
         WorkCursor cur;
         work_begin(p, worker, workers, cur);
         WorkItem wi;
@@ -522,13 +595,19 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             tile_coords<C::BM>(p, wi.tile, b, tm, tn);
             const int acc = lt & 1;
             const uint32_t aph = (lt >> 1) & 1;
-            // The K-block-0 segment of a split tile (the end of this worker's range) also waits for the next
-            // worker's sums of the later segment. One thread does every wait and publishes the outcome, so the four
-            // warps always leave or continue together (the named barriers below cannot time out).
-            const bool sk_wait = wi.kb0 == 0 && wi.kb1 < p.k_blocks;
+            // Stream-K: the K-block-0 segment of a split tile (the end of this worker's range) also waits for the
+            // next worker's sums of the later segment. Split tail: a segment of a tail tile adds to C, once every CTA
+            // has cleared its share of the tail. One thread does every wait and publishes the outcome, so the
+            // epilogue warps always leave or continue together (the named barriers below cannot time out).
+            const bool sk_wait = p.stream_k && wi.kb0 == 0 && wi.kb1 < p.k_blocks;
+            const bool tail_item = p.tail_split && wi.tile >= p.dp_tiles;
             const int sk_slot = (worker + 1) * CG + static_cast<int>(rank);
             if (threadIdx.x == 64) {
                 bool ok = mbar_wait(&tfull[acc], aph, abort_flag);
+                if (ok && tail_item && !tail_ready) {
+                    ok = count_wait(p.tail_zeroed, gridDim.x, abort_flag);
+                    tail_ready = ok;
+                }
                 if (ok && sk_wait) {
                     // This is the worker's last item: its MMAs are complete, so the operand ring is idle and takes
                     // the handed-over sums in one bulk copy.
@@ -543,10 +622,12 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             }
             asm volatile("bar.sync 1, %0;" ::"n"(tc::EPI_THREADS) : "memory");
             if (!epi_go[lt & 1]) goto done;
+            const bool reduce = tail_item;
+            if (reduce && lane == 0) fence_proxy_async_global();  // the reductions follow the cleared tail
             tc_fence_after();
             const int row_in_cta = q * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * tc::BN;
-            if (wi.kb0 > 0) {
+            if (p.stream_k && wi.kb0 > 0) {
                 // The later segment of a split tile (the start of this worker's range): hand its raw sums to the
                 // worker that holds K block 0 (the previous one), then flag them.
                 int32_t* slot = p.sk_part + static_cast<int64_t>(worker * CG + static_cast<int>(rank)) * SK_SLOT_INTS;
@@ -574,7 +655,9 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                 continue;
             }
             const int32_t* sk_in = sk_wait ? reinterpret_cast<const int32_t*>(sA) : nullptr;
-            if (terms) {  // every warp has left the previous tile (the barrier above), so its terms are free
+            // The zero-point terms and the bias enter C once: with the K-block-0 segment of a tail tile.
+            const bool with_terms = terms && (!reduce || wi.kb0 == 0);
+            if (with_terms) {  // every warp has left the previous tile (the barrier above), so its terms are free
                 fill_col_terms(terms_smem, e, b, tn * tc::BN, threadIdx.x - 64, tc::EPI_THREADS);
                 asm volatile("bar.sync 1, %0;" ::"n"(tc::EPI_THREADS) : "memory");
             }
@@ -606,12 +689,15 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                         uint8_t* box = staging + (ew * C::BOXES + h % C::BOXES) * C::BOX_BYTES;
                         if (lane == 0) bulk_wait_group_read<C::BOXES - 1>();
                         __syncwarp();
-                        stage_half<OUT>(terms_smem, e, terms, za_per_row, za, rt, c * 32 + 16 * h, r + 16 * h, box,
-                                        lane);
+                        stage_half<OUT>(terms_smem, e, with_terms, za_per_row, za, rt, c * 32 + 16 * h, r + 16 * h,
+                                        box, lane);
                         fence_proxy_async_smem();
                         __syncwarp();
                         if (lane == 0) {
-                            tma_store_3d(&tmap_c, box, n0 + 16 * h, box_row, b);
+                            if (reduce)
+                                tma_reduce_add_3d(&tmap_c, box, n0 + 16 * h, box_row, b);
+                            else
+                                tma_store_3d(&tmap_c, box, n0 + 16 * h, box_row, b);
                             bulk_commit_group();
                         }
                     }
@@ -652,12 +738,13 @@ done:
             tmem_dealloc(tmem_base, tc::TMEM_COLS);
     }
     if (threadIdx.x == 0 && *abort_flag) atomicExch(p.error_flag, 1);
-    if (p.stream_k && threadIdx.x == 0) {
+    if ((p.stream_k || p.tail_split) && threadIdx.x == 0) {
         // The last CTA to finish advances the generation (every CTA read it when it started) and resets the ticket.
         unsigned int* gen = p.sk_flag + p.sk_slots;
         __threadfence();
         if (atomicAdd(gen + 1, 1u) == gridDim.x - 1) {
             atomicExch(gen + 1, 0u);
+            if (p.tail_split) atomicExch(p.tail_zeroed, 0u);  // every CTA has left its waits on the count
             atomicAdd(gen, 1u);
         }
     }
@@ -783,6 +870,46 @@ static LaunchFn bind_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensor
     };
 }
 
+// The split tail of an int32 product: its tiles beyond the last full wave of whole tiles, split in K over as many
+// workers as get at least TAIL_MIN_BLOCKS K blocks each, when the last wave would leave at least half of the workers
+// idle. Measured on B200, the split segments run below the whole tiles' K-block rate (their operands are shared by
+// fewer concurrent tiles in L2) and add a reduction pass over the tail, so a nearly full last wave is faster left
+// whole: 8192 x 1024 x 8192 (54 tail tiles over 74 CTA pairs) 59.4 us split against 57.3 us whole, while
+// 2048 x 12288 x 4096 (14 tail tiles) takes 75.8 us split against 79.9 us whole. The cut tiles are put together in C
+// with TMA reductions, so C's rows must allow TMA stores.
+constexpr int TAIL_MIN_BLOCKS = 8;
+
+struct TailPlan {
+    int dp_tiles = 0, workers = 0;
+    int64_t units = 0;
+};
+
+static TailPlan tail_plan(int64_t tiles, int64_t k_blocks, int64_t workers) {
+    TailPlan t;
+    const int64_t rem = tiles % workers;
+    t.dp_tiles = static_cast<int>(tiles - rem);
+    if (rem == 0 || 2 * rem > workers) {
+        t.dp_tiles = static_cast<int>(tiles);
+        return t;
+    }
+    t.units = rem * k_blocks;
+    const int64_t w = std::min<int64_t>(workers, t.units / TAIL_MIN_BLOCKS);
+    if (w <= rem) {
+        t.units = 0;
+        t.dp_tiles = static_cast<int>(tiles);
+        return t;
+    }
+    t.workers = static_cast<int>(w);
+    return t;
+}
+
+static bool tail_eligible(const GemmLaunch& L) {
+    if (L.stream_k != 0 || L.epi.out_kind != OUT_I32) return false;
+    const bool c_aligned = (reinterpret_cast<uintptr_t>(L.epi.c) & 15) == 0 && (L.epi.ldc & 3) == 0 &&
+                           (L.batch == 1 || (L.epi.batch_stride_c & 3) == 0);
+    return c_aligned;
+}
+
 // Stream-K runs only when asked for (mode 2) and when every worker gets at least one tile's worth of K blocks, so
 // that a tile is split between two workers at most. It is not chosen by size: measured on B200 the int8 product's
 // K-block rate is capped by operand delivery to the SMs rather than by how many SM pairs are busy, so the partial last
@@ -793,19 +920,26 @@ static bool sk_worthwhile(int64_t tiles, int64_t workers, int mode) {
     return tiles % workers != 0;
 }
 
-bool sk_wanted(const GemmLaunch& L) {
+int tc_split_mode(const GemmLaunch& L) {
     const int cg = tc_cta_group(L);
     const int64_t bm = 128 * cg;
     const int64_t tiles = ((L.m + bm - 1) / bm) * ((L.n + tc::BN - 1) / tc::BN) * int64_t(L.batch);
-    return sk_worthwhile(tiles, L.num_sms / cg, L.stream_k);
+    if (sk_worthwhile(tiles, L.num_sms / cg, L.stream_k)) return 2;
+    return tail_eligible(L) && tail_plan(tiles, (L.k + tc::BK - 1) / tc::BK, L.num_sms / cg).workers > 0 ? 1 : 0;
 }
+
+bool sk_wanted(const GemmLaunch& L) { return tc_split_mode(L) != 0; }
 
 // Hand-over slots: one per CTA of the grid plus one pair (slot (worker + 1) * CG + rank is the largest read).
 static int64_t sk_slots(int num_sms) { return int64_t(num_sms) + 2; }
 
+// Split tail: the count of CTAs that have cleared their share of the tail, after the generation and the ticket.
+constexpr int64_t TAIL_WORDS = 1;
+
 int64_t sk_bytes_needed(int num_sms) {
     return sk_slots(num_sms) * (SK_SLOT_INTS * int64_t(sizeof(int32_t)) + int64_t(sizeof(unsigned int))) +
-           2 * int64_t(sizeof(unsigned int));  // the generation and the ticket
+           2 * int64_t(sizeof(unsigned int)) +  // the generation and the ticket
+           TAIL_WORDS * int64_t(sizeof(unsigned int));
 }
 
 void sk_bind(GemmLaunch& L, void* buffer, int64_t bytes) {
@@ -820,6 +954,7 @@ void sk_bind(GemmLaunch& L, void* buffer, int64_t bytes) {
                                                 sk_slots(L.num_sms) * SK_SLOT_INTS * int64_t(sizeof(int32_t)));
     L.sk_bytes = bytes;
 }
+
 
 template <int CG>
 static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
@@ -847,6 +982,7 @@ static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
     p.k = L.k;
     p.tiles_m = (L.m + C::BM - 1) / C::BM;
     p.tiles_n = (L.n + tc::BN - 1) / tc::BN;
+    p.group_m = tc::GROUP_M;
     p.batch = L.batch;
     p.a_batched = ba > 1;
     p.b_batched = bb > 1;
@@ -865,14 +1001,32 @@ static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
                   make_store_map(&mc, L.epi.c, L.n, L.m, L.batch, uint64_t(L.epi.ldc) * 4,
                                  L.batch > 1 ? uint64_t(L.epi.batch_stride_c) * 4 : round16(uint64_t(L.epi.ldc) * 4 * L.m));
     const int64_t workers = L.num_sms / CG;
-    const int grid = static_cast<int>((total < workers ? total : workers) * CG);
+    int grid = static_cast<int>((total < workers ? total : workers) * CG);
     // Stream-K when it pays (sk_worthwhile) and the caller gave the hand-over buffers.
     p.units = total * p.k_blocks;
     p.sk_part = L.sk_part;
     p.sk_flag = L.sk_flag;
     p.sk_slots = static_cast<int>(sk_slots(L.num_sms));
-    p.stream_k = L.sk_part != nullptr && sk_bytes_needed(L.num_sms) <= L.sk_bytes &&
-                 sk_worthwhile(total, workers, L.stream_k);
+    const bool buffers = L.sk_part != nullptr && sk_bytes_needed(L.num_sms) <= L.sk_bytes;
+    p.stream_k = buffers && sk_worthwhile(total, workers, L.stream_k);
+    // Otherwise the split tail, for int32 results stored through TMA.
+    p.tail_split = 0;
+    p.tail_first = 1;
+    p.dp_tiles = static_cast<int>(total);
+    p.tail_units = 0;
+    p.tail_workers = 0;
+    p.tail_zeroed = nullptr;
+    if (!p.stream_k && buffers && p.tma_store && tail_eligible(L)) {
+        const TailPlan t = tail_plan(total, p.k_blocks, workers);
+        if (t.workers > 0) {
+            p.tail_split = 1;
+            p.dp_tiles = t.dp_tiles;
+            p.tail_units = t.units;
+            p.tail_workers = t.workers;
+            p.tail_zeroed = L.sk_flag + p.sk_slots + 2;
+            grid = static_cast<int>(std::max<int64_t>(grid / CG, t.workers) * CG);
+        }
+    }
     const bool bmn = !L.trans_b;
     switch (L.epi.out_kind) {
         case OUT_I32: return bmn ? bind_tc_t<CG, true, OUT_I32>(L, p, ma, mb, mc, grid)

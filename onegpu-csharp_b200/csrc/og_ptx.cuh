@@ -131,6 +131,21 @@ __device__ __forceinline__ void tma_store_3d(const void* tmap, const void* smem_
                  : "memory");
 }
 
+// 3-D tiled TMA reduction from shared memory: each element of the box is added (integer addition for an int32 tensor
+// map, atomically at L2) to the tensor's element; parts of the box outside the tensor are not touched.
+__device__ __forceinline__ void tma_reduce_add_3d(const void* tmap, const void* smem_src, int32_t x, int32_t y,
+                                                  int32_t z) {
+    asm volatile("cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(tmap)),
+                 "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
+// Orders this thread's async-proxy global-memory accesses (TMA stores, reductions) with its generic-proxy ones.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
 // Waits until the shared-memory sources of all but the newest `N` committed bulk groups have been read.

@@ -159,6 +159,11 @@ EXPORTS = {
     "og_conv_integer_scratch_bytes_per_image": [_P, ctypes.POINTER(ctypes.c_int64)],
     "og_conv_integer_encode": [_P, _P, _P, _BUF, _BUF, _BUF, _OPD, _OPD, _BUF, ctypes.c_int32],
     "og_conv_integer_check": [_P, _BUF, _BUF, _BUF, _OPD, _OPD, _BUF, ctypes.c_int32],
+    "og_comm_unique_id": [_P],
+    "og_comm_create": [_P, ctypes.c_int32, ctypes.c_int32, _P, _PP],
+    "og_comm_destroy": [_P],
+    "og_comm_gather_columns": [_P, _P, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _P, _P, ctypes.c_int32],
+    "og_comm_all_gather": [_P, _P, ctypes.c_uint64, _P],
 }
 
 for _name, _args in EXPORTS.items():
@@ -481,6 +486,58 @@ class GpuDevice:
     def dispose(self) -> None:
         if self.handle:
             _check(_lib.og_device_destroy(self.handle))
+            self.handle = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.dispose()
+
+
+# ---- several GPUs: NCCL over NVLink -----------------------------------------------------------------------------
+
+COMM_ID_BYTES = 128
+
+
+def comm_unique_id() -> bytes:
+    """og_comm_unique_id: a new communicator id, made by one rank and handed to the others by the host."""
+    buf = (ctypes.c_uint8 * COMM_ID_BYTES)()
+    _check(_lib.og_comm_unique_id(buf))
+    return bytes(buf)
+
+
+class Communicator:
+    """og_comm: this device's rank in an NCCL communicator of `nranks` GPUs of one node (one process per GPU). Every
+    call is queued on the device's stream in order with submitted work; every rank makes the same calls in the same
+    order. No counterpart in the reference (its devices never exchange data)."""
+
+    def __init__(self, device: GpuDevice, nranks: int, rank: int, unique_id: bytes):
+        if len(unique_id) != COMM_ID_BYTES:
+            raise ValueError(f"the communicator id has {COMM_ID_BYTES} bytes")
+        h = ctypes.c_void_p()
+        idbuf = (ctypes.c_uint8 * COMM_ID_BYTES).from_buffer_copy(unique_id)
+        _check(_lib.og_comm_create(device.handle, int(nranks), int(rank), idbuf, ctypes.byref(h)))
+        self.handle = h.value
+        self.device = device
+        self.nranks = nranks
+        self.rank = rank
+
+    def gather_columns(self, shard_ptr: int, elem_bytes: int, batch: int, m: int, widths, out_ptr: int = 0,
+                       root: int = 0) -> None:
+        """og_comm_gather_columns: the column shards [batch][m][widths[r]] of every rank put together as the dense
+        [batch][m][sum(widths)] result at `out_ptr` on `root`."""
+        w = (ctypes.c_int32 * self.nranks)(*[int(x) for x in widths])
+        _check(_lib.og_comm_gather_columns(self.handle, ctypes.c_void_p(shard_ptr), int(elem_bytes), int(batch),
+                                           int(m), w, ctypes.c_void_p(out_ptr or None), int(root)))
+
+    def all_gather(self, send_ptr: int, nbytes: int, recv_ptr: int) -> None:
+        """og_comm_all_gather: recv (nranks * nbytes) receives every rank's nbytes of send, in rank order."""
+        _check(_lib.og_comm_all_gather(self.handle, ctypes.c_void_p(send_ptr), int(nbytes), ctypes.c_void_p(recv_ptr)))
+
+    def dispose(self) -> None:
+        if self.handle:
+            _check(_lib.og_comm_destroy(self.handle))
             self.handle = None
 
     def __enter__(self):

@@ -11,6 +11,12 @@ from cases import Case, case_data, oracle_shape
 SENTINEL = 0x5A5A5A5A
 
 
+def base_kernel(kernel: str) -> str:
+    """The kernel configuration a product ran on, without the split-tail schedule suffix (int32 products whose last
+    wave of tiles is partial split that wave in K; the tile and kernel are the same)."""
+    return kernel.replace("-split-tail", "")
+
+
 def typed(device, data: np.ndarray, signed: bool):
     return device.create_buffer(np.int8 if signed else np.uint8, data.view(np.int8 if signed else np.uint8))
 

@@ -77,6 +77,15 @@ def test_bad_arguments_are_rejected():
     assert argument_of(og.check_float, P(2, 8, 2), a, b, f, Op(fl, 0, True)) == (shape, "scale")
     assert argument_of(og.check_requantized, P(2, 2, 2), a, b, a, Op(fl, 0), 300) == (shape, "zeroPointY")
     assert argument_of(og.check_requantized, P(2, 2, 2), a, b, b, Op(fl, 0), 128) == (shape, "zeroPointY")
+    # A bias is one value per column whatever its IsVector says (Int8Gemm.cs:242,296,656): a one-value buffer is
+    # refused for N > 1, as a float bias is (the kernels read one per column).
+    ib1, ib8 = spec(I32, 1), spec(I32, 8)
+    assert argument_of(og.check_int32, P(2, 8, 2), a, b, c, None, None, Op(ib1, 0, False)) == (shape, "bias")
+    og.check_int32(P(2, 8, 2), a, b, c, None, None, Op(ib8, 0, False))
+    assert argument_of(og.check_float, P(2, 8, 2), a, b, f, Op(fl, 0), None, None, Op(fl, 0, False)) == \
+        (shape, "floatBias")
+    assert argument_of(og.check_float, P(2, 8, 2), a, b, f, Op(fl, 0), None, None, None, Op(ib1, 0, False)) == \
+        (shape, "intBias")
     # The valid calls pass.
     og.check_int32(P(2, 2, 2), a, b, c)
     og.check_float(P(2, 8, 2), a, b, f, Op(fl, 0))

@@ -12,7 +12,7 @@ import og_oracle as oracle
 import onegpu_cuda as og
 from cases import (Case, case_data, edge_cases, float_biases, float_scale, golden, oracle_shape, problem, requant_bias,
                    requant_mult)
-from gpu_rig import SENTINEL, align_case, run_int32, typed
+from gpu_rig import SENTINEL, align_case, base_kernel, run_int32, typed
 
 pytestmark = pytest.mark.gpu
 
@@ -43,7 +43,7 @@ def test_edge_shapes_are_bit_exact(device):
                 if name.startswith("tensor-core") and (c.p["k"] == 0 or "aligned" not in c.name):
                     continue
                 b, k = run_int32(device, gemm, c, seed)
-                kernels.add(k)
+                kernels.add(base_kernel(k))
                 assert b == 0, f"[{name}] {c.name} signed {c.a_signed}/{c.b_signed} zp {c.za_mode}/{c.zb_mode}"
             total[name] = kernels
     assert total["portable"] == {"portable"}
@@ -307,51 +307,8 @@ def test_tensor_core_sums_wrap_modulo_2_32(device, cfg):
         for zpa, zpb in ((None, None), (za, zb)):
             cc = Case("wrap", c.p, False, False, 0 if zpa is None else 1, 0 if zpb is None else 2)
             bad, kern = run_int32(device, gemm, cc, 3, data=(a, b, zpa, zpb))
-            assert kern == cfg
+            assert base_kernel(kern) == cfg
             assert bad == 0
-
-
-def full_size_check(device, gemm, m, n, k, batch, a_signed, zp, trans_b=False, sample_rows=24, seed=77):
-    """A product at a config's full size, checked without a full CPU reference: every column sum and row sum of C
-    against (1^T A') B' and A' (B' 1) computed exactly on the host (A' = A - za, B' = B - zb, all modulo 2^32), and
-    a sample of whole rows against the oracle."""
-    rng = np.random.default_rng(seed)
-    a_dt = np.int8 if a_signed else np.uint8
-    a = rng.integers(-128 if a_signed else 0, 128 if a_signed else 256, size=batch * m * k, dtype=np.int16).astype(a_dt)
-    b = rng.integers(-127, 128, size=k * n, dtype=np.int16).astype(np.int8)
-    za = np.array([128 if not a_signed else 3], a_dt) if zp else None
-    zb = rng.integers(-8, 9, size=n).astype(np.int8) if zp else None
-    p = og.Int8GemmProblem(m, n, k, batch=batch, transpose_b=trans_b, stride_a=m * k if batch > 1 else 0)
-    bufs = [device.create_buffer(a_dt, a), device.create_buffer(np.int8, b), device.create_buffer(np.int32, batch * m * n)]
-    zpa = zpb = None
-    if zp:
-        bufs += [device.create_buffer(a_dt, za), device.create_buffer(np.int8, zb)]
-        zpa, zpb = og.Int8Operand(bufs[3], 0), og.Int8Operand(bufs[4], 0, True)
-    enc = device.begin_commands()
-    gemm.encode_int32(enc, p, bufs[0], bufs[1], bufs[2], zpa, zpb)
-    kern = gemm.last_kernel
-    device.submit(enc)
-    c = bufs[2].read().reshape(batch, m, n)
-    for v in bufs:
-        v.dispose()
-    a64 = a.reshape(batch, m, k).astype(np.int64) - (int(za[0]) if zp else 0)
-    b64 = b.reshape(n, k).T.astype(np.int64) if trans_b else b.reshape(k, n).astype(np.int64)
-    b64 = b64 - (zb.astype(np.int64)[None, :] if zp else 0)
-    wrap = lambda x: ((x + 2 ** 31) % 2 ** 32 - 2 ** 31)
-    c64 = c.astype(np.int64)
-    for bt in range(batch):
-        col_want = wrap(a64[bt].sum(axis=0) @ b64)           # (1^T A') B'
-        row_want = wrap(a64[bt] @ b64.sum(axis=1))           # A' (B' 1)
-        assert np.array_equal(wrap(c64[bt].sum(axis=0)), col_want), f"column sums of batch {bt} [{kern}]"
-        assert np.array_equal(wrap(c64[bt].sum(axis=1)), row_want), f"row sums of batch {bt} [{kern}]"
-    rows = rng.choice(m, size=min(sample_rows, m), replace=False)
-    bt = batch - 1
-    a_rows = a.reshape(batch, m, k)[bt][rows].view(np.uint8)
-    want = oracle.int8_gemm(a_rows, a_signed, b.view(np.uint8), True, None if za is None else za.view(np.uint8),
-                            False, None if zb is None else zb.view(np.uint8), True, m=len(rows), n=n, k=k,
-                            transpose_b=trans_b)
-    assert np.array_equal(c[bt][rows].reshape(-1), want), f"sampled rows [{kern}]"
-    return kern
 
 
 @pytest.mark.parametrize("cfg,m,n,k", [("tensor-core-2sm", 1280, 4096, 512), ("tensor-core-1sm", 1280, 4096, 512),
@@ -398,19 +355,6 @@ def test_stream_k_split_tiles_are_bit_exact(device, cfg, m, n, k):
         finally:
             for v in bufs:
                 v.dispose()
-
-
-@pytest.mark.parametrize("workload", ["c3", "c2", "c4", "c5", "c3-transposed"])
-def test_config_sizes_checksums_and_sampled_rows(device, workload):
-    """BASELINE.json's configs at full size: 8192^3 s8 x s8, 4096^3 u8 x s8 with zero points, the batched QKV
-    projection 8 x 2048 x 12288 x 4096, the decode shape 16 x 28672 x 8192, and 8192^3 with B stored N x K."""
-    shapes = {"c3": (8192, 8192, 8192, 1, True, False, False), "c2": (4096, 4096, 4096, 1, False, True, False),
-              "c4": (2048, 12288, 4096, 8, False, True, False), "c5": (16, 28672, 8192, 1, False, True, False),
-              "c3-transposed": (8192, 8192, 8192, 1, True, False, True)}
-    m, n, k, batch, a_signed, zp, trans_b = shapes[workload]
-    with og.Int8Gemm(device) as gemm:
-        kern = full_size_check(device, gemm, m, n, k, batch, a_signed, zp, trans_b)
-        assert kern.startswith("tensor-core")
 
 
 @pytest.mark.parametrize("m,n,k,batch,trans_b", [
@@ -517,5 +461,5 @@ def test_zero_point_byte_sums_are_bit_exact(device, cfg, m, n, k, batch, trans_b
                                            (1, 0, False, True), (0, 2, False, True)):
             c = align_case(Case("sums", problem(m, n, k, batch=batch, trans_b=trans_b), a_s, b_s, za_mode, zb_mode))
             bad, kernel = run_int32(device, gemm, c, 400 + 3 * za_mode + zb_mode)
-            assert kernel == cfg
+            assert base_kernel(kernel) == cfg
             assert bad == 0, f"zp modes {za_mode}/{zb_mode} signed {a_s}/{b_s}"

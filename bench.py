@@ -907,7 +907,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
             line["gather"] = {"us": round(mx["gather"] / 1e3, 2),
                               "gbs": round(gather["bytes_into_root"] / mx["gather"], 1),
                               "bytes_into_root": gather["bytes_into_root"], "root": 0,
-                              "how": "NCCL send/recv over NVLink into staging, placed by pitched copies "
+                              "how": "NCCL send/recv over NVLink into staging, placed by one kernel "
                                      "(og_comm_gather_columns); not part of value"}
         for name, d in subs.items():
             ms = mx[f"{name}_total"] / d["steps"] / 1e6

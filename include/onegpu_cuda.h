@@ -430,7 +430,7 @@ OG_API og_status og_comm_destroy(og_comm* comm);
 /* Gathers the column shards of a dense result [batch][m][N] (N = the sum of widths[0 .. nranks-1]) onto `root`:
  * rank r passes its shard [batch][m][widths[r]] (columns [widths[0] + ... + widths[r-1], + widths[r]) of the result)
  * as `shard`, elements of elem_bytes bytes (1, 2, 4 or 8); root also passes the whole result `out`. The other ranks'
- * shards arrive over NVLink into a staging buffer of the communicator and are put in place with pitched copies. */
+ * shards arrive over NVLink into a staging buffer of the communicator and are put in place by one kernel. */
 OG_API og_status og_comm_gather_columns(og_comm* comm, const void* shard, int32_t elem_bytes, int32_t batch, int32_t m,
                                         const int32_t* widths, void* out, int32_t root);
 /* ncclAllGather: recv (nranks * bytes) receives every rank's `bytes` of send, in rank order. */

@@ -10,6 +10,7 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -86,6 +87,36 @@ void check_nccl(ncclResult_t r, const char* what) {
                   "", "", ""};
 }
 
+// The column shards of a gathered result, as the placement kernel reads them.
+constexpr int kMaxPlaceRanks = 64;
+struct Placement {
+    const uint8_t* src[kMaxPlaceRanks];  // shard of rank r: rows of width[r] bytes, dense
+    int64_t col0[kMaxPlaceRanks];        // its first byte within an output row
+    int64_t width[kMaxPlaceRanks];       // bytes per row
+    int nranks;
+    int64_t row_bytes;                   // of the output
+    int64_t rows;
+    int vec;                             // every offset and width is a multiple of 16 bytes
+};
+
+// Puts the shards in place: output row i is the concatenation of row i of every shard. One CTA per row (grid-stride
+// over rows), consecutive threads on consecutive 16-byte words, so every read and write is coalesced.
+__global__ void __launch_bounds__(256) place_columns_kernel(const __grid_constant__ Placement pl, uint8_t* out) {
+    for (int64_t row = blockIdx.x; row < pl.rows; row += gridDim.x) {
+        uint8_t* dst = out + row * pl.row_bytes;
+        for (int r = 0; r < pl.nranks; r++) {
+            const int64_t w = pl.width[r];
+            const uint8_t* src = pl.src[r] + row * w;
+            if (pl.vec) {
+                for (int64_t j = threadIdx.x * 16; j < w; j += 256 * 16)
+                    *reinterpret_cast<uint4*>(dst + pl.col0[r] + j) = __ldcs(reinterpret_cast<const uint4*>(src + j));
+            } else {
+                for (int64_t j = threadIdx.x; j < w; j += 256) dst[pl.col0[r] + j] = src[j];
+            }
+        }
+    }
+}
+
 og_comm* live(og_comm* c) {
     if (c == nullptr || c->nccl == nullptr)
         throw OgError{OG_ERROR_INVALID_HANDLE, kComm, "comm", "null communicator", "", "", ""};
@@ -153,6 +184,9 @@ OG_API og_status og_comm_gather_columns(og_comm* comm, const void* shard, int32_
             shape(kComm, "elemBytes", "must be 1, 2, 4 or 8, got " + std::to_string(elem_bytes));
         if (batch < 1) shape(kComm, "batch", "must be at least 1, got " + std::to_string(batch));
         if (m < 0) shape(kComm, "m", "must not be negative, got " + std::to_string(m));
+        if (comm->nranks > kMaxPlaceRanks)
+            unsupported(kComm, "a column gather over more than 64 ranks", "Ranks", "at most 64",
+                        std::to_string(comm->nranks));
         if (root < 0 || root >= comm->nranks)
             shape(kComm, "root", std::to_string(root) + " is outside [0, " + std::to_string(comm->nranks) + ")");
         int64_t n = 0;
@@ -174,8 +208,8 @@ OG_API og_status og_comm_gather_columns(og_comm* comm, const void* shard, int32_
             if (mine > 0) check_nccl(api.send(shard, size_t(mine), ncclChar, root, comm->nccl, s), "ncclSend");
             return;
         }
-        // Root: receive every other shard into the staging buffer, then put each one (and its own) in place with a
-        // pitched copy: shard r's row i lands at columns [col0[r], col0[r] + widths[r]) of output row i.
+        // Root: receive every other shard into the staging buffer, then put each one (and its own) in place with one
+        // kernel: shard r's row i lands at columns [col0[r], col0[r] + widths[r]) of output row i.
         std::vector<int64_t> at(comm->nranks, 0);
         int64_t need = 0;
         for (int r = 0; r < comm->nranks; r++) {
@@ -205,16 +239,22 @@ OG_API og_status og_comm_gather_columns(og_comm* comm, const void* shard, int32_
             }
         }
         check_nccl(api.group_end(), "ncclGroupEnd");
-        uint8_t* dst = static_cast<uint8_t*>(out);
-        const size_t pitch = size_t(n) * elem_bytes;
+        Placement pl = {};
+        pl.nranks = comm->nranks;
+        pl.row_bytes = n * elem_bytes;
+        pl.rows = rows;
+        bool vec = (reinterpret_cast<uintptr_t>(out) & 15) == 0 && (pl.row_bytes & 15) == 0;
         for (int r = 0; r < comm->nranks; r++) {
-            if (widths[r] == 0) continue;
-            const void* src = r == root ? shard : stage + at[r];
-            const size_t w = size_t(widths[r]) * elem_bytes;
-            check_cuda(cudaMemcpy2DAsync(dst + col0[r] * elem_bytes, pitch, src, w, w, size_t(rows),
-                                         cudaMemcpyDeviceToDevice, s),
-                       "gather placement");
+            pl.src[r] = static_cast<const uint8_t*>(r == root ? shard : stage + at[r]);
+            pl.col0[r] = col0[r] * elem_bytes;
+            pl.width[r] = int64_t(widths[r]) * elem_bytes;
+            vec = vec && (reinterpret_cast<uintptr_t>(pl.src[r]) & 15) == 0 && (pl.col0[r] & 15) == 0 &&
+                  (pl.width[r] & 15) == 0;
         }
+        pl.vec = vec ? 1 : 0;
+        const int grid = static_cast<int>(std::min<int64_t>(rows, int64_t(comm->device->sm_count) * 8));
+        place_columns_kernel<<<grid, 256, 0, s>>>(pl, static_cast<uint8_t*>(out));
+        check_cuda(cudaGetLastError(), "gather placement");
     });
 }
 

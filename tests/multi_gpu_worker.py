@@ -40,6 +40,7 @@ def gather_rank(rank: int, nranks: int, id_queues, results, m: int, n: int, k: i
                 enc = dev.begin_commands()
                 gemm.encode_int32(enc, og.Int8GemmProblem(m, part.width, k), ba, bb, bc, og.Int8Operand(bza, 0),
                                   og.Int8Operand(bzb, 0, True))
+                kernel = gemm.last_kernel
                 dev.submit(enc)
                 comm.gather_columns(bc.ptr, 4, 1, m, widths, full.ptr if full is not None else 0, root=0)
                 # The operand replicated the other way: each rank holds one part of A, all_gather gives all of A.
@@ -49,7 +50,7 @@ def gather_rank(rank: int, nranks: int, id_queues, results, m: int, n: int, k: i
                 comm.all_gather(mine.ptr, rows * k, everything.ptr)
                 dev.wait_idle()
                 replicated_ok = bool(np.array_equal(everything.read(), a[:nranks * rows * k]))
-            out = {"rank": rank, "replicated_ok": replicated_ok, "kernel": gemm.last_kernel}
+            out = {"rank": rank, "replicated_ok": replicated_ok, "kernel": kernel}
             if rank == 0:
                 got = full.read()
                 want = oracle.int8_gemm(a, False, b.reshape(-1), True, za, False, zb, True, m=m, n=n, k=k)

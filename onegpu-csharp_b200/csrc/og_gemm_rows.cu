@@ -29,16 +29,27 @@ namespace rows {
 constexpr int BN = 128;          // columns of B (rows of the MMA) per CTA
 constexpr int BK = 128;
 constexpr int MAXM = 16;         // rows of A = N of the MMA
-constexpr int STAGES = 6;
+// Stages of B in flight per CTA. Measured on B200, the decode config runs faster with 4 than with 6 (45.1 against
+// 48.0 us at 16 x 28672 x 8192): fewer rows of B open at once keep the CTAs' DRAM reads closer together.
+constexpr int STAGES = 4;
+constexpr int SUMS_STAGES = 6;  // the byte-sums kernel's ring
 constexpr int B_BYTES = BN * BK;          // 16 KB
 constexpr int A_BYTES = MAXM * BK;        // 2 KB
 constexpr int ONES_BYTES = MAXM * BK;     // 16 rows of ones, shared by every stage
 constexpr int THREADS = 192;
-constexpr int TMEM_COLS = 32;             // columns 0..15 dot products, 16..31 column sums of B
+// Four accumulators, one per K = 32 step of a K block: consecutive MMAs of a block write different accumulators, so
+// they do not wait for one another (an N = 16 MMA is short next to the latency of the accumulation it depends on; a
+// single accumulator held one CTA to ~29 GB/s of B however many stages were in flight). The epilogue adds them up.
+constexpr int ACCS = 4;
+constexpr int ACC_COLS = 32;                   // per accumulator: columns 0..15 dot products, 16..31 column sums of B
+constexpr int TMEM_COLS = ACCS * ACC_COLS;     // 128
 constexpr int SMEM_BYTES = STAGES * (B_BYTES + A_BYTES) + ONES_BYTES + 1024 + 256;
 }  // namespace rows
 
-constexpr int SUMS_SMEM_BYTES = rows::STAGES * rows::B_BYTES + rows::ONES_BYTES + 1024 + 256;
+constexpr int SUMS_SMEM_BYTES = rows::SUMS_STAGES * rows::B_BYTES + rows::ONES_BYTES + 1024 + 256;
+// The split kernel holds two 128-column TMEM accumulators per CTA: at most two CTAs per SM (4 x 256 = 512 columns),
+// which a request of more than a third of an SM's shared memory guarantees.
+constexpr int STREAM_SMEM_BYTES = rows::SMEM_BYTES > 80 * 1024 ? rows::SMEM_BYTES : 80 * 1024;
 
 struct RowsParams {
     int m, n, k;
@@ -62,6 +73,23 @@ struct RowsParams {
 
 // One partial record: the 16 x 128 dot products, the 128 column sums of B, the 16 row sums of A of a K range.
 constexpr int PART_INTS = 17 * rows::BN + rows::MAXM;
+
+// The 32 columns of this thread's TMEM lane summed over the accumulators (addition modulo 2^32). A product of
+// fewer than ACCS K steps leaves the later accumulators unwritten, so only those written are read (every K block
+// holds ACCS steps, so any K block count writes all of them).
+__device__ __forceinline__ void tmem_ld_sum(uint32_t taddr, int k_blocks, uint32_t (&r)[32]) {
+    tmem_ld_32x32b_x32(taddr, r);
+    tmem_ld_wait();
+    if (k_blocks < 1) return;
+#pragma unroll 1
+    for (int a = 1; a < rows::ACCS; a++) {
+        uint32_t t[32];
+        tmem_ld_32x32b_x32(taddr + a * rows::ACC_COLS, t);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; i++) r[i] += t[i];
+    }
+}
 
 template <int OUT>
 __device__ __forceinline__ void store_one(const Epilogue& e, int b, int m, int n, uint32_t s) {
@@ -161,10 +189,11 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
                 for (int kk = 0; kk < rows::BK / 32; kk++) {
                     const uint64_t adesc = B_KMAJOR ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
                                                     : smem_desc_sw128(b_addr + kk * 32 * 128, rows::B_BYTES, 1024);
-                    const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
-                    if (!sums_only) mma_i8(tmem_base, adesc, smem_desc_sw128(x_addr + kk * 32, 16, 1024), idesc, acc);
+                    const uint32_t acc = kb != 0 ? 1u : 0u;
+                    const uint32_t d = tmem_base + kk * rows::ACC_COLS;
+                    if (!sums_only) mma_i8(d, adesc, smem_desc_sw128(x_addr + kk * 32, 16, 1024), idesc, acc);
                     if (need_col_sums)
-                        mma_i8(tmem_base + rows::MAXM, adesc, smem_desc_sw128(o_addr + kk * 32, 16, 1024), idesc, acc);
+                        mma_i8(d + rows::MAXM, adesc, smem_desc_sw128(o_addr + kk * 32, 16, 1024), idesc, acc);
                 }
                 mma_commit(&empty[s]);
             }
@@ -223,8 +252,7 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
         if (!mbar_wait(tfull, 0, abort_flag)) goto done;
         tc_fence_after();
         uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16), r);
-        tmem_ld_wait();
+        tmem_ld_sum(tmem_base + (static_cast<uint32_t>(q * 32) << 16), kb_count, r);
         const int n = tile * rows::BN + q * 32 + lane;
         if (sums_only) {
             if (n < p.n) p.sums_out[blockIdx.z * p.sums_split_stride + b * p.sums_stride + n] = static_cast<int32_t>(r[16]);
@@ -367,12 +395,12 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
                 const uint32_t b_addr = smem_u32(sB + st * rows::B_BYTES);
                 const uint32_t x_addr = smem_u32(sX + st * rows::A_BYTES);
                 const uint32_t o_addr = smem_u32(sOnes);
-                const uint32_t d = tmem_base + acc * rows::TMEM_COLS;
 #pragma unroll
                 for (int kk = 0; kk < rows::BK / 32; kk++) {
+                    const uint32_t d = tmem_base + acc * rows::TMEM_COLS + kk * rows::ACC_COLS;
                     const uint64_t adesc = B_KMAJOR ? smem_desc_sw128(b_addr + kk * 32, 16, 1024)
                                                     : smem_desc_sw128(b_addr + kk * 32 * 128, rows::B_BYTES, 1024);
-                    const uint32_t accum = (first && kk == 0) ? 0u : 1u;
+                    const uint32_t accum = first ? 0u : 1u;
                     mma_i8(d, adesc, smem_desc_sw128(x_addr + kk * 32, 16, 1024), idesc, accum);
                     if (need_col_sums)
                         mma_i8(d + rows::MAXM, adesc, smem_desc_sw128(o_addr + kk * 32, 16, 1024), idesc, accum);
@@ -436,8 +464,8 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
             uint32_t r[32];
             if (ok) {
                 tc_fence_after();
-                tmem_ld_32x32b_x32(tmem_base + acc * rows::TMEM_COLS + (static_cast<uint32_t>((warp & 3) * 32) << 16), r);
-                tmem_ld_wait();
+                tmem_ld_sum(tmem_base + acc * rows::TMEM_COLS + (static_cast<uint32_t>((warp & 3) * 32) << 16),
+                            kb1 - kb0, r);
             }
             tc_fence_before();
             __syncwarp();
@@ -544,12 +572,12 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* sB = smem;                                   // [STAGES][128 rows or columns x 128 k]
-    uint8_t* sOnes = sB + rows::STAGES * rows::B_BYTES;   // [16 rows x 128 k] of ones
+    uint8_t* sOnes = sB + rows::SUMS_STAGES * rows::B_BYTES;   // [16 rows x 128 k] of ones
     uint64_t* bars = reinterpret_cast<uint64_t*>(sOnes + rows::ONES_BYTES);
     uint64_t* full = bars;
-    uint64_t* empty = bars + rows::STAGES;
-    uint64_t* tfull = bars + 2 * rows::STAGES;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * rows::STAGES + 1);
+    uint64_t* empty = bars + rows::SUMS_STAGES;
+    uint64_t* tfull = bars + 2 * rows::SUMS_STAGES;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 2 * rows::SUMS_STAGES + 1);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5;
@@ -570,7 +598,7 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
         reinterpret_cast<uint4*>(sOnes)[i] = make_uint4(0x01010101u, 0x01010101u, 0x01010101u, 0x01010101u);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> visible to the tensor cores
     if (threadIdx.x == 0) {
-        for (int s = 0; s < rows::STAGES; s++) {
+        for (int s = 0; s < rows::SUMS_STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -592,8 +620,8 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
 
     if (warp == 0) {
         for (int kb = 0; kb < kb_count; kb++) {
-            const int s = kb % rows::STAGES;
-            const uint32_t ph = (kb / rows::STAGES) & 1;
+            const int s = kb % rows::SUMS_STAGES;
+            const uint32_t ph = (kb / rows::SUMS_STAGES) & 1;
             const int kc = (kb_begin + kb) * rows::BK;
             if (!mbar_wait(&empty[s], ph ^ 1, abort_flag)) goto done;
             if (lane == 0) {
@@ -607,8 +635,8 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
         }
     } else if (warp == 1) {
         for (int kb = 0; kb < kb_count; kb++) {
-            const int s = kb % rows::STAGES;
-            const uint32_t ph = (kb / rows::STAGES) & 1;
+            const int s = kb % rows::SUMS_STAGES;
+            const uint32_t ph = (kb / rows::SUMS_STAGES) & 1;
             if (!mbar_wait(&full[s], ph, abort_flag)) goto done;
             tc_fence_after();
             if (lane == 0) {
@@ -618,8 +646,8 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
                 for (int kk = 0; kk < rows::BK / 32; kk++) {
                     const uint64_t tdesc = job.kmajor ? smem_desc_sw128(t_addr + kk * 32, 16, 1024)
                                                       : smem_desc_sw128(t_addr + kk * 32 * 128, rows::B_BYTES, 1024);
-                    mma_i8(tmem_base, tdesc, smem_desc_sw128(o_addr + kk * 32, 16, 1024), job.idesc,
-                           (kb | kk) != 0 ? 1u : 0u);
+                    mma_i8(tmem_base + kk * rows::MAXM, tdesc, smem_desc_sw128(o_addr + kk * 32, 16, 1024), job.idesc,
+                           kb != 0 ? 1u : 0u);
                 }
                 mma_commit(&empty[s]);
             }
@@ -631,12 +659,15 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
         const int q = warp & 3;
         if (!mbar_wait(tfull, 0, abort_flag)) goto done;
         tc_fence_after();
-        uint32_t r[32];
+        // Accumulator kk (one per K = 32 step of a block) holds its sum in all 16 of its columns kk*16 .. +15.
+        uint32_t r[32], t[32];
         tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16), r);
+        tmem_ld_32x32b_x32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + 32, t);
         tmem_ld_wait();
+        const uint32_t sum = r[0] + r[16] + t[0] + t[16];
         const int c = tile * rows::BN + q * 32 + lane;
         if (c < job.cols)
-            job.out[(static_cast<int64_t>(split) * job.batches + b) * job.cols + c] = static_cast<int32_t>(r[0]);
+            job.out[(static_cast<int64_t>(split) * job.batches + b) * job.cols + c] = static_cast<int32_t>(sum);
         tc_fence_before();
     }
 
@@ -690,26 +721,28 @@ static LaunchFn bind_rows_stream_t(const RowsParams& p, const CUtensorMap& ma, c
         if (e != cudaSuccess) return e;
         const uint64_t bit = uint64_t(1) << (dev & 63);
         if (!(configured.load() & bit)) {
-            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, rows::SMEM_BYTES);
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, STREAM_SMEM_BYTES);
             if (e != cudaSuccess) return e;
             configured.fetch_or(bit);
         }
-        return launch_pdl(kern, grid, dim3(rows::THREADS), rows::SMEM_BYTES, stream, ma, mb, p, idesc);
+        return launch_pdl(kern, grid, dim3(rows::THREADS), STREAM_SMEM_BYTES, stream, ma, mb, p, idesc);
     };
 }
 
-// The even split pays when one CTA per column tile would leave most SMs idle: at most one tile for every two SMs.
-// (Measured on B200: 8, 32 and 64 tiles of 8 to 64 K blocks ran 1.3 to 1.8 times faster split; 112 and 224 tiles
-// ran slower, the workers' scattered K positions costing more DRAM locality than the balance gains.) Two workers
-// per SM; each gets at least 8 units.
+// The split pays when one CTA per column tile would leave SMs idle. Measured on B200 with the decode shapes
+// (K = 8192), the best split gives each tile's K blocks to S workers in equal, aligned parts (every worker one
+// segment of one tile) with about one and a half workers per SM: 16 x 14336 34.7 us with 2 parts per tile against
+// 38.9 us unsplit, 16 x 7168 24.7 us with 4 parts, 16 x 3584 22.6 us with 8 parts, against 38.9 us for both unsplit
+// (more workers, or parts not aligned to the tiles, ran slower); 16 x 28672, with 224 tiles, runs unsplit.
 int rows_workers(const GemmLaunch& L) {
     const int64_t tiles = static_cast<int64_t>((L.n + rows::BN - 1) / rows::BN) * L.batch;
     const int64_t kb = (L.k + rows::BK - 1) / rows::BK;
-    const int64_t sms = L.num_sms;
-    if (kb < 16 || sms < 1 || 2 * tiles > sms) return 0;
-    int64_t w = 2 * sms;
-    if (w > tiles * kb / 8) w = tiles * kb / 8;
-    return w < 2 ? 0 : static_cast<int>(w);
+    const int64_t target = 3 * int64_t(L.num_sms) / 2;
+    if (kb < 8 || L.num_sms < 1 || 10 * tiles >= 9 * target) return 0;
+    int64_t parts = (target + tiles / 2) / tiles;       // the nearest whole number of parts per tile
+    if (parts > kb / 4) parts = kb / 4;                  // segments of at least 4 K blocks
+    const int64_t w = tiles * parts;
+    return (parts < 2 || w > 2 * int64_t(L.num_sms)) ? 0 : static_cast<int>(w);
 }
 
 int64_t rows_part_ints(const GemmLaunch&, int workers) { return static_cast<int64_t>(workers) * 2 * PART_INTS; }

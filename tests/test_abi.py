@@ -39,6 +39,48 @@ def test_every_entry_point_has_a_csharp_binding():
     assert bound == declared_symbols()
 
 
+# The members of Int8Gemm and DynamicQuantizeKernels in the reference's shipped API
+# (src/RecursiveAI.OneGpu.Kernels/PublicAPI.Shipped.txt:491-548), with the entry point each C# body must call.
+SHIPPED_MEMBERS = {
+    "Int8Gemm.cs": [
+        ("public Int8Gemm(GpuDevice device, Int8GemmOptions? options = null, int maxCachedBindGroups = 1024)",
+         "og_int8_gemm_create"),
+        ("public string Variant", "og_int8_gemm_variant"),
+        ("public int BindGroupsCreated", "og_int8_gemm_bind_groups_created"),
+        ("public void ReserveScratch(long elements)", "og_int8_gemm_reserve_scratch"),
+        ("public void ReleaseBindings()", None),
+        ("public void EncodeInt32<TA, TB>(", "og_int8_gemm_encode_int32"),
+        ("public void EncodeFloat<TA, TB>(", "og_int8_gemm_encode_float"),
+        ("public void EncodeRequantized<TA, TB, TY>(", "og_int8_gemm_encode_requantized"),
+        ("public void Dispose()", "og_int8_gemm_destroy"),
+        ("public DynamicQuantizeKernels(GpuDevice device, int maxCachedBindGroups = 1024)",
+         "og_dynamic_quantize_create"),
+        ("public void Encode(GpuCommandEncoder encoder, GpuBuffer<float> x, int offsetX, int count, GpuBuffer<byte> y,",
+         "og_dynamic_quantize_encode"),
+    ],
+}
+
+
+def test_csharp_drop_in_classes_keep_the_shipped_members():
+    """The C# Int8Gemm / DynamicQuantizeKernels of the CUDA backend declare every shipped public member, and each
+    body calls the C entry point it maps to (declared in the header and bound in Native.cs)."""
+    declared = set(declared_symbols())
+    for fname, members in SHIPPED_MEMBERS.items():
+        src = open(os.path.join(CSHARP, fname), encoding="utf-8").read()
+        for signature, entry in members:
+            at = src.find(signature)
+            assert at >= 0, signature
+            if entry is not None:
+                assert entry in declared
+                body = src[at:at + 4000]
+                assert f"Native.{entry}(" in body, (signature, entry)
+    for t in ("public struct Int8GemmProblem", "public readonly record struct Int8Operand<T>(GpuBuffer<T> Buffer, int "
+              "Offset, bool IsVector = false)", "public readonly record struct Int8Scratch(GpuBuffer<int> Buffer, int "
+              "Offset = 0)", "public sealed class Int8GemmOptions", "public bool AllowPackedDot { get; init; } = true;",
+              "public readonly double Ops"):
+        assert t in open(os.path.join(CSHARP, "Int8Gemm.cs"), encoding="utf-8").read(), t
+
+
 def test_no_device_here_is_reported_not_crashed():
     if og.device_count() > 0:
         pytest.skip("a CUDA device is visible")

@@ -173,11 +173,13 @@ __device__ __forceinline__ void fold4(const float4& v, float& mn, float& mx) {
 }
 
 // clamp(round_half_even(x / s) + zero point, 0, 255) with the quotient rule of rne_quotient_r, returned in the low
-// byte. Where the rule accepts m = RN(x * r) (|m| < 2^19, away from half-integers), t = RN(m + cz) with cz = zero
-// point + 1.5 * 2^23 lies in [2^23, 2^24), where floats are the integers: t = cz + round(m) exactly, t - cz gives
-// round(m) for the rule's test, and t's bits (0x4B400000 + round(m) + zero point, monotonic in t) are clamped to
+// byte. Where the rule accepts m = RN(x * r) (away from half-integers), t = RN(m + cz) with cz = zero point +
+// 1.5 * 2^23 lies in [2^23, 2^24), where floats are the integers: t = cz + round(m) exactly, t - cz gives round(m) for
+// the rule's test, and t's bits (0x4B400000 + round(m) + zero point, monotonic in t) are clamped to
 // [0x4B400000, 0x4B4000FF] with integer min / max, leaving the byte in the low 8 bits. Elsewhere the quotient is
-// divided exactly and clamped in floating point (NaN to 0).
+// divided exactly and clamped in floating point (NaN to 0). Here the scale is the tensor's own range over 255, so
+// every finite x has |x / s| <= 255 and |m| <= 256: the rule's margin |m| 2^-20 + 2^-19 is then below 2^-11, and
+// the test is |d| < 1/2 - 2^-11 (NaN, infinities and a non-normal reciprocal fail it and take the exact path).
 struct DqQuant {
     float s, r, zf, cz;
     bool r_ok;
@@ -185,8 +187,7 @@ struct DqQuant {
         const float m = __fmul_rn(x, r);
         const float t = __fadd_rn(m, cz);
         const float d = __fsub_rn(m, __fsub_rn(t, cz));
-        if (r_ok && __fmaf_rn(fabsf(m), 0x1p-20f, fabsf(d)) < 0.5f - 0x1p-19f)
-            return min(max(__float_as_uint(t), 0x4B400000u), 0x4B4000FFu);
+        if (r_ok && fabsf(d) < 0.5f - 0x1p-11f) return min(max(__float_as_uint(t), 0x4B400000u), 0x4B4000FFu);
         return saturate_byte<false>(__fadd_rn(rne_quotient_exact(x, s), zf));
     }
     __device__ __forceinline__ uint32_t four(const float4& v) const {

@@ -83,16 +83,20 @@ struct TcParams {
     int32_t* sk_part;       // [slots][CG][8 chunks][8 quads][128 rows][4] int32
     unsigned int* sk_flag;  // [slots] flags, then the generation and the ticket
     int sk_slots;
-    // Split tail (int32 results): tiles [0, dp_tiles) are whole tiles dealt round-robin to the workers; the K blocks
-    // of the remaining tiles (tail_units of them) are split into equal contiguous ranges over the first tail_workers
-    // workers, each worker taking its range before its whole tiles. The tail tiles are put together in C itself:
-    // every CTA first clears its share of them (the epilogue warps, while the first MMAs run) and counts itself in
-    // tail_zeroed; then every segment adds its sums with TMA reductions, after that count is complete, the segment
-    // holding K block 0 of its tile adding the zero-point terms and bias too. The last CTA to finish sets the count
-    // back to zero, with the stream-K generation and ticket that follow sk_flag's slots.
+    // Split tail (int32 results): tiles [0, dp_tiles) are whole tiles dealt round-robin to the workers; each
+    // remaining tile is cut into tail_parts equal K ranges, and the tail_units = tail tiles x tail_parts pieces,
+    // ordered part by part (piece u is part u / tail tiles of tail tile u % tail tiles), are dealt in equal
+    // contiguous ranges to the first tail_workers workers, each worker taking its range before its whole tiles. The
+    // workers busy with tail pieces at any moment read the same K range of neighbouring tiles, so they share operands
+    // in L2 as a wave of whole tiles does. The tail tiles are put together in C itself: every CTA first clears its
+    // share of them (the epilogue warps, while the first MMAs run) and counts itself in tail_zeroed; then every piece
+    // adds its sums with TMA reductions, after that count is complete, the piece holding K block 0 of its tile adding
+    // the zero-point terms and bias too. The last CTA to finish sets the count back to zero, with the stream-K
+    // generation and ticket that follow sk_flag's slots.
     int tail_split;
     int tail_first;  // a worker takes its tail range before (1) or after (0) its whole tiles
     int dp_tiles;
+    int tail_parts;
     int64_t tail_units;
     int tail_workers;
     unsigned int* tail_zeroed;
@@ -132,12 +136,21 @@ __device__ __forceinline__ bool work_next(const TcParams& p, int workers, WorkCu
         c.tile += workers;
         return true;
     }
+    if (c.u < c.u1 && !p.stream_k) {
+        const int tail_tiles = p.total_tiles - p.dp_tiles;
+        const int part = static_cast<int>(c.u / tail_tiles);
+        w.tile = p.dp_tiles + static_cast<int>(c.u - static_cast<int64_t>(part) * tail_tiles);
+        w.kb0 = static_cast<int>(static_cast<int64_t>(part) * p.k_blocks / p.tail_parts);
+        w.kb1 = static_cast<int>(static_cast<int64_t>(part + 1) * p.k_blocks / p.tail_parts);
+        c.u += 1;
+        return true;
+    }
     if (c.u < c.u1) {
         const int t = static_cast<int>(c.u / p.k_blocks);
         w.kb0 = static_cast<int>(c.u - static_cast<int64_t>(t) * p.k_blocks);
         const int64_t end = static_cast<int64_t>(w.kb0) + (c.u1 - c.u);
         w.kb1 = end < p.k_blocks ? static_cast<int>(end) : p.k_blocks;
-        w.tile = p.stream_k ? t : p.dp_tiles + t;
+        w.tile = t;
         c.u += w.kb1 - w.kb0;
         return true;
     }
@@ -655,7 +668,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
                 continue;
             }
             const int32_t* sk_in = sk_wait ? reinterpret_cast<const int32_t*>(sA) : nullptr;
-            // The zero-point terms and the bias enter C once: with the K-block-0 segment of a tail tile.
+            // The zero-point terms and the bias enter C once: with the K-block-0 piece of a tail tile.
             const bool with_terms = terms && (!reduce || wi.kb0 == 0);
             if (with_terms) {  // every warp has left the previous tile (the barrier above), so its terms are free
                 fill_col_terms(terms_smem, e, b, tn * tc::BN, threadIdx.x - 64, tc::EPI_THREADS);
@@ -870,36 +883,42 @@ static LaunchFn bind_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensor
     };
 }
 
-// The split tail of an int32 product: its tiles beyond the last full wave of whole tiles, split in K over as many
-// workers as get at least TAIL_MIN_BLOCKS K blocks each, when the last wave would leave at least half of the workers
-// idle. Measured on B200, the split segments run below the whole tiles' K-block rate (their operands are shared by
-// fewer concurrent tiles in L2) and add a reduction pass over the tail, so a nearly full last wave is faster left
-// whole: 8192 x 1024 x 8192 (54 tail tiles over 74 CTA pairs) 59.4 us split against 57.3 us whole, while
-// 2048 x 12288 x 4096 (14 tail tiles) takes 75.8 us split against 79.9 us whole. The cut tiles are put together in C
-// with TMA reductions, so C's rows must allow TMA stores.
+// The split tail of an int32 product: the tiles beyond the last full wave of whole tiles are cut into P equal K
+// ranges and the pieces dealt, part by part, over the workers. A worker then spends ceil(tail tiles x P / workers)
+// pieces of 1/P tile on the tail instead of one whole tile; P (2..8, each piece at least TAIL_MIN_BLOCKS K blocks)
+// minimises that fraction, and the tail is split only when it is at most TAIL_MAX_FRACTION of a tile. Every piece
+// costs an epilogue and a TMA reduction of a whole tile's sums into C (L2 read-modify-write traffic that competes
+// with the operand loads), so a split must at least halve the tail. Measured on B200 with zero points (the byte-sums pass included):
+// 8192 x 2048 x 8192 111.8 us in halves against 119.8 us whole, 4096^3 68.6 against 70.7 us, while quarters of
+// 8192 x 1024 x 8192 (54 tail tiles, three quarters per pair) took 80.9 us against 74.9 us whole and thirds of the
+// batched 8 x 2048 x 12288 x 4096 558 against 547 us. The cut tiles are put together in C with TMA reductions, so C's
+// rows must allow TMA stores.
 constexpr int TAIL_MIN_BLOCKS = 8;
+constexpr double TAIL_MAX_FRACTION = 0.5;
 
 struct TailPlan {
-    int dp_tiles = 0, workers = 0;
+    int dp_tiles = 0, workers = 0, parts = 0;
     int64_t units = 0;
 };
 
 static TailPlan tail_plan(int64_t tiles, int64_t k_blocks, int64_t workers) {
     TailPlan t;
+    t.dp_tiles = static_cast<int>(tiles);
     const int64_t rem = tiles % workers;
+    if (rem == 0) return t;
+    double best = 2.0;
+    for (int parts = 2; parts <= 8 && k_blocks / parts >= TAIL_MIN_BLOCKS; parts++) {
+        const int64_t units = rem * parts;
+        const double fraction = static_cast<double>((units + workers - 1) / workers) / parts;
+        if (fraction <= TAIL_MAX_FRACTION + 1e-9 && fraction < best - 1e-9) {
+            best = fraction;
+            t.parts = parts;
+            t.units = units;
+        }
+    }
+    if (t.parts == 0) return t;
     t.dp_tiles = static_cast<int>(tiles - rem);
-    if (rem == 0 || 2 * rem > workers) {
-        t.dp_tiles = static_cast<int>(tiles);
-        return t;
-    }
-    t.units = rem * k_blocks;
-    const int64_t w = std::min<int64_t>(workers, t.units / TAIL_MIN_BLOCKS);
-    if (w <= rem) {
-        t.units = 0;
-        t.dp_tiles = static_cast<int>(tiles);
-        return t;
-    }
-    t.workers = static_cast<int>(w);
+    t.workers = static_cast<int>(std::min<int64_t>(workers, t.units));
     return t;
 }
 
@@ -1013,6 +1032,7 @@ static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
     p.tail_split = 0;
     p.tail_first = 1;
     p.dp_tiles = static_cast<int>(total);
+    p.tail_parts = 0;
     p.tail_units = 0;
     p.tail_workers = 0;
     p.tail_zeroed = nullptr;
@@ -1021,6 +1041,7 @@ static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
         if (t.workers > 0) {
             p.tail_split = 1;
             p.dp_tiles = t.dp_tiles;
+            p.tail_parts = t.parts;
             p.tail_units = t.units;
             p.tail_workers = t.workers;
             p.tail_zeroed = L.sk_flag + p.sk_slots + 2;

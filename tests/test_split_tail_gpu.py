@@ -1,13 +1,13 @@
 """The split tail of the tensor-core int32 product, bit for bit against the oracle.
 
 When the tiles of a product leave at least half of the SM pairs (or of the SMs, one-SM tile) idle in the last wave,
-the tiles past the last full wave are split in K over the workers; a tile cut between workers is stored once, with its
-zero-point terms and bias, by the first segment to finish, and the others add their raw sums into C with TMA
-reductions. Integer addition modulo 2^32 is exact in any order, so C must equal the definition bit for bit. The
-cases cover a partial wave after full ones, fewer tiles than workers, ragged M, N and K edges, every zero-point
-mode and signedness, a bias, batched A, B stored N x K, the one-SM tile, the per-shard shapes of the square
-benchmark product split over 4 and 8 GPUs, and products recorded back to back (the claim words carry the launch's
-generation and are never cleared).
+the tiles past the last full wave are cut into equal K ranges dealt over the workers. Every piece of a cut tile adds
+its sums into C (cleared first) with TMA reductions, the K-block-0 piece with the zero-point terms and the bias;
+integer addition modulo 2^32 is exact in any order, so C must equal the definition bit for bit. The cases cover a
+partial wave after full ones, fewer tiles than workers, ragged M, N and K edges, every zero-point mode and
+signedness, a bias, batched A, B stored N x K, the one-SM tile, the per-shard shapes of the square benchmark product
+split over 4 and 8 GPUs, and products recorded back to back (the count of cleared shares goes back to zero at the
+end of every launch).
 """
 import numpy as np
 import pytest
@@ -108,15 +108,35 @@ def test_split_tail_products_back_to_back(device):
         assert bad == 0
 
 
-def test_whole_tiles_option_and_other_outputs_do_not_split(device):
-    """Option stream_k = 1 keeps whole tiles; the float and requantized forms always do (their epilogue is not
-    additive). Both agree with the split product bit for bit."""
+def test_whole_tiles_option_does_not_split(device):
+    """Option stream_k = 1 keeps whole tiles; both agree with the split product bit for bit."""
     c = align_case(Case("whole", problem(2048, 2560, 2048), False, True, 1, 2))
     with og.Int8Gemm(device, og.Int8GemmOptions(stream_k=1)) as whole, og.Int8Gemm(device) as split:
         bad_w, kw = run_int32(device, whole, c, 77)
         bad_s, ks = run_int32(device, split, c, 77)
         assert bad_w == 0 and bad_s == 0
         assert kw == "tensor-core-2sm" and ks == "tensor-core-2sm-split-tail"
+
+
+def test_other_outputs_do_not_split(device):
+    """The float and requantized forms keep whole tiles (their epilogue is not additive) and agree with the oracle."""
+    with og.Int8Gemm(device) as gemm:
+        a = device.create_buffer(np.uint8, 2048 * 2048)
+        b = device.create_buffer(np.int8, 2048 * 2560)
+        y = device.create_buffer(np.uint8, 2048 * 2560)
+        f = device.create_buffer(np.float32, 2048 * 2560)
+        s = device.create_buffer(np.float32, np.array([0.001], np.float32))
+        try:
+            enc = device.begin_commands()
+            gemm.encode_requantized(enc, og.Int8GemmProblem(2048, 2560, 2048), a, b, y, og.Int8Operand(s, 0), 128)
+            assert gemm.last_kernel == "tensor-core-2sm"
+            gemm.encode_float(enc, og.Int8GemmProblem(2048, 2560, 2048), a, b, f, og.Int8Operand(s, 0))
+            assert gemm.last_kernel == "tensor-core-2sm"
+            device.submit(enc)
+            device.wait_idle()
+        finally:
+            for v in (a, b, y, f, s):
+                v.dispose()
 
 
 @pytest.mark.parametrize("shards", [4, 8])
@@ -146,7 +166,8 @@ def test_square_product_shards_are_bit_exact(device, shards):
                 want = oracle.int8_gemm(a.view(np.uint8), True, b.view(np.uint8), True,
                                         za.view(np.uint8) if zp else None, False, zb.view(np.uint8) if zp else None,
                                         True, m=m, n=n, k=k)
-                # 4 shards: 256 tiles, a last wave of 34 over 74 pairs (split); 8 shards: 128 tiles (whole)
+                # 4 shards: 256 tiles, a last wave of 34 over 74 pairs (split in halves); 8 shards: 128 tiles, 54
+                # past the first wave (left whole)
                 assert kernel == ("tensor-core-2sm-split-tail" if shards == 4 else "tensor-core-2sm")
                 assert np.array_equal(got, want), f"{int(np.count_nonzero(got != want))} sums differ (zp {zp})"
     finally:

@@ -498,14 +498,29 @@ __global__ void __launch_bounds__(rows::THREADS, 2)
                     const int64_t tu0 = static_cast<int64_t>(t) * kbt;
                     const int w_first = rows_owner(tu0, p.units, workers);
                     const int w_last = rows_owner(tu0 + kbt - 1, p.units, workers);
+                    // The other segments' records, four at a time: all their loads are in flight together.
                     int32_t rs = 0;
-                    for (int w = w_first; w <= w_last; w++) {
-                        if (w == worker) continue;
-                        const int wslot = p.units * w / workers >= tu0 ? 0 : 1;  // its first segment, or its last
-                        const int32_t* rec = p.split_part + (static_cast<int64_t>(w) * 2 + wslot) * PART_INTS;
+                    for (int w0 = w_first; w0 <= w_last; w0 += 4) {
+                        uint32_t vals[4][17];
+                        int32_t rsv[4];
 #pragma unroll
-                        for (int v = 0; v < 17; v++) r[v] += static_cast<uint32_t>(__ldcg(rec + v * rows::BN + col));
-                        if (t128 < rows::MAXM) rs += __ldcg(rec + 17 * rows::BN + t128);
+                        for (int j = 0; j < 4; j++) {
+                            const int w = w0 + j;
+                            const bool use = w <= w_last && w != worker;
+                            const int wslot = p.units * w / workers >= tu0 ? 0 : 1;  // its first segment, or its last
+                            const int32_t* rec = p.split_part + (static_cast<int64_t>(use ? w : worker) * 2 + wslot) *
+                                                                    PART_INTS;
+#pragma unroll
+                            for (int v = 0; v < 17; v++)
+                                vals[j][v] = use ? static_cast<uint32_t>(__ldcg(rec + v * rows::BN + col)) : 0u;
+                            rsv[j] = (use && t128 < rows::MAXM) ? __ldcg(rec + 17 * rows::BN + t128) : 0;
+                        }
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+#pragma unroll
+                            for (int v = 0; v < 17; v++) r[v] += vals[j][v];
+                            rs += rsv[j];
+                        }
                     }
                     if (t128 < rows::MAXM) row_sum[t128] += rs;
                     asm volatile("bar.sync 1, 128;" ::: "memory");

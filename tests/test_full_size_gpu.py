@@ -118,9 +118,12 @@ def test_config_4_every_element(device):
         v.dispose()
 
 
-def test_config_5_int32_and_dequantized_every_element(device):
-    m, n, k = 16, 28672, 8192
-    rng = np.random.default_rng(5)
+@pytest.mark.parametrize("n", [28672, 14336, 7168, 3584])
+def test_config_5_int32_and_dequantized_every_element(device, n):
+    """Config 5 whole and as the column shard one GPU computes at 2, 4 and 8 GPUs (the shards split K across the
+    workers and meet through records), int32 and dequantized, every element."""
+    m, k = 16, 8192
+    rng = np.random.default_rng(5 + n)
     a = rng.integers(0, 256, size=m * k, dtype=np.int16).astype(np.uint8)
     b = rng.integers(-127, 128, size=k * n, dtype=np.int16).astype(np.int8)
     zb = rng.integers(-4, 5, size=n).astype(np.int8)

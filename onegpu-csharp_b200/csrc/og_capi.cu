@@ -140,7 +140,36 @@ struct og_readback {
     og_device* device = nullptr;
     cudaEvent_t done = nullptr;
     int* status_host = nullptr;  // the device's failure word as it stood when the copy ran
+    int word = -1;               // its index among the device's pinned words, or -1 when it was page-locked alone
 };
+
+namespace {
+
+// A pinned word for one readback: one of the device's, or (all of them in flight) one of its own.
+void take_status_word(og_device* d, og_readback* r) {
+    {
+        std::lock_guard<std::mutex> g(d->readback_mu);
+        if (!d->readback_free.empty()) {
+            r->word = d->readback_free.back();
+            d->readback_free.pop_back();
+            r->status_host = d->readback_words + r->word;
+            return;
+        }
+    }
+    check_cuda(cudaMallocHost(&r->status_host, sizeof(int)), "ReadAsync");
+}
+
+void give_status_word(og_readback* r) {
+    if (r->word >= 0) {
+        std::lock_guard<std::mutex> g(r->device->readback_mu);
+        r->device->readback_free.push_back(r->word);
+    } else if (r->status_host != nullptr) {
+        cudaFreeHost(r->status_host);
+    }
+    r->status_host = nullptr;
+}
+
+}  // namespace
 
 struct og_graph {
     og_device* device = nullptr;
@@ -696,11 +725,15 @@ OG_API og_status og_device_create(int32_t ordinal, og_device** out) {
             check_cuda(cudaMalloc(&d->status, sizeof(int)), "cudaMalloc");
             check_cuda(cudaMemset(d->status, 0, sizeof(int)), "cudaMemset");
             check_cuda(cudaMallocHost(&d->status_host, sizeof(int)), "cudaMallocHost");
+            check_cuda(cudaMallocHost(&d->readback_words, kReadbackWords * sizeof(int)), "cudaMallocHost");
+            d->readback_free.reserve(kReadbackWords);
+            for (int i = kReadbackWords - 1; i >= 0; i--) d->readback_free.push_back(i);
         } catch (...) {
             if (d->stream) cudaStreamDestroy(d->stream);
             if (d->upload) cudaStreamDestroy(d->upload);
             if (d->readback) cudaStreamDestroy(d->readback);
             if (d->status) cudaFree(d->status);
+            if (d->status_host) cudaFreeHost(d->status_host);
             delete d;
             throw;
         }
@@ -720,6 +753,7 @@ OG_API og_status og_device_destroy(og_device* d) {
         cudaStreamDestroy(d->readback);
         cudaFree(d->status);
         cudaFreeHost(d->status_host);
+        cudaFreeHost(d->readback_words);
         delete d;
     });
 }
@@ -860,7 +894,7 @@ OG_API og_status og_buffer_read_async(og_device* d, void* dst, const void* src, 
         r->device = d;
         try {
             cudaEvent_t submitted = nullptr;
-            check_cuda(cudaMallocHost(&r->status_host, sizeof(int)), "ReadAsync");
+            take_status_word(d, r);
             check_cuda(cudaEventCreateWithFlags(&submitted, cudaEventDisableTiming), "ReadAsync");
             cudaError_t e = cudaEventRecord(submitted, d->stream);  // everything submitted so far
             if (e == cudaSuccess) e = cudaStreamWaitEvent(d->readback, submitted, 0);
@@ -874,7 +908,7 @@ OG_API og_status og_buffer_read_async(og_device* d, void* dst, const void* src, 
             check_cuda(cudaEventRecord(r->done, d->readback), "ReadAsync");
         } catch (...) {
             if (r->done) cudaEventDestroy(r->done);
-            if (r->status_host) cudaFreeHost(r->status_host);
+            give_status_word(r);
             delete r;
             throw;
         }
@@ -889,7 +923,7 @@ OG_API og_status og_readback_wait(og_readback* r) {
             og_readback* r;
             ~Release() {
                 cudaEventDestroy(r->done);
-                cudaFreeHost(r->status_host);
+                give_status_word(r);
                 delete r;
             }
         } release{r};

@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <functional>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -23,7 +24,16 @@ struct og_device {
     int* status_host = nullptr;  // pinned mirror for readbacks
     cudaStream_t upload = nullptr;    // copy-engine stream of og_buffer_write_async
     cudaStream_t readback = nullptr;  // copy-engine stream of og_buffer_read_async
+    // Pinned status words of the asynchronous readbacks (one per readback in flight), page-locked once with the
+    // device: locking a word per readback and releasing it at the wait (cudaFreeHost synchronises the whole device)
+    // would drain the transfer pipeline at every wait, so the uploads of the next step could not overlap the readback
+    // of the last one.
+    int* readback_words = nullptr;
+    std::vector<int> readback_free;  // indices of the unused words
+    std::mutex readback_mu;
 };
+
+constexpr int kReadbackWords = 1024;
 
 // One recorded piece of work: launches on the stream it is given.
 using OgOp = std::function<cudaError_t(cudaStream_t)>;

@@ -52,3 +52,23 @@ def test_pipelined_steps_are_bit_exact(device):
         gemm.dispose()
         pin_in.dispose()
         pin_out.dispose()
+
+
+@pytest.mark.gpu
+def test_more_readbacks_in_flight_than_pinned_status_words(device):
+    """Readbacks take one of the device's 1024 page-locked status words each, and one page-locked on its own once all
+    are in flight: 1100 readbacks of distinct words queued before any wait all land, and the words return to the
+    device's pool (a second round works the same)."""
+    count = 1100
+    src = device.create_buffer(np.int32, np.arange(count, dtype=np.int32) * 7 + 1)
+    pin = og.PinnedHost(count * 4)
+    try:
+        for rnd in range(2):
+            pin.view(np.int32, count)[:] = -1
+            tickets = [device.read_async(pin.ptr + 4 * i, src.ptr + 4 * i, 4) for i in range(count)]
+            for t in tickets:
+                t.wait()
+            assert np.array_equal(pin.view(np.int32, count), np.arange(count, dtype=np.int32) * 7 + 1), rnd
+    finally:
+        pin.dispose()
+        src.dispose()

@@ -162,7 +162,9 @@ OG_API og_status og_encoder_begin(og_device* device, og_encoder** out);
  * encoder whatever the outcome. */
 OG_API og_status og_device_submit(og_device* device, og_encoder* encoder);
 OG_API og_status og_encoder_discard(og_encoder* encoder);
-/* Number of kernel launches the encoder holds (GpuCommandEncoder.DispatchCount). */
+/* Number of kernel launches the encoder holds (GpuCommandEncoder.DispatchCount), as planned when the work was
+ * recorded: a DynamicQuantizeLinear counted as its one cooperative kernel runs as two kernels instead if the device
+ * refuses the cooperative launch when the encoder is submitted (fewer SMs available than at recording). */
 OG_API og_status og_encoder_dispatch_count(og_encoder* encoder, int64_t* count);
 
 OG_API og_status og_timestamps_create(og_device* device, uint32_t count, og_timestamps** out);

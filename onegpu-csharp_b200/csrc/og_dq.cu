@@ -285,7 +285,10 @@ __global__ void __launch_bounds__(DQF_THREADS, 1)
     __syncthreads();
     if (failed) {
         if (t == 0) atomicExch(error_flag, 1);
-        if (n_s > 0 && t == 0) {  // no copy may still be landing when the CTA exits (a second bounded wait)
+        // No copy may still be landing when the CTA exits: a second bounded wait for the staged copies of this CTA's
+        // own slice (they depend on no other CTA). If that one runs out too, the CTA exits anyway rather than wait
+        // without a limit; the failure is already raised, and y is not defined after a failed launch.
+        if (n_s > 0 && t == 0) {
             int unraised = 0;
             mbar_wait(&bar, 0, &unraised);
         }

@@ -163,22 +163,25 @@ class ClockSampler:
                 "power_w_max": round(max(s[1] for s in self.samples), 1)}
 
 
-def cpu_gemm_tops(n: int, k: int, threads: int, target_s: float, max_rows: int, seed: int = 0):
-    """Times the oracle's threaded restatement of the reference's int8 product (Int8Tests.Reference) on a sample of
-    rows of A against the whole B, sized to about `target_s` seconds; returns (TOPS, seconds, rows)."""
+def cpu_gemm_tops(n: int, k: int, threads: int, target_s: float, max_rows: int, seed: int = 0, tiled: bool = False):
+    """Times the oracle's threaded restatement of the reference's int8 product (Int8Tests.Reference; with `tiled`, the
+    same sums through the reference portable kernel's 64 x 64 x 16 blocking, Int8GemmKernel.hlsl) on a sample of rows
+    of A against the whole B, sized to about `target_s` seconds; returns (TOPS, seconds, rows)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import og_oracle as oracle
 
     b = oracle.bytes_(k * n, seed + 31)
-    rows = 4
+    rows = 64 if tiled else 4  # the tiled form computes whole 64-row tiles
     while True:
         a = oracle.bytes_(rows * k, seed + 30)
         t0 = time.perf_counter()
-        oracle.int8_gemm(a, True, b, True, m=rows, n=n, k=k, threads=threads)
+        oracle.int8_gemm(a, True, b, True, m=rows, n=n, k=k, threads=threads, tiled=tiled)
         dt = time.perf_counter() - t0
         if dt >= 0.5 * target_s or rows >= max_rows:
             return 2.0 * rows * n * k / dt / 1e12, dt, rows
         rows = int(min(max_rows, max(rows * 2, rows * target_s / max(dt, 1e-3) * 0.9)))
+        if tiled:
+            rows = max(64, rows // 64 * 64)
 
 
 class L2Flush:
@@ -872,6 +875,14 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
                 tops = 2.0 * wl.M * wl.shard_n * wl.K / (gemm_s + dq_s) / 1e12
                 sample += f"; plus DynamicQuantizeLinear of all {wl.x_host.size} elements on 1 thread ({dq_s:.2f} s)"
             cpu = {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample}
+            # The second CPU baseline: the reference's portable GPU kernel's blocking restated for the host's cores.
+            t_tops, t_dt, t_rows = cpu_gemm_tops(wl.shard_n, wl.K, threads, min(args.cpu_seconds, 6.0), wl.M,
+                                                 tiled=True)
+            cpu["tiled"] = {"value": round(t_tops, 6), "unit": "TOPS", "cores": threads, "kind": "port",
+                            "sample": f"{t_rows} of {wl.M} rows x {wl.shard_n} x K {wl.K} on {threads} threads "
+                                      f"({t_dt:.1f} s), extrapolated; og_oracle_int8_gemm_tiled restates "
+                                      f"Int8GemmKernel.hlsl's 64 x 64 tiles, K chunks of 16, float sums folded "
+                                      f"into int32 every 128 k"}
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,

@@ -132,6 +132,100 @@ void og_oracle_int8_gemm(const og_oracle_problem* p, const uint8_t* a, int32_t a
     for (int32_t t = 0; t < threads; t++) pthread_join(tids[t], NULL);
 }
 
+/* The blocking of the reference's portable kernel, Int8GemmTiled (src/RecursiveAI.OneGpu.Kernels/Shaders/
+ * Int8GemmKernel.hlsl:98-244), restated for the host's cores as the second CPU baseline: 64 x 64 output tiles, K in
+ * chunks of 16 staged as float (A - za) and (B - zb) (zeros past M, N or K), the products accumulated in float per
+ * tile element and folded into a wrapping int32 every 8 chunks (128 k) and at the end. Every partial sum is an integer
+ * below 2^24 in magnitude (|a - za| and |b - zb| are at most 255, 128 products), so the float sums are exact and the
+ * result equals og_oracle_int8_gemm bit for bit. Tiles are dealt to `threads` POSIX threads in turn. */
+#define TB 64
+#define TK 16
+typedef struct tiled_job {
+    const og_oracle_problem* p;
+    const uint8_t *a, *b, *za, *zb;
+    int32_t a_signed, b_signed, za_vector, zb_vector;
+    int32_t* c;
+    int64_t tile_begin, tile_end;
+} tiled_job;
+
+static void* gemm_tiles(void* arg) {
+    const tiled_job* j = (const tiled_job*)arg;
+    const og_oracle_problem* p = j->p;
+    const int64_t M = p->m, N = p->n, K = p->k;
+    const int64_t lda = p->lda == 0 ? K : p->lda;
+    const int64_t ldb = p->ldb == 0 ? (p->transpose_b ? K : N) : p->ldb;
+    const int64_t tm_count = (M + TB - 1) / TB, tn_count = (N + TB - 1) / TB;
+    float as[TK][TB], bs[TK][TB], acc[TB][TB];
+    uint32_t isum[TB][TB];
+    for (int64_t t = j->tile_begin; t < j->tile_end; t++) {
+        const int64_t bt = t / (tm_count * tn_count), r = t % (tm_count * tn_count);
+        const int64_t m0 = (r / tn_count) * TB, n0 = (r % tn_count) * TB;
+        const uint8_t* ab = j->a + p->offset_a + bt * (int64_t)p->stride_a;
+        const uint8_t* bb = j->b + p->offset_b + bt * (int64_t)p->stride_b;
+        memset(acc, 0, sizeof(acc));
+        memset(isum, 0, sizeof(isum));
+        for (int64_t k0 = 0; k0 < K; k0 += TK) {
+            for (int kk = 0; kk < TK; kk++) {
+                const int64_t k = k0 + kk;
+                for (int i = 0; i < TB; i++) {
+                    const int64_t m = m0 + i, n = n0 + i;
+                    float av = 0.0f, bv = 0.0f;
+                    if (m < M && k < K) {
+                        const int32_t z = j->za ? val8(j->za[j->za_vector ? m : 0], j->a_signed) : 0;
+                        av = (float)(val8(ab[m * lda + k], j->a_signed) - z);
+                    }
+                    if (n < N && k < K) {
+                        const int32_t z = j->zb ? val8(j->zb[j->zb_vector ? n : 0], j->b_signed) : 0;
+                        bv = (float)(val8(bb[p->transpose_b ? n * ldb + k : k * ldb + n], j->b_signed) - z);
+                    }
+                    as[kk][i] = av;
+                    bs[kk][i] = bv;
+                }
+            }
+            for (int kk = 0; kk < TK; kk++)
+                for (int i = 0; i < TB; i++) {
+                    const float av = as[kk][i];
+                    for (int q = 0; q < TB; q++) acc[i][q] += av * bs[kk][q];
+                }
+            if (((k0 / TK) & 7) == 7) {
+                for (int i = 0; i < TB; i++)
+                    for (int q = 0; q < TB; q++) {
+                        isum[i][q] += (uint32_t)(int32_t)acc[i][q];
+                        acc[i][q] = 0.0f;
+                    }
+            }
+        }
+        for (int i = 0; i < TB; i++) {
+            const int64_t m = m0 + i;
+            if (m >= M) break;
+            int32_t* crow = j->c + (bt * M + m) * N;
+            for (int q = 0; q < TB && n0 + q < N; q++) crow[n0 + q] = (int32_t)(isum[i][q] + (uint32_t)(int32_t)acc[i][q]);
+        }
+    }
+    return NULL;
+}
+
+void og_oracle_int8_gemm_tiled(const og_oracle_problem* p, const uint8_t* a, int32_t a_signed, const uint8_t* b,
+                               int32_t b_signed, const uint8_t* za, int32_t za_vector, const uint8_t* zb,
+                               int32_t zb_vector, int32_t* c, int32_t threads) {
+    const int64_t tiles = (int64_t)p->batch * ((p->m + TB - 1) / TB) * ((p->n + TB - 1) / TB);
+    if (tiles <= 0) return;
+    if (threads < 1) threads = 1;
+    if (threads > tiles) threads = (int32_t)tiles;
+    if (threads > 256) threads = 256;
+    tiled_job jobs[256];
+    pthread_t tids[256];
+    for (int32_t t = 0; t < threads; t++)
+        jobs[t] = (tiled_job){p, a, b, za, zb, a_signed, b_signed, za_vector, zb_vector, c,
+                              tiles * t / threads, tiles * (t + 1) / threads};
+    if (threads == 1) {
+        gemm_tiles(&jobs[0]);
+        return;
+    }
+    for (int32_t t = 0; t < threads; t++) pthread_create(&tids[t], NULL, gemm_tiles, &jobs[t]);
+    for (int32_t t = 0; t < threads; t++) pthread_join(tids[t], NULL);
+}
+
 /* Int8GemmDot.hlsl:4-10 and Put (:134-140): an unsigned byte u is staged as u xor 0x80 = u - 128 and its zero point z
  * moves to z - 128; then sum (s - z')(t - w') = sum s*t - w' * sum s - z' * sum t + K z' w', all modulo 2^32. */
 void og_oracle_int8_gemm_signed_domain(const og_oracle_problem* p, const uint8_t* a, int32_t a_signed,

@@ -11,6 +11,8 @@
  *   og_oracle_random           tests/RecursiveAI.OneGpu.Kernels.Tests/Rig.cs:8-19          (Rig.Random: seeded uniform floats)
  *   og_oracle_dq_input         tests/RecursiveAI.OneGpu.Kernels.Tests/Int8Tests.cs:632-647 (the seven DQL input kinds)
  *   og_oracle_int8_gemm        tests/RecursiveAI.OneGpu.Kernels.Tests/Int8Tests.cs:52-82   (Reference: wrapping int32 sums)
+ *   og_oracle_int8_gemm_tiled  src/RecursiveAI.OneGpu.Kernels/Shaders/Int8GemmKernel.hlsl:98-244 (the same sums
+ *                              through the reference portable kernel's 64 x 64 x 16 blocking; the second CPU baseline)
  *   og_oracle_requant          tests/RecursiveAI.OneGpu.Kernels.Tests/Int8Tests.cs:84-97   (Requant: QLinearMatMul byte)
  *   og_oracle_float_epilogue   tests/RecursiveAI.OneGpu.Kernels.Tests/Int8Tests.cs:356-373 (float form, two roundings)
  *   og_oracle_dynamic_quantize tests/RecursiveAI.OneGpu.Kernels.Tests/Int8Tests.cs:577-615 (DynamicReference)
@@ -57,6 +59,12 @@ void og_oracle_dq_input(float* out, int64_t count, int32_t seed, int32_t kind);
 void og_oracle_int8_gemm(const og_oracle_problem* p, const uint8_t* a, int32_t a_signed, const uint8_t* b,
                          int32_t b_signed, const uint8_t* za, int32_t za_vector, const uint8_t* zb, int32_t zb_vector,
                          int32_t* c, int32_t threads);
+/* The same sums through the reference portable kernel's blocking (Int8GemmKernel.hlsl:98-244): 64 x 64 tiles over
+ * `threads` threads, K in chunks of 16 accumulated in float and folded into int32 every 128 k. Bit-identical to
+ * og_oracle_int8_gemm; timed as the second CPU baseline. */
+void og_oracle_int8_gemm_tiled(const og_oracle_problem* p, const uint8_t* a, int32_t a_signed, const uint8_t* b,
+                               int32_t b_signed, const uint8_t* za, int32_t za_vector, const uint8_t* zb,
+                               int32_t zb_vector, int32_t* c, int32_t threads);
 
 /* Same sums computed the packed-dot way: bytes xor 0x80 into the signed domain, byte sums, correction at the end. */
 void og_oracle_int8_gemm_signed_domain(const og_oracle_problem* p, const uint8_t* a, int32_t a_signed,

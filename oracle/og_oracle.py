@@ -51,6 +51,7 @@ def lib():
         gemm_args = [ctypes.POINTER(Problem), u8p, ctypes.c_int32, u8p, ctypes.c_int32, u8p, ctypes.c_int32, u8p,
                      ctypes.c_int32, i32p]
         _lib.og_oracle_int8_gemm.argtypes = gemm_args + [ctypes.c_int32]
+        _lib.og_oracle_int8_gemm_tiled.argtypes = gemm_args + [ctypes.c_int32]
         _lib.og_oracle_int8_gemm_signed_domain.argtypes = gemm_args
         _lib.og_oracle_requant.argtypes = [ctypes.c_int32, ctypes.c_float, ctypes.c_int32, ctypes.c_int32]
         _lib.og_oracle_requant.restype = ctypes.c_int32
@@ -106,7 +107,8 @@ def _problem(m, n, k, batch=1, transpose_b=False, lda=0, ldb=0, offset_a=0, offs
 
 
 def int8_gemm(a: np.ndarray, a_signed: bool, b: np.ndarray, b_signed: bool, za=None, za_vector=False, zb=None,
-              zb_vector=False, threads: int = 0, signed_domain: bool = False, **shape) -> np.ndarray:
+              zb_vector=False, threads: int = 0, signed_domain: bool = False, tiled: bool = False,
+              **shape) -> np.ndarray:
     """Int8Tests.Reference (Int8Tests.cs:52-82): int32 sums (wrapping) of sum_k (A - za)(B - zb); returns
     [batch*m*n]. Bytes are passed as uint8 whatever their signedness."""
     p = _problem(**shape)
@@ -120,6 +122,8 @@ def int8_gemm(a: np.ndarray, a_signed: bool, b: np.ndarray, b_signed: bool, za=N
             _p(zb, u8), int(zb_vector), _p(out, ctypes.c_int32)]
     if signed_domain:
         lib().og_oracle_int8_gemm_signed_domain(*args)
+    elif tiled:  # Int8GemmKernel.hlsl's blocking: the same sums, the second CPU baseline
+        lib().og_oracle_int8_gemm_tiled(*args, threads if threads > 0 else (os.cpu_count() or 1))
     else:
         lib().og_oracle_int8_gemm(*args, threads if threads > 0 else (os.cpu_count() or 1))
     return out[: p.batch * p.m * p.n]

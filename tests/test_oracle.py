@@ -249,3 +249,22 @@ def test_conv_integer_equals_the_int8_product_of_its_columns():
             got = oracle.int8_gemm(a.reshape(-1), True, cols.reshape(-1), False, wz[g * 3:(g + 1) * 3], True, xz,
                                    False, threads=1, m=3, n=oh * ow, k=12)
             assert np.array_equal(got.reshape(3, oh, ow), want[n, g * 3:(g + 1) * 3])
+
+
+def test_tiled_restatement_equals_the_definition():
+    """og_oracle_int8_gemm_tiled (the reference portable kernel's 64 x 64 x 16 blocking with float sums folded into
+    int32 every 128 k, Int8GemmKernel.hlsl:98-244) against og_oracle_int8_gemm (Int8Tests.Reference): ragged tiles, K
+    past one fold and not a multiple of 16, batches, B stored N x K, every zero-point mode and signedness."""
+    rng = np.random.default_rng(11)
+    for (m, n, k, batch, tb) in [(70, 90, 100, 1, False), (130, 65, 300, 2, False), (64, 64, 16, 1, True),
+                                 (200, 129, 1000, 1, True), (1, 1, 1, 1, False), (33, 257, 2047, 3, False)]:
+        for (a_s, b_s, zam, zbm) in [(False, True, 1, 2), (True, False, 2, 1), (True, True, 0, 0), (False, False, 2, 2)]:
+            a = rng.integers(0, 256, batch * m * k, dtype=np.uint8)
+            b = rng.integers(0, 256, batch * k * n, dtype=np.uint8)
+            za = None if zam == 0 else rng.integers(0, 256, m if zam == 2 else 1, dtype=np.uint8)
+            zb = None if zbm == 0 else rng.integers(0, 256, n if zbm == 2 else 1, dtype=np.uint8)
+            shape = dict(m=m, n=n, k=k, batch=batch, transpose_b=tb, stride_a=m * k if batch > 1 else 0,
+                         stride_b=k * n if batch > 1 else 0)
+            want = oracle.int8_gemm(a, a_s, b, b_s, za, zam == 2, zb, zbm == 2, **shape)
+            got = oracle.int8_gemm(a, a_s, b, b_s, za, zam == 2, zb, zbm == 2, tiled=True, threads=3, **shape)
+            assert np.array_equal(got, want), (m, n, k, batch, tb, a_s, b_s, zam, zbm)

@@ -382,6 +382,7 @@ def run_family(args, rank: int, world: int, local_rank: int):
     ts = stamps.read(0)
     per_step = [ts[2 * i + 1] - ts[2 * i] for i in range(args.steps)]
     total_ns = sum(per_step)
+    floor_us = event_floor_us(dev, og, flush)
     scale_unit = 1e12 if f["unit"] == "TOPS" else 1e9
     value = d["work"] * args.steps / (total_ns * 1e-9) / scale_unit
 
@@ -439,7 +440,8 @@ def run_family(args, rank: int, world: int, local_rank: int):
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(d["work"] / (e2e_ns * 1e-9) / scale_unit, 3), "unit": f["unit"],
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
-            "gpu_launches": int(launches), "clocks": clocks.summary(), "wall_s": round(wall, 3)}
+            "gpu_launches": int(launches), "event_floor_us": floor_us, "clocks": clocks.summary(),
+            "wall_s": round(wall, 3)}
     print(json.dumps(line), flush=True)
     op.dispose()
     stamps.dispose()
@@ -617,6 +619,22 @@ class Workload:
         self.gemm.dispose()
 
 
+def event_floor_us(dev, og, flush, reps: int = 12) -> float:
+    """The part of every timed step that no kernel work removes: one 1-element torch kernel, flushed and bracketed by
+    CUDA events exactly like a step, median over `reps` (on B200 an event pair alone is ~2.6 us and the first kernel
+    after an event adds ~3.5 us more)."""
+    stamps = og.GpuTimestampSet(dev, 2 * reps)
+    for i in range(reps):
+        flush(i)
+        dev.timestamp(stamps, 2 * i)
+        with flush.torch.cuda.stream(flush.stream):
+            flush.sink.zero_()
+        dev.timestamp(stamps, 2 * i + 1)
+    ts = stamps.read(0)
+    stamps.dispose()
+    return round(statistics.median(ts[2 * i + 1] - ts[2 * i] for i in range(reps)) / 1e3, 2)
+
+
 def timed_steps(dev, og, flush, wl: Workload, steps: int, warmup: int, barrier=None):
     """Runs `warmup` untimed and `steps` timed steps (L2 flushed before each, CUDA events around the step on the
     device stream); returns the per-step nanoseconds and the number of kernel launches recorded in the timed steps."""
@@ -680,6 +698,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
     with ClockSampler(local_rank) as clocks:
         per_step_ns, launches, wall = timed_steps(dev, og, flush, wl, args.steps, args.warmup, barrier)
     kernel, variant = wl.gemm.last_kernel, wl.gemm.variant
+    floor_us = event_floor_us(dev, og, flush)
     gemm_ns = sum(per_step_ns)
 
     # Decode also as a CUDA graph: the step (the product alone) captured once and replayed back to back. B (235 MB)
@@ -909,6 +928,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
                     "replicated_operand": ("A uploaded 1/N per rank, all-gathered over NVLink" if split_a else
                                            "B uploaded 1/N per rank, all-gathered over NVLink" if split_b else None)},
             "gpu_launches": int(launches),
+            "event_floor_us": floor_us,
             "clocks": clk,
             "library_int8_tops": round(lib_tops, 3) if isinstance(lib_tops, float) else lib_tops,
             "graph_replay": graph_replay,

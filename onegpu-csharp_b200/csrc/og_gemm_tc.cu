@@ -64,7 +64,6 @@ struct Cfg {
 struct TcParams {
     int m, n, k;
     int tiles_m, tiles_n;
-    int group_m;  // output tiles per raster group along M
     int batch;
     int a_batched, b_batched;
     int k_blocks;
@@ -112,8 +111,11 @@ struct WorkCursor {
     int tile;       // whole tiles: the next tile
 };
 
+template <bool SPLIT>
 __device__ __forceinline__ void work_begin(const TcParams& p, int worker, int workers, WorkCursor& c) {
-    if (p.stream_k) {
+    if (!SPLIT) {
+        c.u = c.u1 = 0;
+    } else if (p.stream_k) {
         c.u = p.units * worker / workers;
         c.u1 = p.units * (worker + 1) / workers;
     } else if (p.tail_split && worker < p.tail_workers) {
@@ -128,7 +130,16 @@ __device__ __forceinline__ void work_begin(const TcParams& p, int worker, int wo
 // A worker of the split tail takes its range of tail units before its whole tiles (tail_first; after them
 // otherwise): the reductions of its tail segments then overlap the MMAs of its whole tiles, and every worker ends on
 // a whole tile whose epilogue is a plain store.
+template <bool SPLIT>
 __device__ __forceinline__ bool work_next(const TcParams& p, int workers, WorkCursor& c, WorkItem& w) {
+    if (!SPLIT) {  // whole tiles only
+        if (c.tile >= p.total_tiles) return false;
+        w.tile = c.tile;
+        w.kb0 = 0;
+        w.kb1 = p.k_blocks;
+        c.tile += workers;
+        return true;
+    }
     if (!p.stream_k && !p.tail_first && c.tile < p.dp_tiles) {
         w.tile = c.tile;
         w.kb0 = 0;
@@ -224,10 +235,10 @@ __device__ __forceinline__ void tile_coords(const TcParams& p, int tile, int& b,
     const int per_batch = p.tiles_m * p.tiles_n;
     b = tile / per_batch;
     const int r = tile - b * per_batch;
-    const int group_span = p.group_m * p.tiles_n;
+    const int group_span = tc::GROUP_M * p.tiles_n;
     const int group = r / group_span;
-    const int first_m = group * p.group_m;
-    const int gsize = min(p.tiles_m - first_m, p.group_m);
+    const int first_m = group * tc::GROUP_M;
+    const int gsize = min(p.tiles_m - first_m, tc::GROUP_M);
     const int in_group = r - group * group_span;
     tm = first_m + in_group % gsize;
     tn = in_group / gsize;
@@ -403,7 +414,7 @@ __device__ __forceinline__ void store_chunk(const ColTerms& t, const Epilogue& e
     }
 }
 
-template <int CG, bool B_MN, int OUT>
+template <int CG, bool B_MN, int OUT, bool SPLIT>
 __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b,
                                              const CUtensorMap& tmap_c, const TcParams& p, uint32_t idesc) {
     using C = tc::Cfg<CG>;
@@ -429,6 +440,8 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
     const bool leader = rank == 0;
     const int worker = CG == 2 ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
     const int workers = CG == 2 ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+    const bool stream_k = SPLIT && p.stream_k;
+    const bool tail_split = SPLIT && p.tail_split;
 
     pdl_trigger();
     if (threadIdx.x == 0) {
@@ -453,7 +466,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
     if (tma_store && warp == 2 && lane == 0) prefetch_tmap(&tmap_c);
     pdl_wait();  // the preceding grid is done: its outputs are readable and its TMEM is free
     // This launch's stream-K generation: flags set to it belong to this launch.
-    if (threadIdx.x == 0) *sk_gen = (p.stream_k || p.tail_split) ? __ldcg(p.sk_flag + p.sk_slots) + 1u : 0u;
+    if (threadIdx.x == 0) *sk_gen = (stream_k || tail_split) ? __ldcg(p.sk_flag + p.sk_slots) + 1u : 0u;
     if (warp == 1) {
         if constexpr (CG == 2) {
             tmem_alloc_pair(tmem_holder, tc::TMEM_COLS);
@@ -473,9 +486,9 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         // TMA producer: the whole warp walks the ring, lane 0 issues.
         uint32_t it = 0;
         WorkCursor cur;
-        work_begin(p, worker, workers, cur);
+        work_begin<SPLIT>(p, worker, workers, cur);
         WorkItem wi;
-        while (work_next(p, workers, cur, wi)) {
+        while (work_next<SPLIT>(p, workers, cur, wi)) {
             int b, tm, tn;
             tile_coords<C::BM>(p, wi.tile, b, tm, tn);
             const int ba = p.a_batched ? b : 0;
@@ -521,9 +534,9 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         if (leader) {
             uint32_t it = 0;
             WorkCursor cur;
-            work_begin(p, worker, workers, cur);
+            work_begin<SPLIT>(p, worker, workers, cur);
             WorkItem wi;
-            for (int lt = 0; work_next(p, workers, cur, wi); lt++) {
+            for (int lt = 0; work_next<SPLIT>(p, workers, cur, wi); lt++) {
                 const int acc = lt & 1;
                 const uint32_t aph = (lt >> 1) & 1;
                 if (!mbar_wait(&tempty[acc], aph ^ 1, abort_flag)) goto done;
@@ -576,7 +589,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         // Column terms are needed unless the result is the raw int32 sum.
         const bool terms = OUT != OUT_I32 || e.za != nullptr || e.zb != nullptr || e.int_bias != nullptr;
         const bool za_per_row = e.za != nullptr && e.za_vector;
-        if (p.tail_split) {
+        if (tail_split) {
             // Clear this CTA's share of the tail tiles (rows of 256 columns, dealt to the epilogue warps of the grid in
             // turn) while the first MMAs run, then count the CTA in the launch's tally. C's rows start on 16-byte
             // boundaries and N is a multiple of 4 (the TMA-store condition), so whole 16-byte stores stay inside C.
@@ -601,9 +614,9 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
         }
         bool tail_ready = false;  // thread 64: the whole grid has cleared the tail
         WorkCursor cur;
-        work_begin(p, worker, workers, cur);
+        work_begin<SPLIT>(p, worker, workers, cur);
         WorkItem wi;
-        for (int lt = 0; work_next(p, workers, cur, wi); lt++) {
+        for (int lt = 0; work_next<SPLIT>(p, workers, cur, wi); lt++) {
             int b, tm, tn;
             tile_coords<C::BM>(p, wi.tile, b, tm, tn);
             const int acc = lt & 1;
@@ -612,8 +625,8 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             // next worker's sums of the later segment. Split tail: a segment of a tail tile adds to C, once every CTA
             // has cleared its share of the tail. One thread does every wait and publishes the outcome, so the
             // epilogue warps always leave or continue together (the named barriers below cannot time out).
-            const bool sk_wait = p.stream_k && wi.kb0 == 0 && wi.kb1 < p.k_blocks;
-            const bool tail_item = p.tail_split && wi.tile >= p.dp_tiles;
+            const bool sk_wait = stream_k && wi.kb0 == 0 && wi.kb1 < p.k_blocks;
+            const bool tail_item = tail_split && wi.tile >= p.dp_tiles;
             const int sk_slot = (worker + 1) * CG + static_cast<int>(rank);
             if (threadIdx.x == 64) {
                 bool ok = mbar_wait(&tfull[acc], aph, abort_flag);
@@ -640,7 +653,7 @@ __device__ __forceinline__ void gemm_tc_body(const CUtensorMap& tmap_a, const CU
             tc_fence_after();
             const int row_in_cta = q * 32 + lane;
             const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * tc::BN;
-            if (p.stream_k && wi.kb0 > 0) {
+            if (stream_k && wi.kb0 > 0) {
                 // The later segment of a split tile (the start of this worker's range): hand its raw sums to the
                 // worker that holds K block 0 (the previous one), then flag them.
                 int32_t* slot = p.sk_part + static_cast<int64_t>(worker * CG + static_cast<int>(rank)) * SK_SLOT_INTS;
@@ -751,30 +764,30 @@ done:
             tmem_dealloc(tmem_base, tc::TMEM_COLS);
     }
     if (threadIdx.x == 0 && *abort_flag) atomicExch(p.error_flag, 1);
-    if ((p.stream_k || p.tail_split) && threadIdx.x == 0) {
+    if ((stream_k || tail_split) && threadIdx.x == 0) {
         // The last CTA to finish advances the generation (every CTA read it when it started) and resets the ticket.
         unsigned int* gen = p.sk_flag + p.sk_slots;
         __threadfence();
         if (atomicAdd(gen + 1, 1u) == gridDim.x - 1) {
             atomicExch(gen + 1, 0u);
-            if (p.tail_split) atomicExch(p.tail_zeroed, 0u);  // every CTA has left its waits on the count
+            if (tail_split) atomicExch(p.tail_zeroed, 0u);  // every CTA has left its waits on the count
             atomicAdd(gen, 1u);
         }
     }
 }
 
-template <bool B_MN, int OUT>
+template <bool B_MN, int OUT, bool SPLIT>
 __global__ void __launch_bounds__(tc::THREADS, 1)
     int8_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         const __grid_constant__ CUtensorMap tmap_c, const TcParams p, uint32_t idesc) {
-    gemm_tc_body<1, B_MN, OUT>(tmap_a, tmap_b, tmap_c, p, idesc);
+    gemm_tc_body<1, B_MN, OUT, SPLIT>(tmap_a, tmap_b, tmap_c, p, idesc);
 }
 
-template <bool B_MN, int OUT>
+template <bool B_MN, int OUT, bool SPLIT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(tc::THREADS, 1)
     int8_gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                          const __grid_constant__ CUtensorMap tmap_c, const TcParams p, uint32_t idesc) {
-    gemm_tc_body<2, B_MN, OUT>(tmap_a, tmap_b, tmap_c, p, idesc);
+    gemm_tc_body<2, B_MN, OUT, SPLIT>(tmap_a, tmap_b, tmap_c, p, idesc);
 }
 
 // ---- host side ---------------------------------------------------------------------------------------------------
@@ -862,7 +875,7 @@ static cudaError_t configure(K kern, int smem, std::atomic<uint64_t>& configured
 
 // Binds the kernel and its arguments; the returned function only sets the shared-memory limit (first time per
 // device) and launches.
-template <int CG, bool B_MN, int OUT>
+template <int CG, bool B_MN, int OUT, bool SPLIT>
 static LaunchFn bind_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensorMap& ma, const CUtensorMap& mb,
                           const CUtensorMap& mc, int grid) {
     using C = tc::Cfg<CG>;
@@ -870,17 +883,25 @@ static LaunchFn bind_tc_t(const GemmLaunch& L, const TcParams& p, const CUtensor
     return [=](cudaStream_t stream) -> cudaError_t {
         static std::atomic<uint64_t> configured{0};  // devices whose attribute is set
         if constexpr (CG == 2) {
-            auto kern = int8_gemm_tc2_kernel<B_MN, OUT>;
+            auto kern = int8_gemm_tc2_kernel<B_MN, OUT, SPLIT>;
             cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
             if (e != cudaSuccess) return e;
             return launch_pdl(kern, dim3(grid), dim3(tc::THREADS), C::SMEM_BYTES, stream, ma, mb, mc, p, idesc);
         } else {
-            auto kern = int8_gemm_tc_kernel<B_MN, OUT>;
+            auto kern = int8_gemm_tc_kernel<B_MN, OUT, SPLIT>;
             cudaError_t e = configure(kern, C::SMEM_BYTES, configured);
             if (e != cudaSuccess) return e;
             return launch_pdl(kern, dim3(grid), dim3(tc::THREADS), C::SMEM_BYTES, stream, ma, mb, mc, p, idesc);
         }
     };
+}
+
+// The kernel without the stream-K and split-tail paths when neither is in use (whole tiles only).
+template <int CG, bool B_MN, int OUT>
+static LaunchFn bind_tc_s(const GemmLaunch& L, const TcParams& p, const CUtensorMap& ma, const CUtensorMap& mb,
+                          const CUtensorMap& mc, int grid) {
+    return (p.stream_k || p.tail_split) ? bind_tc_t<CG, B_MN, OUT, true>(L, p, ma, mb, mc, grid)
+                                        : bind_tc_t<CG, B_MN, OUT, false>(L, p, ma, mb, mc, grid);
 }
 
 // The split tail of an int32 product: the tiles beyond the last full wave of whole tiles are cut into P equal K
@@ -1001,7 +1022,6 @@ static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
     p.k = L.k;
     p.tiles_m = (L.m + C::BM - 1) / C::BM;
     p.tiles_n = (L.n + tc::BN - 1) / tc::BN;
-    p.group_m = tc::GROUP_M;
     p.batch = L.batch;
     p.a_batched = ba > 1;
     p.b_batched = bb > 1;
@@ -1050,14 +1070,14 @@ static LaunchFn prepare_cg(const GemmLaunch& L, cudaError_t* err) {
     }
     const bool bmn = !L.trans_b;
     switch (L.epi.out_kind) {
-        case OUT_I32: return bmn ? bind_tc_t<CG, true, OUT_I32>(L, p, ma, mb, mc, grid)
-                                 : bind_tc_t<CG, false, OUT_I32>(L, p, ma, mb, mc, grid);
-        case OUT_F32: return bmn ? bind_tc_t<CG, true, OUT_F32>(L, p, ma, mb, mc, grid)
-                                 : bind_tc_t<CG, false, OUT_F32>(L, p, ma, mb, mc, grid);
-        case OUT_U8: return bmn ? bind_tc_t<CG, true, OUT_U8>(L, p, ma, mb, mc, grid)
-                                : bind_tc_t<CG, false, OUT_U8>(L, p, ma, mb, mc, grid);
-        default: return bmn ? bind_tc_t<CG, true, OUT_S8>(L, p, ma, mb, mc, grid)
-                            : bind_tc_t<CG, false, OUT_S8>(L, p, ma, mb, mc, grid);
+        case OUT_I32: return bmn ? bind_tc_s<CG, true, OUT_I32>(L, p, ma, mb, mc, grid)
+                                 : bind_tc_s<CG, false, OUT_I32>(L, p, ma, mb, mc, grid);
+        case OUT_F32: return bmn ? bind_tc_s<CG, true, OUT_F32>(L, p, ma, mb, mc, grid)
+                                 : bind_tc_s<CG, false, OUT_F32>(L, p, ma, mb, mc, grid);
+        case OUT_U8: return bmn ? bind_tc_s<CG, true, OUT_U8>(L, p, ma, mb, mc, grid)
+                                : bind_tc_s<CG, false, OUT_U8>(L, p, ma, mb, mc, grid);
+        default: return bmn ? bind_tc_s<CG, true, OUT_S8>(L, p, ma, mb, mc, grid)
+                            : bind_tc_s<CG, false, OUT_S8>(L, p, ma, mb, mc, grid);
     }
 }
 

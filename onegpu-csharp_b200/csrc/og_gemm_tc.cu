@@ -912,8 +912,9 @@ static LaunchFn bind_tc_s(const GemmLaunch& L, const TcParams& p, const CUtensor
 // with the operand loads), so a split must at least halve the tail. Measured on B200 with zero points (the byte-sums pass included):
 // 8192 x 2048 x 8192 111.8 us in halves against 119.8 us whole, 4096^3 68.6 against 70.7 us, while quarters of
 // 8192 x 1024 x 8192 (54 tail tiles, three quarters per pair) took 80.9 us against 74.9 us whole and thirds of the
-// batched 8 x 2048 x 12288 x 4096 558 against 547 us. The cut tiles are put together in C with TMA reductions, so C's
-// rows must allow TMA stores.
+// batched 8 x 2048 x 12288 x 4096 558 against 547 us. Without zero points the same shard took 63.4 us in quarters and
+// 77.8 us in eighths against 55.2 us whole: each piece's reduction of a whole tile into C takes longer than its share
+// of the MMAs. The cut tiles are put together in C with TMA reductions, so C's rows must allow TMA stores.
 constexpr int TAIL_MIN_BLOCKS = 8;
 constexpr double TAIL_MAX_FRACTION = 0.5;
 

@@ -14,6 +14,10 @@
 // types (u8 or s8); the zero points are applied afterwards from byte sums (og_kernels.cuh). Ragged M, N and K
 // edges are zero-filled by TMA and never stored. No load uses cluster multicast, so the kernel is the same on any
 // number of GPUs.
+//
+// Every kernel is compiled twice, on SPLIT: with the stream-K and split-tail schedules, for the launches that use
+// them, and without, for launches of whole tiles only (most of them), whose loops then carry none of that code
+// (8192 x 1024 x 8192 took 57.3 us with it and 55.2 us without).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>

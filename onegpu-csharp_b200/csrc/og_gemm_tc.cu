@@ -44,9 +44,10 @@ constexpr int EPI_WARPS = 8;               // two per TMEM lane quadrant, each t
 constexpr int EPI_THREADS = 32 * EPI_WARPS;
 constexpr int THREADS = 64 + EPI_THREADS;  // producer, MMA, epilogue warps
 // Output tiles per raster group along M: 16 when there are at least 32 tile rows, 8 otherwise. A group walks its
-// rows of A against every column tile of B, so taller groups read B fewer times; measured on B200, 8192^3 took
-// 319.4-320.4 us with 16 against 323.6 us with 8 (and 337.6-338.9 us with 32), while 4096^3 with the dequantize
-// epilogue (both operands fit in L2) was ~0.9 us slower with 16, and the shard shapes did not change.
+// rows of A against every column tile of B, so taller groups read B fewer times. Measured on B200, 8192^3 took
+// 319.4-320.4 us with 16 against 323.6 us with 8 (12, 20, 24 and 32 were 1-16 us slower than 16), while 4096^3
+// with the dequantize epilogue (both operands fit in L2) was ~0.9 us slower with 16, and the shard shapes did not
+// change.
 constexpr int GROUP_M = 8;
 constexpr int GROUP_M_TALL = 16;
 

@@ -20,6 +20,7 @@ product (oracle/, all host threads) on a bounded row sample of the same workload
 from __future__ import annotations
 
 import argparse
+import contextlib
 import functools
 import json
 import os
@@ -103,6 +104,39 @@ def nvml_index(local_rank: int):
         if local_rank < len(items):
             return items[local_rank]
     return local_rank
+
+
+class HostBinding:
+    """Binds this process's threads to the CPUs NVML names as nearest the rank's GPU (nvmlDeviceSetCpuAffinity, which
+    sets the calling thread's CPU affinity and nothing on the GPU), so that the page-locked buffers of the e2e leg are
+    allocated on the GPU's own socket. `everywhere()` lends the process all of its original CPUs back for the CPU
+    baselines, which use every host thread."""
+
+    def __init__(self, local_rank: int):
+        self.original = os.sched_getaffinity(0)
+        self.cpus = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            idx = nvml_index(local_rank)
+            h = (pynvml.nvmlDeviceGetHandleByUUID(idx) if isinstance(idx, str) and idx.startswith(("GPU-", "MIG-"))
+                 else pynvml.nvmlDeviceGetHandleByIndex(int(idx)))
+            pynvml.nvmlDeviceSetCpuAffinity(h)
+            self.bound = os.sched_getaffinity(0)
+            self.cpus = len(self.bound)
+        except Exception:  # noqa: BLE001 - no NVML or no affinity: the process stays where it was
+            self.bound = self.original
+
+    @contextlib.contextmanager
+    def everywhere(self):
+        os.sched_setaffinity(0, self.original)
+        try:
+            yield
+        finally:
+            os.sched_setaffinity(0, self.bound)
+
+    def summary(self):
+        return {"cpus_near_gpu": self.cpus, "cpus_total": len(self.original)}
 
 
 class ClockSampler:
@@ -316,6 +350,7 @@ def run_family(args, rank: int, world: int, local_rank: int):
         raise SystemExit(f"{args.workload} is measured on one GPU")
     f = FAMILIES[args.workload]
     d = family_inputs(args.workload)
+    host = HostBinding(local_rank)
     dev = og.GpuDevice(local_rank)
     bufs = []
 
@@ -429,7 +464,8 @@ def run_family(args, rank: int, world: int, local_rank: int):
                  "traffic": profile_traffic(args.workload)})
     cpu = None
     if not args.no_cpu:
-        v, cores, sample = cpu_family(args.workload, os.cpu_count() or 1, args.cpu_seconds)
+        with host.everywhere():
+            v, cores, sample = cpu_family(args.workload, os.cpu_count() or 1, args.cpu_seconds)
         cpu = {"value": round(v, 6), "unit": f["unit"], "cores": cores, "kind": "port", "sample": sample}
     line = {"metric": f["metric"], "value": round(value, 3), "unit": f["unit"], "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ns / args.steps / 1e6, 4), "higher_is_better": True,
@@ -441,7 +477,7 @@ def run_family(args, rank: int, world: int, local_rank: int):
             "e2e": {"value": round(d["work"] / (e2e_ns * 1e-9) / scale_unit, 3), "unit": f["unit"],
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": int(launches), "event_floor_us": floor_us, "clocks": clocks.summary(),
-            "wall_s": round(wall, 3)}
+            "host": host.summary(), "wall_s": round(wall, 3)}
     print(json.dumps(line), flush=True)
     op.dispose()
     stamps.dispose()
@@ -685,6 +721,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
 
     from onegpu_cuda import shard as sh
 
+    host = HostBinding(local_rank)
     dev = og.GpuDevice(local_rank)
     flush = L2Flush(dev, local_rank)
 
@@ -877,31 +914,34 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
         peaks, peak, peak_kind, burst, sust, capped = roofline_peaks(clk, gemm_ns * 1e-9 > 1.0 or wall > 1.0)
         cpu = None
         if world == 1 and not args.no_cpu:
-            threads = os.cpu_count() or 1
-            tops, dt, rows = cpu_gemm_tops(wl.shard_n, wl.K, threads, args.cpu_seconds, wl.M)
-            sample = (f"{rows} of {wl.M} rows x {wl.shard_n} x K {wl.K} on {threads} threads ({dt:.1f} s), "
-                      f"extrapolated to TOPS")
-            if wl.w.get("dql_in_step"):
-                # Config 2's step also quantizes the activations: the oracle's DynamicReference over the whole x
-                # (one thread), added to the product's extrapolated time.
-                sys.path.insert(0, os.path.join(ROOT, "oracle"))
-                import og_oracle as oracle
+            with host.everywhere():  # the CPU baselines use every host thread
+                threads = os.cpu_count() or 1
+                tops, dt, rows = cpu_gemm_tops(wl.shard_n, wl.K, threads, args.cpu_seconds, wl.M)
+                sample = (f"{rows} of {wl.M} rows x {wl.shard_n} x K {wl.K} on {threads} threads ({dt:.1f} s), "
+                          f"extrapolated to TOPS")
+                if wl.w.get("dql_in_step"):
+                    # Config 2's step also quantizes the activations: the oracle's DynamicReference over the whole x
+                    # (one thread), added to the product's extrapolated time.
+                    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+                    import og_oracle as oracle
 
-                t0 = time.perf_counter()
-                oracle.dynamic_quantize(wl.x_host)
-                dq_s = time.perf_counter() - t0
-                gemm_s = 2.0 * wl.M * wl.shard_n * wl.K / (tops * 1e12)
-                tops = 2.0 * wl.M * wl.shard_n * wl.K / (gemm_s + dq_s) / 1e12
-                sample += f"; plus DynamicQuantizeLinear of all {wl.x_host.size} elements on 1 thread ({dq_s:.2f} s)"
-            cpu = {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample}
-            # The second CPU baseline: the reference's portable GPU kernel's blocking restated for the host's cores.
-            t_tops, t_dt, t_rows = cpu_gemm_tops(wl.shard_n, wl.K, threads, min(args.cpu_seconds, 6.0), wl.M,
-                                                 tiled=True)
-            cpu["tiled"] = {"value": round(t_tops, 6), "unit": "TOPS", "cores": threads, "kind": "port",
-                            "sample": f"{t_rows} of {wl.M} rows x {wl.shard_n} x K {wl.K} on {threads} threads "
-                                      f"({t_dt:.1f} s), extrapolated; og_oracle_int8_gemm_tiled restates "
-                                      f"Int8GemmKernel.hlsl's 64 x 64 tiles, K chunks of 16, float sums folded "
-                                      f"into int32 every 128 k"}
+                    t0 = time.perf_counter()
+                    oracle.dynamic_quantize(wl.x_host)
+                    dq_s = time.perf_counter() - t0
+                    gemm_s = 2.0 * wl.M * wl.shard_n * wl.K / (tops * 1e12)
+                    tops = 2.0 * wl.M * wl.shard_n * wl.K / (gemm_s + dq_s) / 1e12
+                    sample += (f"; plus DynamicQuantizeLinear of all {wl.x_host.size} elements on 1 thread "
+                               f"({dq_s:.2f} s)")
+                cpu = {"value": round(tops, 6), "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample}
+                # The second CPU baseline: the reference's portable GPU kernel's blocking restated for the host's
+                # cores.
+                t_tops, t_dt, t_rows = cpu_gemm_tops(wl.shard_n, wl.K, threads, min(args.cpu_seconds, 6.0), wl.M,
+                                                     tiled=True)
+                cpu["tiled"] = {"value": round(t_tops, 6), "unit": "TOPS", "cores": threads, "kind": "port",
+                                "sample": f"{t_rows} of {wl.M} rows x {wl.shard_n} x K {wl.K} on {threads} threads "
+                                          f"({t_dt:.1f} s), extrapolated; og_oracle_int8_gemm_tiled restates "
+                                          f"Int8GemmKernel.hlsl's 64 x 64 tiles, K chunks of 16, float sums folded "
+                                          f"into int32 every 128 k"}
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
@@ -929,6 +969,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist):
                                            "B uploaded 1/N per rank, all-gathered over NVLink" if split_b else None)},
             "gpu_launches": int(launches),
             "event_floor_us": floor_us,
+            "host": host.summary(),
             "clocks": clk,
             "library_int8_tops": round(lib_tops, 3) if isinstance(lib_tops, float) else lib_tops,
             "graph_replay": graph_replay,

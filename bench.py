@@ -15,7 +15,9 @@ batch-sharded), and at N > 1 the gather of the sharded result onto rank 0 over N
 outside `value`). `e2e` runs the same product through the C ABI from pinned host buffers (uploads of the step's inputs
 - at N > 1 each rank only its 1/N of the replicated operand, all-gathered over NVLink -, the product, readback of the
 rank's result), pipelined over two buffer sets. `--impl reference` times the CPU restatement of the reference's int8
-product (oracle/, all host threads) on a bounded row sample of the same workload.
+product (oracle/, all host threads) on a bounded row sample of the same workload. Each line also reports
+`event_floor_us` (one 1-element kernel flushed and timed like a step: the part of every step no kernel work removes)
+and `host` (each rank runs on the CPUs NVML names as nearest its GPU; the CPU baselines get every host thread back).
 """
 from __future__ import annotations
 
